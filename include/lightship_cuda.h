@@ -1,0 +1,246 @@
+/*
+ * lightship_cuda.h -- C ABI of the B200 (sm_100a) CUDA backend for LightShip.
+ *
+ * The backend sits behind LightShip's `Backend` trait
+ * (lightship-core/src/backend/backend.rs:128-163).  A Rust `backend/cuda.rs` binds the
+ * functions below with an `extern "C"` block and implements the trait on top of them;
+ * each declaration names the reference interface it replaces.  Status codes extend the
+ * public LightShip C API's error enum (c-api/include/lightship.h:36-59) with the
+ * backend error kinds of `BackendErrorCode` (backend.rs:9-23) and
+ * `BackendError` (lightship-core/src/common/error.rs:79-103).
+ *
+ * Conventions
+ *  - Plain pointers and sizes only.  `lsc_stream` is a cudaStream_t (NULL = legacy
+ *    default stream).  Device pointers must belong to the calling thread's current
+ *    device unless a backend handle says otherwise.
+ *  - Every function is thread-safe and re-entrant.  None aborts, traps or waits without a
+ *    bound: device-side waits give up after 2 s and raise LSC_ERROR_TIMEOUT.
+ *  - On failure a function returns a non-zero lsc_status and stores a message that
+ *    lsc_last_error() returns (per calling thread).
+ *  - Kernel-level entry points (lsc_gemm_i8, lsc_quantize_f32, ...) are stream-ordered and
+ *    return after the launch; errors raised on the device are reported by the next
+ *    lsc_check_device / lsc_synchronize.
+ */
+#ifndef LIGHTSHIP_CUDA_H
+#define LIGHTSHIP_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LSC_ABI_VERSION 1
+#define LSC_MAX_DIMS 8
+
+/* ---- status codes (lightship.h:36-59 + backend.rs:9-23) ----------------------------- */
+typedef enum lsc_status {
+  LSC_SUCCESS = 0,                     /* LIGHTSHIP_SUCCESS */
+  LSC_ERROR = 1,                       /* LIGHTSHIP_ERROR */
+  LSC_ERROR_INVALID_ARGUMENT = 2,      /* LIGHTSHIP_ERROR_INVALID_ARGUMENT / InvalidParameter */
+  LSC_ERROR_OUT_OF_MEMORY = 3,         /* LIGHTSHIP_ERROR_OUT_OF_MEMORY / OutOfMemory */
+  LSC_ERROR_BACKEND_NOT_AVAILABLE = 6, /* LIGHTSHIP_ERROR_BACKEND_NOT_AVAILABLE / NotAvailable */
+  LSC_ERROR_SHAPE_MISMATCH = 7,        /* LIGHTSHIP_ERROR_SHAPE_MISMATCH */
+  LSC_ERROR_UNSUPPORTED_DATATYPE = 8,  /* LIGHTSHIP_ERROR_UNSUPPORTED_DATATYPE */
+  LSC_ERROR_DEVICE_ERROR = 9,          /* LIGHTSHIP_ERROR_DEVICE_ERROR */
+  LSC_ERROR_NOT_IMPLEMENTED = 10,      /* LIGHTSHIP_ERROR_NOT_IMPLEMENTED */
+  LSC_ERROR_UNSUPPORTED_OPERATOR = 11, /* BackendErrorCode::UnsupportedOperator */
+  LSC_ERROR_COMPILATION_FAILED = 12,   /* BackendErrorCode::CompilationFailed */
+  LSC_ERROR_EXECUTION_FAILED = 13,     /* BackendErrorCode::ExecutionFailed */
+  LSC_ERROR_UNSUPPORTED_LAYOUT = 14,   /* BackendError::UnsupportedLayout */
+  LSC_ERROR_TIMEOUT = 15               /* LightShipError::Timeout: a device wait ran out */
+} lsc_status;
+
+/* ---- data types (lightship.h:66-87, DataType in common/types.rs:5-44) --------------- */
+typedef enum lsc_dtype {
+  LSC_DTYPE_F32 = 0,
+  LSC_DTYPE_F16 = 1,
+  LSC_DTYPE_F64 = 2,
+  LSC_DTYPE_I8 = 3,
+  LSC_DTYPE_I16 = 4,
+  LSC_DTYPE_I32 = 5,
+  LSC_DTYPE_I64 = 6,
+  LSC_DTYPE_U8 = 7,
+  LSC_DTYPE_QUINT8 = 8,
+  LSC_DTYPE_QINT8 = 9,
+  LSC_DTYPE_QINT32 = 10
+} lsc_dtype;
+
+/* StorageLayout (lightship.h:90-97; common/types.rs) */
+typedef enum lsc_layout {
+  LSC_LAYOUT_NCHW = 0,
+  LSC_LAYOUT_NHWC = 1,
+  LSC_LAYOUT_OIHW = 2,
+  LSC_LAYOUT_OHWI = 3, /* conv weight [Cout, KH, KW, Cin/groups] for NHWC kernels */
+  LSC_LAYOUT_DEFAULT = 4
+} lsc_layout;
+
+/* Operators on the dense-contraction path (OperatorType, ir/operator.rs:9-100) */
+typedef enum lsc_op_type {
+  LSC_OP_CONV2D = 0,
+  LSC_OP_FULLY_CONNECTED = 1,
+  LSC_OP_MATMUL = 2,
+  LSC_OP_BATCHNORM = 3,
+  LSC_OP_RELU = 4,
+  LSC_OP_RELU6 = 5,
+  LSC_OP_SILU = 6,
+  LSC_OP_QUANTIZE = 7,   /* quantize_tensor (quantization/helpers.rs:11-50) */
+  LSC_OP_DEQUANTIZE = 8, /* dequantize_tensor (quantization/helpers.rs:53-94) */
+  LSC_OP_QGEMM = 9       /* quantized_gemm_int8 + requant/dequant (cpu/quantized_ops.rs:13-48) */
+} lsc_op_type;
+
+/* FusionType (ir/fusion.rs:8-23); LSC_FUSION_NONE = no FusionInfo */
+typedef enum lsc_fusion_type {
+  LSC_FUSION_NONE = -1,
+  LSC_FUSION_CONV_RELU = 0,
+  LSC_FUSION_CONV_RELU6 = 1,
+  LSC_FUSION_CONV_SIGMOID = 2,
+  LSC_FUSION_CONV_BATCHNORM = 3,
+  LSC_FUSION_BATCHNORM_RELU = 4,
+  LSC_FUSION_ADD_RELU = 5,
+  LSC_FUSION_MUL_RELU = 6
+} lsc_fusion_type;
+
+/* epilogue activations */
+#define LSC_ACT_NONE 0
+#define LSC_ACT_RELU 1  /* x > 0 ? x : 0           platform/simd.rs:552-556 */
+#define LSC_ACT_RELU6 2 /* f32::clamp(x, 0, 6)     platform/simd.rs:558-562 */
+#define LSC_ACT_SILU 3  /* x / (1 + exp(-x)), +-20 cut-offs  operator/silu.rs:47-61 */
+
+/* rounding of the requantize step */
+#define LSC_ROUND_HALF_AWAY 0 /* Rust f32::round (cpu/quantized_ops.rs:45, helpers.rs:153) */
+#define LSC_ROUND_HALF_EVEN 1
+
+/* FP32 contraction mode */
+#define LSC_FP32_3XTF32 0 /* split-TF32, three tensor-core products: ~fp32 accuracy */
+#define LSC_FP32_TF32 1   /* single TF32 product: 10-bit mantissa inputs */
+
+/* tensor memory location */
+#define LSC_MEM_HOST 0
+#define LSC_MEM_DEVICE 1
+
+typedef void* lsc_stream;
+typedef struct lsc_backend lsc_backend;
+typedef struct lsc_op lsc_op;
+
+/* GpuBackendConfig (backend/backend.rs:81-96) plus the CUDA backend's extensions */
+typedef struct lsc_config {
+  int32_t device_id;    /* GpuBackendConfig::device_id */
+  int32_t enable_fp16;  /* GpuBackendConfig::enable_fp16 (accepted, FP16 paths not used) */
+  int32_t rounding;     /* default requantize rounding: LSC_ROUND_* */
+  int32_t fp32_mode;    /* LSC_FP32_* */
+  uint64_t arena_bytes; /* device arena size; 0 = 1 GiB */
+} lsc_config;
+
+/* BackendCapabilities subset (backend/capabilities.rs:46-67) */
+typedef struct lsc_caps {
+  int32_t backend_type; /* BackendType::GPU = 1 (lightship.h:104) */
+  int32_t device_id;
+  int32_t sm_count;
+  int32_t cc_major, cc_minor;
+  uint64_t total_memory;
+  uint32_t memory_alignment;
+  uint32_t supported_ops_mask; /* bit (1 << lsc_op_type) per supported operator */
+} lsc_caps;
+
+/* Quantization (ir/tensor.rs:9-18); count = 0 means "not quantized" */
+typedef struct lsc_quant {
+  const float* scale;
+  const int32_t* zero_point;
+  int32_t count;
+  int32_t bit_width;
+} lsc_quant;
+
+/* Tensor (ir/tensor.rs:39-54) with its data either in host memory (TensorData::Owned bytes)
+ * or on the device (the TensorData::Device variant this backend adds). */
+typedef struct lsc_tensor {
+  const char* name;
+  int32_t ndim;
+  int64_t shape[LSC_MAX_DIMS];
+  int32_t dtype;    /* lsc_dtype */
+  int32_t layout;   /* lsc_layout */
+  int32_t location; /* LSC_MEM_HOST | LSC_MEM_DEVICE */
+  int32_t device;
+  void* data;
+  uint64_t nbytes;
+  lsc_quant quant;
+} lsc_tensor;
+
+/* OperatorDef (ir/operator.rs:200-226) with the attributes the dense path reads, plus
+ * FusionInfo::fusion_type (ir/fusion.rs:41-49). */
+typedef struct lsc_op_desc {
+  int32_t op_type; /* lsc_op_type */
+  int32_t fusion;  /* lsc_fusion_type */
+  int32_t stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w, groups;
+  int32_t activation;  /* extra epilogue activation, LSC_ACT_* */
+  int32_t rounding;    /* LSC_ROUND_*, -1 = backend default */
+  int32_t fp32_mode;   /* LSC_FP32_*, -1 = backend default */
+  float bn_epsilon;    /* BatchNorm epsilon (operator/batchnorm.rs:49 default 1e-5) */
+  float output_scale;  /* s_out of a requantized int8 output */
+  int32_t output_dtype; /* dtype of outputs[0] for QGEMM / quantized Conv2d */
+} lsc_op_desc;
+
+/* Backend::allocate result (backend/memory.rs:32-45) */
+typedef struct lsc_memory_block {
+  uint64_t id;
+  void* ptr;
+  uint64_t size;
+  uint64_t alignment;
+  int32_t location; /* StorageLocation::GPU */
+} lsc_memory_block;
+
+/* ---- library ----------------------------------------------------------------------------- */
+const char* lsc_version(void);               /* LightShip_GetVersion (lightship.h:29) */
+const char* lsc_last_error(void);            /* per-thread; capi/handle.rs:593 pattern */
+const char* lsc_status_string(int32_t code); /* LightShipError_GetMessage (lightship.h:62) */
+int32_t lsc_device_count(void);
+
+/* ---- Backend trait (backend/backend.rs:128-163) ------------------------------------------ */
+lsc_status lsc_backend_create(const lsc_config* config, lsc_backend** out); /* GpuBackend ctor */
+void lsc_backend_destroy(lsc_backend* backend);                             /* Drop */
+int32_t lsc_backend_is_available(const lsc_backend* backend);               /* is_available */
+lsc_status lsc_backend_capabilities(const lsc_backend* backend, lsc_caps* caps); /* capabilities */
+/* compile_operator(def, fusion, inputs, outputs): weights/static inputs that carry data are
+ * prepacked on the device now (BN fold, per-channel INT8 quantization, layout change). */
+lsc_status lsc_compile_operator(lsc_backend* backend, const lsc_op_desc* def,
+                                const lsc_tensor* inputs, int32_t n_inputs,
+                                const lsc_tensor* outputs, int32_t n_outputs, lsc_op** out);
+/* execute(op, inputs, outputs): host or device tensors; sets outputs[i].shape/ndim. */
+lsc_status lsc_execute(lsc_backend* backend, const lsc_op* op, const lsc_tensor* inputs,
+                       int32_t n_inputs, lsc_tensor* outputs, int32_t n_outputs,
+                       lsc_stream stream);
+void lsc_op_destroy(lsc_op* op);
+lsc_status lsc_allocate(lsc_backend* backend, uint64_t size, uint64_t alignment,
+                        lsc_memory_block* block);                 /* allocate */
+void lsc_deallocate(lsc_backend* backend, lsc_memory_block* block); /* deallocate */
+lsc_status lsc_synchronize(lsc_backend* backend);                   /* synchronize */
+/* arena statistics (memory/stats.rs:7-110): current and peak bytes in use */
+lsc_status lsc_memory_stats(const lsc_backend* backend, uint64_t* current, uint64_t* peak,
+                            uint64_t* capacity);
+lsc_status lsc_memcpy_h2d(void* dst, const void* src, uint64_t bytes, lsc_stream stream);
+lsc_status lsc_memcpy_d2h(void* dst, const void* src, uint64_t bytes, lsc_stream stream);
+
+/* Reads (and clears) the current device's sticky device-error word: 0 = no error.  Returns
+ * LSC_ERROR_TIMEOUT when a kernel gave up on a bounded wait. */
+lsc_status lsc_check_device(uint32_t* word);
+
+/* ---- kernel-level entry points (device pointers, stream-ordered) ------------------------- */
+
+/* INT8 chain (cpu/quantized_ops.rs:13-48 with quantization/helpers.rs:139-160):
+ *   acc[m,n] = sum_k A[m,k] * W[n,k]           (A [M,K] and W [N,K] row-major int8, exact i32)
+ *   acc     += bias[n]                         (bias may be NULL)
+ *   y        = (f32)acc * scale[n]             (scale has N entries)
+ *   y        = act(y)                          (LSC_ACT_*)
+ *   out_f32  = y ; out_i8 = (i8)clamp(R(y / s_out), -128, 127) ; out_i32 = acc
+ * Any of out_i8 / out_f32 / out_i32 may be NULL (at least one must be given); each output
+ * is row-major [M, N].  Needs K % 16 == 0 and 16-byte aligned A and W. */
+lsc_status lsc_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k,
+                       const int32_t* bias, const float* scale, float s_out, int32_t act,
+                       int32_t rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
+                       lsc_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LIGHTSHIP_CUDA_H */

@@ -1,0 +1,53 @@
+// lsc_internal.h -- shared host-side declarations of the CUDA backend library.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "lightship_cuda.h"
+
+namespace lsc {
+
+// Records a message for lsc_last_error() on this thread and returns `code`.
+lsc_status set_error(lsc_status code, const char* fmt, ...);
+// Maps a CUDA runtime error to LSC_ERROR_DEVICE_ERROR (or OUT_OF_MEMORY) with a message.
+lsc_status cuda_error(cudaError_t e, const char* what);
+
+#define LSC_CUDA_TRY(expr)                                 \
+  do {                                                     \
+    cudaError_t _e = (expr);                               \
+    if (_e != cudaSuccess) return ::lsc::cuda_error(_e, #expr); \
+  } while (0)
+
+// Per-device facts and the device-resident error word, set up once per device.
+struct DeviceState {
+  int device = -1;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  size_t smem_optin = 0;
+  size_t total_memory = 0;
+  uint32_t* err_word = nullptr;  // device address of the sticky error word
+};
+
+// State of the calling thread's current device; nullptr (with the error set) on failure.
+DeviceState* current_device_state();
+DeviceState* device_state(int device);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda needed).
+// 2-D tensor: `inner` contiguous elements per row, `outer` rows, `row_stride_bytes` apart.
+lsc_status encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                          uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                          uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+lsc_status encode_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                          const uint64_t dims[4], const uint64_t strides_bytes[3],
+                          const uint32_t box[4], const uint32_t elem_strides[4],
+                          CUtensorMapSwizzle swizzle);
+
+// INT8 GEMM + requant/dequant epilogue (gemm_i8.cu).  ldo = row stride of the outputs in
+// elements.  Validates its arguments.
+lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k,
+                          const int32_t* bias, const float* scale, float s_out, int act,
+                          int rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
+                          int64_t ldo, cudaStream_t stream);
+
+}  // namespace lsc

@@ -1,0 +1,59 @@
+"""Kernel-level operators on torch device tensors, calling the C ABI directly.
+
+torch is only the device-memory and stream plumbing here: every operator below launches
+this package's own sm_100a kernels through ``liblightship_cuda.so``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(device=None):
+    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _need(t, dtype, name):
+    if t is None:
+        return
+    if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise ValueError(f"{name}: expected a contiguous CUDA {dtype} tensor, got {t.dtype} "
+                         f"on {t.device} (contiguous={t.is_contiguous()})")
+
+
+def gemm_i8(a, w, scale, bias=None, s_out=1.0, act=_lib.ACT_NONE,
+            rounding=_lib.ROUND_HALF_AWAY, out_i8=True, out_f32=False, out_i32=False):
+    """INT8 chain on the tensor cores: returns (q_i8, y_f32, acc_i32), each None unless asked.
+
+    a: [M,K] int8, w: [N,K] int8, scale: [N] f32 (= s_a * s_w[n]), bias: [N] int32 or None.
+    """
+    _need(a, torch.int8, "a")
+    _need(w, torch.int8, "w")
+    _need(scale, torch.float32, "scale")
+    _need(bias, torch.int32, "bias")
+    m, k = a.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"gemm_i8: K mismatch {a.shape} vs {w.shape}")
+    dev = a.device
+    q = torch.empty((m, n), dtype=torch.int8, device=dev) if out_i8 else None
+    y = torch.empty((m, n), dtype=torch.float32, device=dev) if out_f32 else None
+    acc = torch.empty((m, n), dtype=torch.int32, device=dev) if out_i32 else None
+    check(lib().lsc_gemm_i8(_ptr(a), _ptr(w), m, n, k, _ptr(bias), _ptr(scale), float(s_out),
+                            act, rounding, _ptr(q), _ptr(y), _ptr(acc), _stream(dev)))
+    return q, y, acc
+
+
+def check_device() -> int:
+    """Synchronizes and returns the device error word (raises on a device-side error)."""
+    w = C.c_uint32(0)
+    check(lib().lsc_check_device(C.byref(w)))
+    return w.value

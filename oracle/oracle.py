@@ -1,0 +1,290 @@
+"""ctypes wrapper of the CPU oracle ``oracle/liblsc_oracle.so``.
+
+TEST INFRASTRUCTURE ONLY: imported by ``tests/``, ``__graft_entry__.smoke()`` and the CPU
+baseline leg of ``bench.py``, as the checker (or the timed CPU baseline).  The product
+(``lightship_b200``) never imports this module.  The algorithms and their reference
+citations are in ``lsc_oracle.cpp``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liblsc_oracle.so")
+
+ROUND_HALF_AWAY = 0
+ROUND_HALF_EVEN = 1
+ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SILU = 0, 1, 2, 3
+QUINT8, QINT8, QINT32 = 0, 1, 2
+
+
+def build() -> str:
+    """Runs the oracle's Makefile (g++ only, no GPU)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        _lib = C.CDLL(LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+P = C.c_void_p
+I64 = C.c_int64
+I32 = C.c_int32
+F32 = C.c_float
+
+
+def _declare(l):
+    sig = {
+        "orc_gemm_scalar": [P, P, P, I64, I64, I64],
+        "orc_gemm_blocked": [P, P, P, I64, I64, I64],
+        "orc_matmul": [P, P, P, I64, I64, I64, C.c_int],
+        "orc_fully_connected": [P, P, P, I64, I64, I64, C.c_int],
+        "orc_conv2d_nchw": [P, P, P, P] + [I64] * 14 + [C.c_int],
+        "orc_conv2d_nchw_reference_korder": [P, P, P] + [I64] * 14,
+        "orc_batchnorm_inference": [P, P, I64, I64, I64, P, P, P, P, F32],
+        "orc_bn_fold": [P, P, P, P, P, P, F32, I64, I64, P, P],
+        "orc_act_inplace": [P, I64, C.c_int],
+        "orc_quantize_tensor": [P, I64, F32, I32, C.c_int, P],
+        "orc_dequantize_tensor": [P, I64, F32, I32, C.c_int, P],
+        "orc_quantize_sym": [P, P, I64, F32, C.c_int],
+        "orc_quantize_weights_per_channel": [P, I64, I64, P, P],
+        "orc_gemm_i8_nn": [P, P, P, I64, I64, I64, C.c_int],
+        "orc_gemm_i8_tn": [P, P, P, I64, I64, I64, C.c_int],
+        "orc_requant": [P, I64, I64, P, P, C.c_int, F32, C.c_int, P, P, P],
+        "orc_gemm_i8_chain": [P, P, I64, I64, I64, P, P, C.c_int, F32, C.c_int, P, P, P, C.c_int],
+        "orc_conv2d_i8_nhwc_chain": [P, P] + [I64] * 14 + [P, P, C.c_int, F32, C.c_int, P, P, P, C.c_int],
+    }
+    for name, args in sig.items():
+        f = getattr(l, name)
+        f.argtypes = args
+        f.restype = None
+    l.orc_act.argtypes = [F32, C.c_int]
+    l.orc_act.restype = F32
+    l.orc_round.argtypes = [F32, C.c_int]
+    l.orc_round.restype = F32
+    l.orc_quantize_value.argtypes = [F32, F32, I32, C.c_int]
+    l.orc_quantize_value.restype = I32
+    l.orc_dequantize_value.argtypes = [I32, F32, I32]
+    l.orc_dequantize_value.restype = F32
+    l.orc_find_scale_zp.argtypes = [P, I64, C.c_int, C.c_int, C.POINTER(F32), C.POINTER(I32)]
+    l.orc_find_scale_zp.restype = C.c_int
+    l.orc_conv_out_dim.argtypes = [I64] * 5
+    l.orc_conv_out_dim.restype = I64
+    l.orc_version.restype = C.c_char_p
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _c(a, dtype):
+    return None if a is None else np.ascontiguousarray(a, dtype=dtype)
+
+
+# ---------------------------------------------------------------- FP32 path
+def gemm_scalar(a, b, c=None):
+    a, b = _c(a, np.float32), _c(b, np.float32)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.zeros((m, n), np.float32) if c is None else _c(c, np.float32).copy()
+    lib().orc_gemm_scalar(_p(a), _p(b), _p(c), m, n, k)
+    return c
+
+
+def gemm_blocked(a, b, c=None):
+    a, b = _c(a, np.float32), _c(b, np.float32)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.zeros((m, n), np.float32) if c is None else _c(c, np.float32).copy()
+    lib().orc_gemm_blocked(_p(a), _p(b), _p(c), m, n, k)
+    return c
+
+
+def matmul(a, b, threads=0):
+    a, b = _c(a, np.float32), _c(b, np.float32)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.empty((m, n), np.float32)
+    lib().orc_matmul(_p(a), _p(b), _p(c), m, n, k, threads)
+    return c
+
+
+def fully_connected(x, w, threads=0):
+    x, w = _c(x, np.float32), _c(w, np.float32)
+    b, i = x.shape
+    o = w.shape[0]
+    y = np.empty((b, o), np.float32)
+    lib().orc_fully_connected(_p(x), _p(w), _p(y), b, i, o, threads)
+    return y
+
+
+def conv_out_dim(n, k, s, p, d):
+    return lib().orc_conv_out_dim(n, k, s, p, d)
+
+
+def conv2d_nchw(x, w, bias=None, stride=(1, 1), pad=(0, 0), dilation=(1, 1), groups=1,
+                threads=0, reference_korder=False):
+    x, w, bias = _c(x, np.float32), _c(w, np.float32), _c(bias, np.float32)
+    n, ci, h, wd = x.shape
+    co, _, kh, kw = w.shape
+    oh = conv_out_dim(h, kh, stride[0], pad[0], dilation[0])
+    ow = conv_out_dim(wd, kw, stride[1], pad[1], dilation[1])
+    y = np.zeros((n, co, oh, ow), np.float32)
+    args = [n, ci, h, wd, co, kh, kw, stride[0], stride[1], pad[0], pad[1], dilation[0], dilation[1], groups]
+    if reference_korder:
+        lib().orc_conv2d_nchw_reference_korder(_p(x), _p(w), _p(y), *args)
+    else:
+        lib().orc_conv2d_nchw(_p(x), _p(w), _p(bias), _p(y), *args, threads)
+    return y
+
+
+def batchnorm_inference(x, gamma=None, beta=None, mean=None, var=None, eps=1e-5):
+    x = _c(x, np.float32)
+    n, c = x.shape[0], x.shape[1]
+    spatial = int(np.prod(x.shape[2:])) if x.ndim > 2 else 1
+    y = np.empty_like(x)
+    lib().orc_batchnorm_inference(_p(x), _p(y), n, c, spatial, _p(_c(gamma, np.float32)),
+                                  _p(_c(beta, np.float32)), _p(_c(mean, np.float32)),
+                                  _p(_c(var, np.float32)), eps)
+    return y
+
+
+def bn_fold(w, bias, gamma, beta, mean, var, eps=1e-5):
+    w = _c(w, np.float32)
+    co = w.shape[0]
+    per = int(np.prod(w.shape[1:]))
+    wo = np.empty_like(w)
+    bo = np.empty(co, np.float32)
+    lib().orc_bn_fold(_p(w), _p(_c(bias, np.float32)), _p(_c(gamma, np.float32)), _p(_c(beta, np.float32)),
+                      _p(_c(mean, np.float32)), _p(_c(var, np.float32)), eps, co, per, _p(wo), _p(bo))
+    return wo, bo
+
+
+def act(x, kind):
+    y = _c(x, np.float32).copy()
+    lib().orc_act_inplace(_p(y), y.size, kind)
+    return y
+
+
+# ---------------------------------------------------------------- quantization
+def quantize_value(v, scale, zp, qdtype):
+    return lib().orc_quantize_value(v, scale, zp, qdtype)
+
+
+def dequantize_value(q, scale, zp):
+    return lib().orc_dequantize_value(q, scale, zp)
+
+
+def find_scale_zp(data, qdtype=QINT8, symmetric=True):
+    d = _c(data, np.float32).ravel()
+    s, z = F32(), I32()
+    lib().orc_find_scale_zp(_p(d), d.size, qdtype, int(symmetric), C.byref(s), C.byref(z))
+    return s.value, z.value
+
+
+def quantize_tensor(x, scale, zp, qdtype=QINT8):
+    x = _c(x, np.float32)
+    dt = {QINT8: np.int8, QUINT8: np.uint8, QINT32: np.int32}[qdtype]
+    out = np.empty(x.shape, dt)
+    lib().orc_quantize_tensor(_p(x), x.size, scale, zp, qdtype, _p(out))
+    return out
+
+
+def dequantize_tensor(q, scale, zp, qdtype=QINT8):
+    dt = {QINT8: np.int8, QUINT8: np.uint8, QINT32: np.int32}[qdtype]
+    q = _c(q, dt)
+    out = np.empty(q.shape, np.float32)
+    lib().orc_dequantize_tensor(_p(q), q.size, scale, zp, qdtype, _p(out))
+    return out
+
+
+def quantize_sym(x, scale, rounding=ROUND_HALF_AWAY):
+    x = _c(x, np.float32)
+    q = np.empty(x.shape, np.int8)
+    lib().orc_quantize_sym(_p(x), _p(q), x.size, scale, rounding)
+    return q
+
+
+def quantize_weights_per_channel(w):
+    w = _c(w, np.float32)
+    rows = w.shape[0]
+    cols = w.size // rows
+    q = np.empty(w.shape, np.int8)
+    s = np.empty(rows, np.float32)
+    lib().orc_quantize_weights_per_channel(_p(w), rows, cols, _p(q), _p(s))
+    return q, s
+
+
+# ---------------------------------------------------------------- INT8 chain
+def gemm_i8_nn(a, b, threads=0):
+    a, b = _c(a, np.int8), _c(b, np.int8)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.empty((m, n), np.int32)
+    lib().orc_gemm_i8_nn(_p(a), _p(b), _p(c), m, n, k, threads)
+    return c
+
+
+def gemm_i8_tn(a, w, threads=0):
+    a, w = _c(a, np.int8), _c(w, np.int8)
+    m, k = a.shape
+    n = w.shape[0]
+    c = np.empty((m, n), np.int32)
+    lib().orc_gemm_i8_tn(_p(a), _p(w), _p(c), m, n, k, threads)
+    return c
+
+
+def requant(acc, bias, scale, act=ACT_NONE, s_out=1.0, rounding=ROUND_HALF_AWAY):
+    acc = _c(acc, np.int32)
+    m, n = acc.shape
+    oi8 = np.empty((m, n), np.int8)
+    of32 = np.empty((m, n), np.float32)
+    oacc = np.empty((m, n), np.int32)
+    lib().orc_requant(_p(acc), m, n, _p(_c(bias, np.int32)), _p(_c(scale, np.float32)), act, s_out,
+                      rounding, _p(oi8), _p(of32), _p(oacc))
+    return oi8, of32, oacc
+
+
+def gemm_i8_chain(a, w, bias, scale, act=ACT_NONE, s_out=1.0, rounding=ROUND_HALF_AWAY,
+                  threads=0, want=("i8", "f32", "i32")):
+    a, w = _c(a, np.int8), _c(w, np.int8)
+    m, k = a.shape
+    n = w.shape[0]
+    oi8 = np.empty((m, n), np.int8) if "i8" in want else None
+    of32 = np.empty((m, n), np.float32) if "f32" in want else None
+    oacc = np.empty((m, n), np.int32) if "i32" in want else None
+    lib().orc_gemm_i8_chain(_p(a), _p(w), m, n, k, _p(_c(bias, np.int32)), _p(_c(scale, np.float32)), act,
+                            s_out, rounding, _p(oi8), _p(of32), _p(oacc), threads)
+    return oi8, of32, oacc
+
+
+def conv2d_i8_nhwc_chain(x, w, bias, scale, stride=(1, 1), pad=(0, 0), dilation=(1, 1), groups=1,
+                         act=ACT_NONE, s_out=1.0, rounding=ROUND_HALF_AWAY, threads=0):
+    """x: [N,H,W,Cin] int8; w: [Cout,KH,KW,Cin/groups] int8; returns NHWC outputs."""
+    x, w = _c(x, np.int8), _c(w, np.int8)
+    n, h, wd, ci = x.shape
+    co, kh, kw, _ = w.shape
+    oh = conv_out_dim(h, kh, stride[0], pad[0], dilation[0])
+    ow = conv_out_dim(wd, kw, stride[1], pad[1], dilation[1])
+    oi8 = np.empty((n, oh, ow, co), np.int8)
+    of32 = np.empty((n, oh, ow, co), np.float32)
+    oacc = np.empty((n, oh, ow, co), np.int32)
+    lib().orc_conv2d_i8_nhwc_chain(_p(x), _p(w), n, h, wd, ci, co, kh, kw, stride[0], stride[1], pad[0],
+                                   pad[1], dilation[0], dilation[1], groups, _p(_c(bias, np.int32)),
+                                   _p(_c(scale, np.float32)), act, s_out, rounding, _p(oi8), _p(of32),
+                                   _p(oacc), threads)
+    return oi8, of32, oacc
