@@ -240,6 +240,35 @@ lsc_status lsc_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n, i
                        int32_t rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
                        lsc_stream stream);
 
+/* quantize_tensor, per-tensor (quantization/helpers.rs:11-50 with quantize_value :139-155):
+ *   q = clamp(sat_i32(R(x / scale)) + zero_point, qmin, qmax)   (i32 add wraps)
+ * qdtype: LSC_DTYPE_QINT8/I8 -> int8 out, QUINT8/U8 -> uint8, QINT32/I32 -> int32.
+ * R = LSC_ROUND_HALF_AWAY reproduces the reference; HALF_EVEN is offered as a variant. */
+lsc_status lsc_quantize_f32(const float* x, void* out, int64_t n, int32_t qdtype, float scale,
+                            int32_t zero_point, int32_t rounding, lsc_stream stream);
+/* per-channel form (QuantizationParameters::new_per_channel, quantization/scheme.rs:75-90):
+ * element i uses channel c = (i / inner) % channels; scales/zero_points are device arrays
+ * (zero_points may be NULL = all zero). */
+lsc_status lsc_quantize_f32_per_channel(const float* x, void* out, int64_t n, int32_t qdtype,
+                                        const float* scales, const int32_t* zero_points,
+                                        int32_t channels, int64_t inner, int32_t rounding,
+                                        lsc_stream stream);
+/* dequantize_tensor (quantization/helpers.rs:53-94, dequantize_value :158-160):
+ *   x = ((f32)q - (f32)zero_point) * scale */
+lsc_status lsc_dequantize(const void* q, int32_t qdtype, float* out, int64_t n, float scale,
+                          int32_t zero_point, lsc_stream stream);
+lsc_status lsc_dequantize_per_channel(const void* q, int32_t qdtype, float* out, int64_t n,
+                                      const float* scales, const int32_t* zero_points,
+                                      int32_t channels, int64_t inner, lsc_stream stream);
+/* find_scale_zp (quantization/helpers.rs:101-136) over a device f32 array.  Writes the scale
+ * and zero point to device memory.  `workspace` is caller-provided device scratch of at
+ * least lsc_find_scale_zp_workspace_size() bytes (4-byte aligned); calls that share a
+ * workspace must be ordered on one stream. */
+uint64_t lsc_find_scale_zp_workspace_size(void);
+lsc_status lsc_find_scale_zp_f32(const float* x, int64_t n, int32_t qdtype, int32_t symmetric,
+                                 void* workspace, uint64_t workspace_bytes, float* scale_out,
+                                 int32_t* zero_point_out, lsc_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -106,6 +106,12 @@ SIGNATURES = {
     "lsc_memcpy_d2h": (ST, [P, P, C.c_uint64, P]),
     "lsc_check_device": (ST, [C.POINTER(C.c_uint32)]),
     "lsc_gemm_i8": (ST, [P, P, I64, I64, I64, P, P, F32, I32, I32, P, P, P, P]),
+    "lsc_quantize_f32": (ST, [P, P, I64, I32, F32, I32, I32, P]),
+    "lsc_quantize_f32_per_channel": (ST, [P, P, I64, I32, P, P, I32, I64, I32, P]),
+    "lsc_dequantize": (ST, [P, I32, P, I64, F32, I32, P]),
+    "lsc_dequantize_per_channel": (ST, [P, I32, P, I64, P, P, I32, I64, P]),
+    "lsc_find_scale_zp_workspace_size": (C.c_uint64, []),
+    "lsc_find_scale_zp_f32": (ST, [P, I64, I32, I32, P, C.c_uint64, P, P, P]),
 }
 
 _lib = None

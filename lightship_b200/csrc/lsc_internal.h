@@ -50,4 +50,17 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
                           int rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
                           int64_t ldo, cudaStream_t stream);
 
+// Quantization kernels (quant.cu).  `scales` == nullptr selects the per-tensor form with
+// scale0/zp0; otherwise channel c = (i / inner) % channels.
+lsc_status launch_quantize(const float* x, void* out, int64_t n, int qdtype, const float* scales,
+                           const int32_t* zps, float scale0, int32_t zp0, int32_t channels,
+                           int64_t inner, int rounding, cudaStream_t st);
+lsc_status launch_dequantize(const void* q, int qdtype, float* out, int64_t n, const float* scales,
+                             const int32_t* zps, float scale0, int32_t zp0, int32_t channels,
+                             int64_t inner, cudaStream_t st);
+constexpr uint64_t kFindScaleZpWorkspace = 16;
+lsc_status launch_find_scale_zp(const float* x, int64_t n, int qdtype, int symmetric,
+                                void* workspace, uint64_t workspace_bytes, float* scale_out,
+                                int32_t* zp_out, cudaStream_t st);
+
 }  // namespace lsc

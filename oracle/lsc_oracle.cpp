@@ -351,7 +351,9 @@ int orc_find_scale_zp(const float* data, int64_t n, int qdtype, int symmetric, f
     *scale = am > 0.0f ? am / (float)qmax : 1.0f;
     *zero_point = 0;
   } else {
-    const float s = mx > mn ? (mx - mn) / (float)(qmax - qmin) : 1.0f;
+    // (qmax - qmin) is an i32 subtraction in the reference; it wraps for QInt32.
+    const int32_t span = (int32_t)((uint32_t)qmax - (uint32_t)qmin);
+    const float s = mx > mn ? (mx - mn) / (float)span : 1.0f;
     const float z = (float)qmin - mn / s;
     *scale = s;
     *zero_point = rust_f32_to_i32(roundf(z));
