@@ -240,6 +240,20 @@ lsc_status lsc_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n, i
                        int32_t rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
                        lsc_stream stream);
 
+/* INT8 convolution on NHWC activations, as an implicit GEMM with the INT8 chain's epilogue
+ * (the quantized form of Conv2d::forward, operator/convolution.rs:90-267, with
+ * Conv2dConfig's stride/padding/dilation, convolution.rs:12-62; groups = 1):
+ *   x [N, H, W, C] int8 with C a multiple of 16 (pad channels with zeros),
+ *   w [Cout, KH, KW, C] int8 (K ordered kh, kw, c), scale [Cout], bias [Cout] or NULL,
+ *   outputs NHWC [N, OH, OW, Cout] with OH = (H + 2 ph - dh (KH-1) - 1) / sh + 1 (same for W).
+ * Limits of the im2col load unit: stride <= 8, padding <= 127. */
+lsc_status lsc_conv2d_i8_nhwc(const int8_t* x, const int8_t* w, int64_t n, int64_t h, int64_t wd,
+                              int64_t c, int64_t c_out, int64_t kh, int64_t kw, int64_t sh,
+                              int64_t sw, int64_t ph, int64_t pw, int64_t dh, int64_t dw,
+                              const int32_t* bias, const float* scale, float s_out, int32_t act,
+                              int32_t rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
+                              lsc_stream stream);
+
 /* quantize_tensor, per-tensor (quantization/helpers.rs:11-50 with quantize_value :139-155):
  *   q = clamp(sat_i32(R(x / scale)) + zero_point, qmin, qmax)   (i32 add wraps)
  * qdtype: LSC_DTYPE_QINT8/I8 -> int8 out, QUINT8/U8 -> uint8, QINT32/I32 -> int32.

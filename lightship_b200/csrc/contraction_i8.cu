@@ -1,0 +1,603 @@
+// contraction_i8.cu -- INT8 x INT8 -> INT32 contractions on the 5th-generation tensor cores
+// with the requantize / dequantize epilogue fused in:
+//   * GEMM  C[M,N] = A[M,K] W[N,K]^T      replaces quantized_gemm_int8 + dequantize +
+//                                         quantize_sym (lightship-core/src/cpu/quantized_ops.rs:13-48)
+//   * NHWC convolution as an implicit GEMM (M = N*OH*OW output pixels, K = KH*KW*C) --
+//     the INT8 counterpart of Conv2d::forward's im2col + GEMM
+//     (lightship-core/src/operator/convolution.rs:90-267) with the column matrix never
+//     materialised: the TMA engine gathers it in im2col mode straight into shared memory.
+//
+// Design (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: the A tile (128 rows x 128 B of K) -- a 2-D tile for GEMM, or
+//               128/ACB im2col loads of ACB channels each for convolution -- and the W tile
+//               (BN rows x 128 B), into a STAGES-deep shared-memory ring (full/empty mbarriers).
+//   warp 1      MMA issuer: one thread issues tcgen05.mma.kind::i8 (M=128, N=BN, K=32) into a
+//               double-buffered s32 accumulator in TMEM (2 x BN columns) and commits each
+//               stage back to the producer and each finished tile to the epilogue.
+//   warps 2-9   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+31, half of the tile's columns), bias, per-channel scale,
+//               activation, requantize, vectorised global stores.  The accumulator buffer is
+//               released right after its last TMEM read so the next tile's MMAs overlap
+//               this tile's epilogue math.
+#include <stdio.h>
+
+#include <mutex>
+
+#include "epilogue.cuh"
+#include "lsc_internal.h"
+#include "sm100.cuh"
+
+namespace lsc {
+namespace {
+
+struct I8Params {
+  int32_t m, n, k;  // GEMM view: rows, output channels, K bytes
+  const int32_t* bias;
+  const float* scale;
+  float s_out;
+  int32_t rounding;
+  int8_t* out_i8;
+  float* out_f32;
+  int32_t* out_i32;
+  int64_t ldo;
+  int32_t vec_ok;  // 16-byte vector stores are legal for full column chunks
+  uint32_t* err;
+  // convolution (ACB > 0)
+  int32_t ow, ohw;           // output width, OH*OW
+  int32_t sw, sh, pw, ph;    // stride / padding
+  int32_t dw, dh, kw;        // dilation, filter width
+  int32_t chunks_per_tap;    // C / ACB
+  int32_t total_chunks;      // KH*KW*C / ACB
+};
+
+template <int BN_>
+struct I8Cfg {
+  static constexpr int BM = 128;
+  static constexpr int BN = BN_;
+  static constexpr int BK = 128;  // int8 elements (= bytes) of K per stage
+  static constexpr int STAGES = BN_ == 256 ? 4 : (BN_ == 128 ? 6 : 8);
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulator buffers; power of 2 >= 32
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int COLS_PER_EPI_WARP = BN / 2;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+  static constexpr uint32_t IDESC = idesc_i8(BM, BN);
+  static_assert(STAGES * STAGE_BYTES + 1024 + BAR_BYTES <= 232448, "shared memory budget");
+  static_assert((2 * STAGES + 5) * 8 + 8 <= BAR_BYTES, "barrier area");
+};
+
+// Epilogue for 32 consecutive columns of one output row held by this thread.
+template <int ACT>
+__device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t (&r)[32],
+                                               int row, int col0) {
+  if (row >= p.m) return;
+  const bool full = (col0 + 32 <= p.n);
+  int32_t acc[32];
+  float y[32];
+  if (full) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      int4 b = make_int4(0, 0, 0, 0);
+      if (p.bias) b = __ldg(reinterpret_cast<const int4*>(p.bias + col0 + j));
+      const float4 s = __ldg(reinterpret_cast<const float4*>(p.scale + col0 + j));
+      acc[j + 0] = static_cast<int32_t>(r[j + 0] + static_cast<uint32_t>(b.x));
+      acc[j + 1] = static_cast<int32_t>(r[j + 1] + static_cast<uint32_t>(b.y));
+      acc[j + 2] = static_cast<int32_t>(r[j + 2] + static_cast<uint32_t>(b.z));
+      acc[j + 3] = static_cast<int32_t>(r[j + 3] + static_cast<uint32_t>(b.w));
+      y[j + 0] = apply_act<ACT>(dequant(acc[j + 0], s.x));
+      y[j + 1] = apply_act<ACT>(dequant(acc[j + 1], s.y));
+      y[j + 2] = apply_act<ACT>(dequant(acc[j + 2], s.z));
+      y[j + 3] = apply_act<ACT>(dequant(acc[j + 3], s.w));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int c = col0 + j;
+      if (c < p.n) {
+        const int32_t b = p.bias ? __ldg(p.bias + c) : 0;
+        acc[j] = static_cast<int32_t>(r[j] + static_cast<uint32_t>(b));
+        y[j] = apply_act<ACT>(dequant(acc[j], __ldg(p.scale + c)));
+      } else {
+        acc[j] = 0;
+        y[j] = 0.0f;
+      }
+    }
+  }
+  const int64_t base = static_cast<int64_t>(row) * p.ldo + col0;
+  if (full && p.vec_ok) {
+    if (p.out_i8) {
+      uint32_t pk[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t w = 0;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int32_t q = p.rounding == LSC_ROUND_HALF_EVEN
+                                ? requant_i8<LSC_ROUND_HALF_EVEN>(y[4 * j + t], p.s_out)
+                                : requant_i8<LSC_ROUND_HALF_AWAY>(y[4 * j + t], p.s_out);
+          w |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * t);
+        }
+        pk[j] = w;
+      }
+      uint4* dst = reinterpret_cast<uint4*>(p.out_i8 + base);
+      dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    }
+    if (p.out_f32) {
+      float4* dst = reinterpret_cast<float4*>(p.out_f32 + base);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dst[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+    }
+    if (p.out_i32) {
+      int4* dst = reinterpret_cast<int4*>(p.out_i32 + base);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dst[j] = make_int4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (col0 + j >= p.n) break;
+      if (p.out_i8)
+        p.out_i8[base + j] = static_cast<int8_t>(
+            p.rounding == LSC_ROUND_HALF_EVEN ? requant_i8<LSC_ROUND_HALF_EVEN>(y[j], p.s_out)
+                                              : requant_i8<LSC_ROUND_HALF_AWAY>(y[j], p.s_out));
+      if (p.out_f32) p.out_f32[base + j] = y[j];
+      if (p.out_i32) p.out_i32[base + j] = acc[j];
+    }
+  }
+}
+
+// Shared-memory descriptor of the A operand for the kk-th K=32 slice of a stage.
+// ACB = 0: dense 128-byte rows (128-byte swizzle).  ACB > 0: the stage holds 128/ACB
+// im2col sub-tiles of [128 rows x ACB bytes] with the swizzle that matches ACB.
+template <int ACB>
+__device__ __forceinline__ uint64_t a_desc(uint32_t a0, int kk) {
+  if constexpr (ACB == 0 || ACB == 128) {
+    return smem_desc_sw128_kmajor(a0 + kk * 32);
+  } else if constexpr (ACB == 64) {
+    return smem_desc_sw64_kmajor(a0 + (kk >> 1) * (128 * 64) + (kk & 1) * 32);
+  } else if constexpr (ACB == 32) {
+    return smem_desc_sw32_kmajor(a0 + kk * (128 * 32));
+  } else {
+    static_assert(ACB == 16, "channel block must be 16, 32, 64 or 128 bytes");
+    return smem_desc_noswz_kmajor(a0 + kk * 2 * (128 * 16), 128 * 16, 128);
+  }
+}
+
+template <int BN, int ACT, int ACB>
+__global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
+    contraction_i8_kernel(const __grid_constant__ CUtensorMap tmA,
+                          const __grid_constant__ CUtensorMap tmW, const I8Params p) {
+  using C = I8Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sW = smem + C::STAGES * C::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C::STAGES;
+  uint64_t* tfull = bars + 2 * C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], C::EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int m_tiles = (p.m + C::BM - 1) / C::BM;
+  const int n_tiles = (p.n + C::BN - 1) / C::BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kblocks = (p.k + C::BK - 1) / C::BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- TMA producer
+      uint32_t stage = 0, phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mb = tile % m_tiles, nb = tile / m_tiles;
+        // filter-origin coordinates of the tile's first output pixel (convolution only)
+        int32_t cw = 0, chh = 0, cn = 0;
+        if constexpr (ACB > 0) {
+          const int m0 = mb * C::BM;
+          cn = m0 / p.ohw;
+          const int rem = m0 - cn * p.ohw;
+          const int oy = rem / p.ow;
+          const int ox = rem - oy * p.ow;
+          cw = ox * p.sw - p.pw;
+          chh = oy * p.sh - p.ph;
+        }
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          uint8_t* a_dst = sA + stage * C::A_BYTES;
+          if constexpr (ACB == 0) {
+            tma_load_2d(&tmA, &full[stage], a_dst, kb * C::BK, mb * C::BM);
+          } else {
+            constexpr int SUB = 128 / ACB;
+#pragma unroll
+            for (int i = 0; i < SUB; ++i) {
+              int j = kb * SUB + i;  // channel chunk index in (kh, kw, c) order
+              if (j >= p.total_chunks) j = 0;  // past the filter: weights are zero there
+              const int tap = j / p.chunks_per_tap;
+              const int c0 = (j - tap * p.chunks_per_tap) * ACB;
+              const int ky = tap / p.kw;
+              const int kx = tap - ky * p.kw;
+              tma_load_im2col_4d(&tmA, &full[stage], a_dst + i * (C::BM * ACB), c0, cw, chh, cn,
+                                 static_cast<uint16_t>(kx * p.dw), static_cast<uint16_t>(ky * p.dh));
+            }
+          }
+          tma_load_2d(&tmW, &full[stage], sW + stage * C::B_BYTES, kb * C::BK, nb * C::BN);
+          ++issued;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already in flight land before the CTA can exit.
+        volatile uint32_t no_abort = 0;
+        const int outstanding = issued < C::STAGES ? issued : C::STAGES;
+        for (int i = 1; i <= outstanding; ++i) {
+          const int idx = issued - i;
+          const int s = idx % C::STAGES;
+          const uint32_t ph = static_cast<uint32_t>((idx / C::STAGES) & 1);
+          mbar_wait(&full[s], ph, &no_abort, p.err);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- MMA issuer
+      uint32_t stage = 0, phase = 0;
+      int local = 0;
+      bool ok = true;
+      bool any_mma = false;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!mbar_wait(&tempty[buf], buf_phase ^ 1u, abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * C::BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t w0 = smem_u32(sW + stage * C::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < C::BK / 32; ++kk) {
+            const uint64_t ad = a_desc<ACB>(a0, kk);
+            const uint64_t wd = smem_desc_sw128_kmajor(w0 + kk * 32);
+            mma_i8(d_tmem, ad, wd, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+          }
+          any_mma = true;
+          mma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) mma_commit(&tfull[buf]);
+      }
+      if (!ok && any_mma) {
+        // Wait for the MMAs already issued before TMEM is released.
+        volatile uint32_t no_abort = 0;
+        mma_commit(drain);
+        mbar_wait(drain, 0u, &no_abort, p.err);
+      }
+    }
+  } else {
+    // --------------------------------------------------------------- epilogue
+    const int epi = warp - 2;       // 0..7
+    const int quarter = warp & 3;   // TMEM lane quarter this warp may read
+    const int half = epi >> 2;      // which half of the tile's columns
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int mb = tile % m_tiles, nb = tile / m_tiles;
+      const int buf = local & 1;
+      const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
+      if (!mbar_wait(&tfull[buf], buf_phase, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int row = mb * C::BM + row_in_tile;
+      constexpr int CHUNKS = C::COLS_PER_EPI_WARP / 32;
+#pragma unroll 1
+      for (int c = 0; c < CHUNKS; ++c) {
+        const int tcol = half * C::COLS_PER_EPI_WARP + c * 32;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(buf * C::BN + tcol);
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr, r);
+        tmem_ld_wait();
+        if (c == CHUNKS - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+        epilogue_chunk<ACT>(p, r, row, nb * C::BN + tcol);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int BN, int ACT, int ACB>
+lsc_status launch_cfg(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p,
+                      int sm_count, cudaStream_t stream) {
+  using C = I8Cfg<BN>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(contraction_i8_kernel<BN, ACT, ACB>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(contraction_i8)");
+  const int tiles = ((p.m + C::BM - 1) / C::BM) * ((p.n + C::BN - 1) / C::BN);
+  const int grid = tiles < sm_count ? tiles : sm_count;
+  contraction_i8_kernel<BN, ACT, ACB><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tw, p);
+  LSC_CUDA_TRY(cudaGetLastError());
+  return LSC_SUCCESS;
+}
+
+template <int BN, int ACB>
+lsc_status launch_act(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p, int act,
+                      int sm_count, cudaStream_t stream) {
+  switch (act) {
+    case LSC_ACT_RELU: return launch_cfg<BN, LSC_ACT_RELU, ACB>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_RELU6: return launch_cfg<BN, LSC_ACT_RELU6, ACB>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_SILU: return launch_cfg<BN, LSC_ACT_SILU, ACB>(ta, tw, p, sm_count, stream);
+    default: return launch_cfg<BN, LSC_ACT_NONE, ACB>(ta, tw, p, sm_count, stream);
+  }
+}
+
+template <int ACB>
+lsc_status launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p,
+                     int act, int sm_count, cudaStream_t stream) {
+  switch (bn) {
+    case 64: return launch_act<64, ACB>(ta, tw, p, act, sm_count, stream);
+    case 128: return launch_act<128, ACB>(ta, tw, p, act, sm_count, stream);
+    default: return launch_act<256, ACB>(ta, tw, p, act, sm_count, stream);
+  }
+}
+
+// Column tile width: the widest tile that does not waste most of its columns.
+int pick_bn(int64_t n) {
+  if (n <= 64) return 64;
+  if (n <= 128) return 128;
+  if (n % 256 == 0 || n % 128 != 0) return 256;
+  return 128;
+}
+
+lsc_status check_common(int64_t m, int64_t n, int act, int rounding, const float* scale,
+                        int8_t* out_i8, float* out_f32, int32_t* out_i32, const char* who) {
+  if (m < 0 || n < 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: negative size", who);
+  if (!out_i8 && !out_f32 && !out_i32)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: no output given", who);
+  if (m > 0 && n > 0 && !scale) return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: null scale", who);
+  if (act < LSC_ACT_NONE || act > LSC_ACT_SILU)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: bad activation %d", who, act);
+  if (rounding != LSC_ROUND_HALF_AWAY && rounding != LSC_ROUND_HALF_EVEN)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: bad rounding %d", who, rounding);
+  return LSC_SUCCESS;
+}
+
+void fill_outputs(I8Params& p, const int32_t* bias, const float* scale, float s_out, int rounding,
+                  int8_t* out_i8, float* out_f32, int32_t* out_i32, int64_t ldo, uint32_t* err) {
+  p.bias = bias;
+  p.scale = scale;
+  p.s_out = s_out;
+  p.rounding = rounding;
+  p.out_i8 = out_i8;
+  p.out_f32 = out_f32;
+  p.out_i32 = out_i32;
+  p.ldo = ldo;
+  const uintptr_t align_bits = reinterpret_cast<uintptr_t>(out_i8) |
+                               reinterpret_cast<uintptr_t>(out_f32) |
+                               reinterpret_cast<uintptr_t>(out_i32) |
+                               reinterpret_cast<uintptr_t>(scale) |
+                               reinterpret_cast<uintptr_t>(bias);
+  p.vec_ok = ((align_bits & 15) == 0 && (ldo % 16) == 0) ? 1 : 0;
+  p.err = err;
+}
+
+}  // namespace
+
+lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k,
+                          const int32_t* bias, const float* scale, float s_out, int act,
+                          int rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
+                          int64_t ldo, cudaStream_t stream) {
+  lsc_status st = check_common(m, n, act, rounding, scale, out_i8, out_f32, out_i32, "gemm_i8");
+  if (st) return st;
+  if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_i8: size too large");
+  if (m == 0 || n == 0) return LSC_SUCCESS;
+  if (!a || !w) return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_i8: null operand");
+  if (k <= 0 || k % 16 != 0)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT,
+                     "gemm_i8: K must be a positive multiple of 16 (got %lld)", (long long)k);
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w)) & 15)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_i8: A and W must be 16-byte aligned");
+  if (ldo < n) return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_i8: ldo < n");
+  DeviceState* ds = current_device_state();
+  if (!ds) return LSC_ERROR_DEVICE_ERROR;
+  if (ds->cc_major != 10)
+    return set_error(LSC_ERROR_BACKEND_NOT_AVAILABLE,
+                     "gemm_i8: needs an sm_100 (B200) device, found sm_%d%d", ds->cc_major,
+                     ds->cc_minor);
+
+  const int bn = pick_bn(n);
+  CUtensorMap ta, tw;
+  st = encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, m, k, 128, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  st = encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, k, n, k, 128, bn,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+
+  I8Params p{};
+  p.m = static_cast<int32_t>(m);
+  p.n = static_cast<int32_t>(n);
+  p.k = static_cast<int32_t>(k);
+  fill_outputs(p, bias, scale, s_out, rounding, out_i8, out_f32, out_i32, ldo, ds->err_word);
+  return launch_bn<0>(bn, ta, tw, p, act, ds->sm_count, stream);
+}
+
+lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& g,
+                          const int32_t* bias, const float* scale, float s_out, int act,
+                          int rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
+                          cudaStream_t stream) {
+  const int64_t m = g.n * g.oh * g.ow;
+  lsc_status st = check_common(m, g.c_out, act, rounding, scale, out_i8, out_f32, out_i32, "conv_i8");
+  if (st) return st;
+  if (g.n < 0 || g.h <= 0 || g.w <= 0 || g.c <= 0 || g.kh <= 0 || g.kw <= 0 || g.sh <= 0 ||
+      g.sw <= 0 || g.dh <= 0 || g.dw <= 0 || g.ph < 0 || g.pw < 0)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "conv_i8: bad geometry");
+  if (g.oh != (g.h + 2 * g.ph - g.dh * (g.kh - 1) - 1) / g.sh + 1 ||
+      g.ow != (g.w + 2 * g.pw - g.dw * (g.kw - 1) - 1) / g.sw + 1 || g.oh <= 0 || g.ow <= 0)
+    return set_error(LSC_ERROR_SHAPE_MISMATCH, "conv_i8: output size does not match the geometry");
+  if (g.c % 16 != 0)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "conv_i8: stored channels must be a multiple of 16 (got %lld)",
+                     (long long)g.c);
+  if (g.sh > 8 || g.sw > 8 || g.ph > 127 || g.pw > 127 ||
+      g.ph - (g.kh - 1) * g.dh < -128 || g.pw - (g.kw - 1) * g.dw < -128 ||
+      (g.kh - 1) * g.dh > 65535 || (g.kw - 1) * g.dw > 65535)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "conv_i8: stride/padding/filter outside the im2col unit's range");
+  if (m == 0 || g.c_out == 0) return LSC_SUCCESS;
+  if (m > INT32_MAX / 2 || g.n * g.h * g.w * g.c > (int64_t(1) << 40))
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "conv_i8: problem too large");
+  if (!x || !w) return set_error(LSC_ERROR_INVALID_ARGUMENT, "conv_i8: null operand");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "conv_i8: x and w must be 16-byte aligned");
+  DeviceState* ds = current_device_state();
+  if (!ds) return LSC_ERROR_DEVICE_ERROR;
+  if (ds->cc_major != 10)
+    return set_error(LSC_ERROR_BACKEND_NOT_AVAILABLE, "conv_i8: needs an sm_100 (B200) device");
+
+  const int acb = g.c % 128 == 0 ? 128 : (g.c % 64 == 0 ? 64 : (g.c % 32 == 0 ? 32 : 16));
+  const int64_t k = g.kh * g.kw * g.c;
+  const uint64_t dims[4] = {static_cast<uint64_t>(g.c), static_cast<uint64_t>(g.w),
+                            static_cast<uint64_t>(g.h), static_cast<uint64_t>(g.n)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(g.c), static_cast<uint64_t>(g.w * g.c),
+                               static_cast<uint64_t>(g.h * g.w * g.c)};
+  const int lower[2] = {static_cast<int>(-g.pw), static_cast<int>(-g.ph)};
+  const int upper[2] = {static_cast<int>(g.pw - (g.kw - 1) * g.dw),
+                        static_cast<int>(g.ph - (g.kh - 1) * g.dh)};
+  const uint32_t estr[4] = {1, static_cast<uint32_t>(g.sw), static_cast<uint32_t>(g.sh), 1};
+  const CUtensorMapSwizzle swz = acb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : acb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                 : acb == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                             : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUtensorMap ta, tw;
+  st = encode_tmap_im2col(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, x, dims, strides, lower, upper,
+                          static_cast<uint32_t>(acb), 128, estr, swz);
+  if (st) return st;
+  const int bn = pick_bn(g.c_out);
+  st = encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, static_cast<uint64_t>(k),
+                      static_cast<uint64_t>(g.c_out), static_cast<uint64_t>(k), 128, bn,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+
+  I8Params p{};
+  p.m = static_cast<int32_t>(m);
+  p.n = static_cast<int32_t>(g.c_out);
+  const int64_t total_chunks = g.kh * g.kw * (g.c / acb);
+  const int64_t sub = 128 / acb;
+  p.k = static_cast<int32_t>(((total_chunks + sub - 1) / sub) * 128);
+  p.ow = static_cast<int32_t>(g.ow);
+  p.ohw = static_cast<int32_t>(g.oh * g.ow);
+  p.sw = static_cast<int32_t>(g.sw);
+  p.sh = static_cast<int32_t>(g.sh);
+  p.pw = static_cast<int32_t>(g.pw);
+  p.ph = static_cast<int32_t>(g.ph);
+  p.dw = static_cast<int32_t>(g.dw);
+  p.dh = static_cast<int32_t>(g.dh);
+  p.kw = static_cast<int32_t>(g.kw);
+  p.chunks_per_tap = static_cast<int32_t>(g.c / acb);
+  p.total_chunks = static_cast<int32_t>(total_chunks);
+  fill_outputs(p, bias, scale, s_out, rounding, out_i8, out_f32, out_i32, g.c_out, ds->err_word);
+  switch (acb) {
+    case 128: return launch_bn<128>(bn, ta, tw, p, act, ds->sm_count, stream);
+    case 64: return launch_bn<64>(bn, ta, tw, p, act, ds->sm_count, stream);
+    case 32: return launch_bn<32>(bn, ta, tw, p, act, ds->sm_count, stream);
+    default: return launch_bn<16>(bn, ta, tw, p, act, ds->sm_count, stream);
+  }
+}
+
+}  // namespace lsc
+
+extern "C" lsc_status lsc_conv2d_i8_nhwc(const int8_t* x, const int8_t* w, int64_t n, int64_t h,
+                                         int64_t wd, int64_t c, int64_t c_out, int64_t kh,
+                                         int64_t kw, int64_t sh, int64_t sw, int64_t ph,
+                                         int64_t pw, int64_t dh, int64_t dw, const int32_t* bias,
+                                         const float* scale, float s_out, int32_t act,
+                                         int32_t rounding, int8_t* out_i8, float* out_f32,
+                                         int32_t* out_i32, lsc_stream stream) {
+  lsc::ConvGeometry g{};
+  g.n = n;
+  g.h = h;
+  g.w = wd;
+  g.c = c;
+  g.c_out = c_out;
+  g.kh = kh;
+  g.kw = kw;
+  g.sh = sh;
+  g.sw = sw;
+  g.ph = ph;
+  g.pw = pw;
+  g.dh = dh;
+  g.dw = dw;
+  if (sh <= 0 || sw <= 0)
+    return lsc::set_error(LSC_ERROR_INVALID_ARGUMENT, "conv2d_i8: stride must be positive");
+  g.oh = (h + 2 * ph - dh * (kh - 1) - 1) / sh + 1;
+  g.ow = (wd + 2 * pw - dw * (kw - 1) - 1) / sw + 1;
+  return lsc::launch_conv_i8(x, w, g, bias, scale, s_out, act, rounding, out_i8, out_f32,
+                             out_i32, static_cast<cudaStream_t>(stream));
+}

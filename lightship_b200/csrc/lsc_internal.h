@@ -43,7 +43,30 @@ lsc_status encode_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, const voi
                           const uint32_t box[4], const uint32_t elem_strides[4],
                           CUtensorMapSwizzle swizzle);
 
-// INT8 GEMM + requant/dequant epilogue (gemm_i8.cu).  ldo = row stride of the outputs in
+// 4-D NHWC tensor map in im2col mode (cuTensorMapEncodeIm2col).
+lsc_status encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                              const uint64_t dims[4], const uint64_t strides_bytes[3],
+                              const int lower[2], const int upper[2], uint32_t channels_per_pixel,
+                              uint32_t pixels_per_column, const uint32_t elem_strides[4],
+                              CUtensorMapSwizzle swizzle);
+
+// Convolution geometry for the NHWC INT8 implicit GEMM.
+struct ConvGeometry {
+  int64_t n, h, w, c;       // input NHWC; c = channels as stored (multiple of 16)
+  int64_t c_out;
+  int64_t kh, kw;
+  int64_t sh, sw, ph, pw, dh, dw;
+  int64_t oh, ow;
+};
+
+// INT8 NHWC convolution as an implicit GEMM (contraction_i8.cu): x [N,H,W,C] int8,
+// w [Cout, KH*KW*C] int8 (K ordered kh, kw, c), outputs NHWC [N,OH,OW,Cout].
+lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& g,
+                          const int32_t* bias, const float* scale, float s_out, int act,
+                          int rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
+                          cudaStream_t stream);
+
+// INT8 GEMM + requant/dequant epilogue (contraction_i8.cu).  ldo = row stride of the outputs in
 // elements.  Validates its arguments.
 lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k,
                           const int32_t* bias, const float* scale, float s_out, int act,

@@ -122,7 +122,46 @@ lsc_status encode(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, 
                      static_cast<int>(r));
   return LSC_SUCCESS;
 }
+typedef CUresult (*EncodeIm2colFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const int*, const int*,
+                                   cuuint32_t, cuuint32_t, const cuuint32_t*,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeIm2colFn encode_im2col_fn() {
+  static std::once_flag once;
+  static EncodeIm2colFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeIm2colFn>(p);
+  });
+  return fn;
+}
 }  // namespace
+
+lsc_status encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                              const uint64_t dims[4], const uint64_t strides_bytes[3],
+                              const int lower[2], const int upper[2], uint32_t channels_per_pixel,
+                              uint32_t pixels_per_column, const uint32_t elem_strides[4],
+                              CUtensorMapSwizzle swizzle) {
+  EncodeIm2colFn fn = encode_im2col_fn();
+  if (!fn) return set_error(LSC_ERROR_DEVICE_ERROR, "cuTensorMapEncodeIm2col unavailable");
+  const cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  const cuuint64_t s[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  const cuuint32_t e[4] = {elem_strides[0], elem_strides[1], elem_strides[2], elem_strides[3]};
+  const CUresult r = fn(map, dtype, 4, const_cast<void*>(base), d, s, lower, upper,
+                        channels_per_pixel, pixels_per_column, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "cuTensorMapEncodeIm2col failed (CUresult %d)",
+                     static_cast<int>(r));
+  return LSC_SUCCESS;
+}
 
 lsc_status encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
                           uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,

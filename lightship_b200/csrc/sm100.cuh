@@ -154,6 +154,54 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_kmajor(uint32_t saddr) {
   return d;
 }
 
+// K-major operand with 64-byte rows (64-byte swizzle): 8-row atoms of 512 B.
+__device__ __forceinline__ uint64_t smem_desc_sw64_kmajor(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(512u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)4u << 61;
+  return d;
+}
+
+// K-major operand with 32-byte rows (32-byte swizzle): 8-row atoms of 256 B.
+__device__ __forceinline__ uint64_t smem_desc_sw32_kmajor(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(256u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)6u << 61;
+  return d;
+}
+
+// K-major operand without swizzle: 8x16-byte core matrices; `lbo` = bytes between the two
+// 16-byte K chunks of one MMA, `sbo` = bytes between consecutive 8-row groups.
+__device__ __forceinline__ uint64_t smem_desc_noswz_kmajor(uint32_t saddr, uint32_t lbo,
+                                                           uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  return d;
+}
+
+// TMA load in im2col mode: 4-D NHWC tensor (coordinates c, w, h, n of the first output
+// pixel's filter origin), filter offsets (w_off, h_off).  The box is the tensor map's
+// pixelsPerColumn output pixels x channelsPerPixel channels.
+__device__ __forceinline__ void tma_load_im2col_4d(const CUtensorMap* m, uint64_t* bar, void* dst,
+                                                   int32_t c, int32_t w, int32_t h, int32_t n,
+                                                   uint16_t w_off, uint16_t h_off) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c), "r"(w), "r"(h), "r"(n),
+      "h"(w_off), "h"(h_off)
+      : "memory");
+}
+
 // Same for an MN-major operand: 128-byte rows along M/N (one K index per row), 8 K-rows per
 // atom (SBO = 1024 B); consecutive 128-byte column blocks are `lbo` bytes apart.
 __device__ __forceinline__ uint64_t smem_desc_sw128_mnmajor(uint32_t saddr, uint32_t lbo) {

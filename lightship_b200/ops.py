@@ -52,6 +52,36 @@ def gemm_i8(a, w, scale, bias=None, s_out=1.0, act=_lib.ACT_NONE,
     return q, y, acc
 
 
+def conv2d_i8_nhwc(x, w, scale, bias=None, stride=(1, 1), pad=(0, 0), dilation=(1, 1),
+                   s_out=1.0, act=_lib.ACT_NONE, rounding=_lib.ROUND_HALF_AWAY,
+                   out_i8=True, out_f32=False, out_i32=False):
+    """INT8 NHWC convolution (implicit GEMM on the tensor cores, im2col by the TMA unit).
+
+    x: [N,H,W,C] int8 (C a multiple of 16), w: [Cout,KH,KW,C] int8, scale: [Cout] f32,
+    bias: [Cout] int32 or None.  Returns (q_i8, y_f32, acc_i32) as NHWC, None unless asked.
+    """
+    _need(x, torch.int8, "x")
+    _need(w, torch.int8, "w")
+    _need(scale, torch.float32, "scale")
+    _need(bias, torch.int32, "bias")
+    n, h, wd, c = x.shape
+    co, kh, kw, cw = w.shape
+    if cw != c:
+        raise ValueError(f"conv2d_i8_nhwc: channel mismatch {x.shape} vs {w.shape}")
+    oh = (h + 2 * pad[0] - dilation[0] * (kh - 1) - 1) // stride[0] + 1
+    ow = (wd + 2 * pad[1] - dilation[1] * (kw - 1) - 1) // stride[1] + 1
+    dev = x.device
+    shape = (n, oh, ow, co)
+    q = torch.empty(shape, dtype=torch.int8, device=dev) if out_i8 else None
+    y = torch.empty(shape, dtype=torch.float32, device=dev) if out_f32 else None
+    acc = torch.empty(shape, dtype=torch.int32, device=dev) if out_i32 else None
+    check(lib().lsc_conv2d_i8_nhwc(_ptr(x), _ptr(w), n, h, wd, c, co, kh, kw, stride[0], stride[1],
+                                   pad[0], pad[1], dilation[0], dilation[1], _ptr(bias), _ptr(scale),
+                                   float(s_out), act, rounding, _ptr(q), _ptr(y), _ptr(acc),
+                                   _stream(dev)))
+    return q, y, acc
+
+
 def check_device() -> int:
     """Synchronizes and returns the device error word (raises on a device-side error)."""
     w = C.c_uint32(0)
