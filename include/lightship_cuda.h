@@ -282,6 +282,16 @@ uint64_t lsc_find_scale_zp_workspace_size(void);
 lsc_status lsc_find_scale_zp_f32(const float* x, int64_t n, int32_t qdtype, int32_t symmetric,
                                  void* workspace, uint64_t workspace_bytes, float* scale_out,
                                  int32_t* zero_point_out, lsc_stream stream);
+/* find_scale_zp applied per channel (the per-channel QuantizationParameters of
+ * quantization/scheme.rs:75-90 calibrated with helpers.rs:101-136): x is [channels,
+ * per_channel] row-major (a weight [Cout, K]); writes channels scales and zero points to
+ * device memory.  `workspace`: caller-provided device scratch of at least
+ * lsc_find_scale_zp_per_channel_workspace_size(channels) bytes (12 per channel). */
+uint64_t lsc_find_scale_zp_per_channel_workspace_size(int64_t channels);
+lsc_status lsc_find_scale_zp_per_channel_f32(const float* x, int64_t channels, int64_t per_channel,
+                                             int32_t qdtype, int32_t symmetric, void* workspace,
+                                             uint64_t workspace_bytes, float* scales_out,
+                                             int32_t* zero_points_out, lsc_stream stream);
 
 #ifdef __cplusplus
 }

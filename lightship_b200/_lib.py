@@ -113,6 +113,8 @@ SIGNATURES = {
     "lsc_dequantize_per_channel": (ST, [P, I32, P, I64, P, P, I32, I64, P]),
     "lsc_find_scale_zp_workspace_size": (C.c_uint64, []),
     "lsc_find_scale_zp_f32": (ST, [P, I64, I32, I32, P, C.c_uint64, P, P, P]),
+    "lsc_find_scale_zp_per_channel_workspace_size": (C.c_uint64, [I64]),
+    "lsc_find_scale_zp_per_channel_f32": (ST, [P, I64, I64, I32, I32, P, C.c_uint64, P, P, P]),
 }
 
 _lib = None

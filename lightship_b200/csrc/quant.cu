@@ -123,6 +123,28 @@ __device__ __forceinline__ float fkey_inv(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
+// The reference's scale / zero point from the folded min/max keys.  No key (all inputs NaN
+// or none) leaves the fold at (+inf, -inf), as the reference's fold does.
+__device__ __forceinline__ void finalize_scale_zp(uint32_t gmin, uint32_t gmax, int qdtype,
+                                                  int symmetric, float* scale_out,
+                                                  int32_t* zp_out) {
+  const float mn = gmin == 0xFFFFFFFFu ? __int_as_float(0x7f800000) : fkey_inv(gmin);
+  const float mx = gmax == 0u ? -__int_as_float(0x7f800000) : fkey_inv(gmax);
+  const QRange r = qrange(qdtype);
+  if (symmetric) {
+    const float am = fmaxf(fabsf(mx), fabsf(mn));
+    *scale_out = am > 0.0f ? __fdiv_rn(am, static_cast<float>(r.hi)) : 1.0f;
+    *zp_out = 0;
+  } else {
+    // (qmax - qmin) is an i32 subtraction in the reference; it wraps for QInt32.
+    const int32_t span = static_cast<int32_t>(static_cast<uint32_t>(r.hi) - static_cast<uint32_t>(r.lo));
+    const float s = mx > mn ? __fdiv_rn(__fsub_rn(mx, mn), static_cast<float>(span)) : 1.0f;
+    const float z = __fsub_rn(static_cast<float>(r.lo), __fdiv_rn(mn, s));
+    *scale_out = s;
+    *zp_out = sat_f32_i32(roundf(z));
+  }
+}
+
 // find_scale_zp: f32::min / f32::max fold (NaN skipped), then the reference's symmetric /
 // asymmetric formulas, computed by the last block to finish.  ws = 3 x u32:
 // [min key, max key, finished-block count]; it must be zeroed/initialised before launch.
@@ -161,29 +183,69 @@ __global__ void find_scale_zp_kernel(const float* __restrict__ x, int64_t n, int
   __syncthreads();
   if (!last || threadIdx.x != 0) return;
   __threadfence();
-  const uint32_t gmin = atomicAdd(&ws[0], 0u), gmax = atomicAdd(&ws[1], 0u);
-  // An all-NaN input leaves the fold at (+inf, -inf), as the reference's fold does.
-  const float mn = gmin == 0xFFFFFFFFu ? __int_as_float(0x7f800000) : fkey_inv(gmin);
-  const float mx = gmax == 0u ? -__int_as_float(0x7f800000) : fkey_inv(gmax);
-  const QRange r = qrange(qdtype);
-  if (symmetric) {
-    const float am = fmaxf(fabsf(mx), fabsf(mn));
-    *scale_out = am > 0.0f ? __fdiv_rn(am, static_cast<float>(r.hi)) : 1.0f;
-    *zp_out = 0;
-  } else {
-    // (qmax - qmin) is an i32 subtraction in the reference; it wraps for QInt32.
-    const int32_t span = static_cast<int32_t>(static_cast<uint32_t>(r.hi) - static_cast<uint32_t>(r.lo));
-    const float s = mx > mn ? __fdiv_rn(__fsub_rn(mx, mn), static_cast<float>(span)) : 1.0f;
-    const float z = __fsub_rn(static_cast<float>(r.lo), __fdiv_rn(mn, s));
-    *scale_out = s;
-    *zp_out = sat_f32_i32(roundf(z));
-  }
+  finalize_scale_zp(atomicAdd(&ws[0], 0u), atomicAdd(&ws[1], 0u), qdtype, symmetric, scale_out,
+                    zp_out);
 }
 
 __global__ void init_minmax_ws(uint32_t* ws) {
   ws[0] = 0xFFFFFFFFu;
   ws[1] = 0u;
   ws[2] = 0u;
+}
+
+// Per-channel find_scale_zp over the rows of x [rows, cols] (channel = row, as for a
+// weight [Cout, K]).  Block b handles chunk (b % chunks) of row (b / chunks); per-row
+// partial keys and a finished-chunk count live in ws[3*row .. 3*row+2], and the last chunk
+// of a row writes that row's scale and zero point.
+__global__ void find_scale_zp_rows_kernel(const float* __restrict__ x, int64_t rows, int64_t cols,
+                                          int64_t chunk, int32_t chunks, int qdtype,
+                                          int symmetric, uint32_t* ws, float* scales,
+                                          int32_t* zps) {
+  const int64_t row = blockIdx.x / chunks;
+  const int64_t part = blockIdx.x - row * chunks;
+  if (row >= rows) return;
+  const float* xr = x + row * cols;
+  const int64_t begin = part * chunk;
+  const int64_t end = begin + chunk < cols ? begin + chunk : cols;
+  uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+  for (int64_t i = begin + threadIdx.x; i < end; i += blockDim.x) {
+    const float v = __ldg(xr + i);
+    if (v != v) continue;
+    const uint32_t k = fkey(v);
+    kmin = k < kmin ? k : kmin;
+    kmax = k > kmax ? k : kmax;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint32_t a = __shfl_xor_sync(0xFFFFFFFFu, kmin, o);
+    const uint32_t b = __shfl_xor_sync(0xFFFFFFFFu, kmax, o);
+    kmin = a < kmin ? a : kmin;
+    kmax = b > kmax ? b : kmax;
+  }
+  uint32_t* w = ws + 3 * row;
+  if ((threadIdx.x & 31) == 0) {
+    if (kmin != 0xFFFFFFFFu) atomicMin(&w[0], kmin);
+    if (kmax != 0u) atomicMax(&w[1], kmax);
+  }
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(&w[2], 1u) == static_cast<uint32_t>(chunks - 1);
+  }
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  finalize_scale_zp(atomicAdd(&w[0], 0u), atomicAdd(&w[1], 0u), qdtype, symmetric, scales + row,
+                    zps + row);
+}
+
+__global__ void init_minmax_rows(uint32_t* ws, int64_t rows) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < rows;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    ws[3 * i] = 0xFFFFFFFFu;
+    ws[3 * i + 1] = 0u;
+    ws[3 * i + 2] = 0u;
+  }
 }
 
 int grid_for(int64_t work_items, int sm_count, int block) {
@@ -306,6 +368,54 @@ lsc_status launch_find_scale_zp(const float* x, int64_t n, int qdtype, int symme
   return LSC_SUCCESS;
 }
 
+namespace {
+__global__ void fill_default_params(float* scales, int32_t* zps, int64_t rows) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < rows;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    scales[i] = 1.0f;
+    zps[i] = 0;
+  }
+}
+}  // namespace
+
+uint64_t find_scale_zp_rows_workspace(int64_t rows) {
+  return rows > 0 ? static_cast<uint64_t>(rows) * 12u : 0u;
+}
+
+lsc_status launch_find_scale_zp_rows(const float* x, int64_t rows, int64_t cols, int qdtype,
+                                     int symmetric, uint32_t* ws, uint64_t ws_bytes,
+                                     float* scales, int32_t* zps, cudaStream_t st) {
+  if (rows < 0 || cols < 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "find_scale_zp_per_channel: negative size");
+  if (rows == 0) return LSC_SUCCESS;
+  if (!scales || !zps) return set_error(LSC_ERROR_INVALID_ARGUMENT, "find_scale_zp_per_channel: null output");
+  if (cols > 0 && !x) return set_error(LSC_ERROR_INVALID_ARGUMENT, "find_scale_zp_per_channel: null input");
+  if (!valid_qdtype(qdtype))
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "find_scale_zp_per_channel: dtype %d", qdtype);
+  if (!ws || ws_bytes < find_scale_zp_rows_workspace(rows) || (reinterpret_cast<uintptr_t>(ws) & 3))
+    return set_error(LSC_ERROR_INVALID_ARGUMENT,
+                     "find_scale_zp_per_channel: needs a 4-byte aligned workspace of %llu bytes",
+                     static_cast<unsigned long long>(find_scale_zp_rows_workspace(rows)));
+  DeviceState* ds = current_device_state();
+  if (!ds) return LSC_ERROR_DEVICE_ERROR;
+  const int fill_grid = grid_for(rows, ds->sm_count, 256);
+  if (cols == 0) {
+    // QuantizationParameters::default() per channel (quantization/scheme.rs:123-127)
+    fill_default_params<<<fill_grid, 256, 0, st>>>(scales, zps, rows);
+    LSC_CUDA_TRY(cudaGetLastError());
+    return LSC_SUCCESS;
+  }
+  // Rows longer than 64 Ki elements are split so long channels still fill the GPU.
+  const int64_t chunk = cols < 65536 ? cols : 65536;
+  const int64_t chunks = (cols + chunk - 1) / chunk;
+  if (rows * chunks > INT32_MAX)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "find_scale_zp_per_channel: too many blocks");
+  init_minmax_rows<<<fill_grid, 256, 0, st>>>(ws, rows);
+  find_scale_zp_rows_kernel<<<static_cast<unsigned>(rows * chunks), 256, 0, st>>>(
+      x, rows, cols, chunk, static_cast<int32_t>(chunks), qdtype, symmetric, ws, scales, zps);
+  LSC_CUDA_TRY(cudaGetLastError());
+  return LSC_SUCCESS;
+}
+
 }  // namespace lsc
 
 using namespace lsc;
@@ -348,6 +458,19 @@ lsc_status lsc_find_scale_zp_f32(const float* x, int64_t n, int32_t qdtype, int3
                                  int32_t* zero_point_out, lsc_stream stream) {
   return launch_find_scale_zp(x, n, qdtype, symmetric, workspace, workspace_bytes, scale_out,
                               zero_point_out, static_cast<cudaStream_t>(stream));
+}
+
+uint64_t lsc_find_scale_zp_per_channel_workspace_size(int64_t channels) {
+  return find_scale_zp_rows_workspace(channels);
+}
+
+lsc_status lsc_find_scale_zp_per_channel_f32(const float* x, int64_t channels, int64_t per_channel,
+                                             int32_t qdtype, int32_t symmetric, void* workspace,
+                                             uint64_t workspace_bytes, float* scales_out,
+                                             int32_t* zero_points_out, lsc_stream stream) {
+  return launch_find_scale_zp_rows(x, channels, per_channel, qdtype, symmetric,
+                                   static_cast<uint32_t*>(workspace), workspace_bytes, scales_out,
+                                   zero_points_out, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

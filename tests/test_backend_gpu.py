@@ -234,3 +234,31 @@ def test_backend_destroyed_before_its_operators(cuda):
     gc.collect()
     del op
     gc.collect()
+
+
+@pytest.mark.parametrize("rows,cols,symmetric,qdtype", [(64, 576, 1, 9), (1000, 512, 1, 9),
+                                                        (3, 200_003, 0, 8), (7, 1, 0, 10),
+                                                        (5, 0, 1, 9)])
+def test_find_scale_zp_per_channel(cuda, rows, cols, symmetric, qdtype):
+    """find_scale_zp per output channel (weights [Cout, K]), including rows split over
+    several blocks, NaN entries, an all-zero row and empty rows."""
+    import torch
+    from lightship_b200 import _lib
+    lib = _lib.lib()
+    rng = np.random.default_rng(rows + cols)
+    x = rng.normal(0.1, 0.05, size=(rows, cols)).astype(np.float32)
+    if cols > 2:
+        x[0, 1] = np.nan
+        x[rows - 1] = 0.0
+    tx = torch.from_numpy(x).to(cuda) if x.size else torch.zeros(1, device=cuda)
+    ws_bytes = lib.lsc_find_scale_zp_per_channel_workspace_size(rows)
+    ws = torch.zeros(max(1, ws_bytes // 4), dtype=torch.int32, device=cuda)
+    s = torch.zeros(rows, dtype=torch.float32, device=cuda)
+    z = torch.zeros(rows, dtype=torch.int32, device=cuda)
+    _lib.check(lib.lsc_find_scale_zp_per_channel_f32(tx.data_ptr(), rows, cols, qdtype, symmetric,
+                                                     ws.data_ptr(), ws_bytes, s.data_ptr(), z.data_ptr(),
+                                                     torch.cuda.current_stream().cuda_stream))
+    oq = {9: orc.QINT8, 8: orc.QUINT8, 10: orc.QINT32}[qdtype]
+    want = [orc.find_scale_zp(x[r], oq, bool(symmetric)) for r in range(rows)]
+    assert s.cpu().numpy().tolist() == [np.float32(w[0]) for w in want]
+    assert z.cpu().numpy().tolist() == [w[1] for w in want]
