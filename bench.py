@@ -68,7 +68,7 @@ def load_peaks():
 
 def load_traffic():
     """dram bytes per launch of the GEMM kernel from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "gemm_i8_tn_4096.md")
+    p = os.path.join(ROOT, "profiles", "contraction_i8_gemm_4096.md")
     if not os.path.exists(p):
         return None
     with open(p) as f:
