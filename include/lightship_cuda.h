@@ -292,6 +292,19 @@ lsc_status lsc_find_scale_zp_per_channel_f32(const float* x, int64_t channels, i
                                              int32_t qdtype, int32_t symmetric, void* workspace,
                                              uint64_t workspace_bytes, float* scales_out,
                                              int32_t* zero_points_out, lsc_stream stream);
+/* No counterpart in the reference.  lsc_find_scale_zp_per_channel_f32 for callers that
+ * cannot allocate device memory -- code running inside a host runtime that owns the GPU's
+ * memory (a framework's caching allocator, a serving process with a fixed budget), where a
+ * cudaMalloc would synchronise the device and fail once the owner holds the memory.  It
+ * takes no workspace and allocates nothing: its scratch is a static device array sized for
+ * at most 16384 channels (192 KiB, held on every GPU that loads the library until exit);
+ * more channels are rejected with LSC_ERROR_INVALID_ARGUMENT.  The first call on a device
+ * looks up that array's address, so make it before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race with each other; sequential calls do not. */
+lsc_status lsc_find_scale_zp_per_channel_f32_noalloc(const float* x, int64_t channels,
+                                                     int64_t per_channel, int32_t qdtype,
+                                                     int32_t symmetric, float* scales_out,
+                                                     int32_t* zero_points_out, lsc_stream stream);
 
 #ifdef __cplusplus
 }

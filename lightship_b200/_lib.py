@@ -115,6 +115,7 @@ SIGNATURES = {
     "lsc_find_scale_zp_f32": (ST, [P, I64, I32, I32, P, C.c_uint64, P, P, P]),
     "lsc_find_scale_zp_per_channel_workspace_size": (C.c_uint64, [I64]),
     "lsc_find_scale_zp_per_channel_f32": (ST, [P, I64, I64, I32, I32, P, C.c_uint64, P, P, P]),
+    "lsc_find_scale_zp_per_channel_f32_noalloc": (ST, [P, I64, I64, I32, I32, P, P, P]),
 }
 
 _lib = None

@@ -5,6 +5,8 @@
 // Per-tensor (quantize_tensor / dequantize_tensor, helpers.rs:11-94) and per-channel
 // (QuantizationParameters per-channel, quantization/scheme.rs:58-121) forms.
 // Loads and stores are 16-byte vectors; grids are a multiple of the SM count.
+#include <mutex>
+
 #include "lsc_internal.h"
 #include "sm100.cuh"
 
@@ -462,6 +464,71 @@ lsc_status lsc_find_scale_zp_f32(const float* x, int64_t n, int32_t qdtype, int3
 
 uint64_t lsc_find_scale_zp_per_channel_workspace_size(int64_t channels) {
   return find_scale_zp_rows_workspace(channels);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Per-channel find_scale_zp for callers that cannot allocate device memory.
+//
+// Some callers run inside a host runtime that owns all device memory -- a framework whose
+// caching allocator has reserved the GPU, or a serving process with a fixed memory budget
+// -- and must not call cudaMalloc: it synchronises the device and fails once the owner
+// holds the memory.  This variant needs no caller workspace.  Its scratch is a file-scope
+// device array of kNoAllocMaxChannels * 12 bytes (192 KiB), which every GPU that loads
+// this library holds until the process exits.
+namespace {
+constexpr int64_t kNoAllocMaxChannels = 16384;
+static __device__ __align__(256) uint32_t g_fsz_noalloc_scratch[3 * kNoAllocMaxChannels];
+
+std::mutex g_noalloc_mu;
+uint32_t* g_noalloc_ptr[64] = {};
+
+// Device address of the scratch array for the current device.  The host-side name of a
+// __device__ array is not a device address, so the address is queried once per device,
+// with that device current, and cached.
+lsc_status noalloc_scratch(uint32_t** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return set_error(LSC_ERROR_INVALID_ARGUMENT, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_fsz_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(find_scale_zp scratch)");
+    g_noalloc_ptr[dev] = static_cast<uint32_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return LSC_SUCCESS;
+}
+}  // namespace
+
+extern "C" {
+
+// Same results as lsc_find_scale_zp_per_channel_f32, with the library's own static scratch
+// in place of the caller's workspace.  The first call on a device looks up the scratch
+// address (make it before any stream capture).  Every call shares the one array: calls
+// that overlap on the GPU (e.g. on two streams) race; each call re-initialises the part it
+// uses, so back-to-back calls are independent.
+lsc_status lsc_find_scale_zp_per_channel_f32_noalloc(const float* x, int64_t channels,
+                                                     int64_t per_channel, int32_t qdtype,
+                                                     int32_t symmetric, float* scales_out,
+                                                     int32_t* zero_points_out, lsc_stream stream) {
+  if (channels > kNoAllocMaxChannels)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT,
+                     "find_scale_zp_per_channel_noalloc: %lld channels exceed the static scratch "
+                     "limit of %lld; use lsc_find_scale_zp_per_channel_f32 with a workspace",
+                     static_cast<long long>(channels), static_cast<long long>(kNoAllocMaxChannels));
+  if (channels <= 0) return launch_find_scale_zp_rows(x, channels, per_channel, qdtype, symmetric,
+                                                      nullptr, 0, scales_out, zero_points_out,
+                                                      static_cast<cudaStream_t>(stream));
+  uint32_t* ws = nullptr;
+  lsc_status st = noalloc_scratch(&ws);
+  if (st) return st;
+  return launch_find_scale_zp_rows(x, channels, per_channel, qdtype, symmetric, ws,
+                                   sizeof(g_fsz_noalloc_scratch), scales_out, zero_points_out,
+                                   static_cast<cudaStream_t>(stream));
 }
 
 lsc_status lsc_find_scale_zp_per_channel_f32(const float* x, int64_t channels, int64_t per_channel,
