@@ -16,7 +16,9 @@ namespace lsc {
 
 uint32_t supported_ops_mask() {
   return (1u << LSC_OP_QGEMM) | (1u << LSC_OP_FULLY_CONNECTED) | (1u << LSC_OP_QUANTIZE) |
-         (1u << LSC_OP_DEQUANTIZE);
+         (1u << LSC_OP_DEQUANTIZE) | (1u << LSC_OP_CONV2D) | (1u << LSC_OP_MATMUL) |
+         (1u << LSC_OP_BATCHNORM) | (1u << LSC_OP_RELU) | (1u << LSC_OP_RELU6) |
+         (1u << LSC_OP_SILU);
 }
 
 namespace {
@@ -287,7 +289,21 @@ lsc_status compile_op(lsc_backend* be, lsc_op* op, const lsc_tensor* in, int n_i
       return compile_qgemm(op, in, n_in, out, n_out, false);
     case LSC_OP_FULLY_CONNECTED:
       if (n_in >= 1 && is_int8(in[0].dtype)) return compile_qgemm(op, in, n_in, out, n_out, true);
+      if (n_in >= 1 && in[0].dtype == LSC_DTYPE_F32) return compile_fc_f32(op, in, n_in, n_out);
       break;
+    case LSC_OP_CONV2D:
+      if (n_in >= 1 && (is_int8(in[0].dtype) || in[0].dtype == LSC_DTYPE_F32))
+        return compile_conv(op, in, n_in, out, n_out);
+      break;
+    case LSC_OP_MATMUL:
+      if (n_in >= 1 && in[0].dtype == LSC_DTYPE_F32) return compile_matmul_f32(op, in, n_in, n_out);
+      break;
+    case LSC_OP_BATCHNORM:
+      if (n_in >= 1 && in[0].dtype == LSC_DTYPE_F32) return compile_batchnorm(op, in, n_in, n_out);
+      break;
+    case LSC_OP_RELU: return compile_activation(op, in, n_in, n_out, LSC_ACT_RELU);
+    case LSC_OP_RELU6: return compile_activation(op, in, n_in, n_out, LSC_ACT_RELU6);
+    case LSC_OP_SILU: return compile_activation(op, in, n_in, n_out, LSC_ACT_SILU);
     case LSC_OP_QUANTIZE: {
       if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Quantize needs 1 input and 1 output");
       if (in[0].dtype != LSC_DTYPE_F32)
@@ -322,6 +338,12 @@ lsc_status execute_op(lsc_backend* be, const lsc_op* op, const lsc_tensor* in, i
     case OpKind::kQGemm: return execute_qgemm(op, in, n_in, out, n_out, s);
     case OpKind::kQuantize: return execute_quant(op, in, n_in, out, n_out, s, true);
     case OpKind::kDequantize: return execute_quant(op, in, n_in, out, n_out, s, false);
+    case OpKind::kConvF32:
+    case OpKind::kConvI8: return execute_conv(op, in, n_in, out, n_out, s);
+    case OpKind::kMatMulF32: return execute_matmul_f32(op, in, n_in, out, n_out, s);
+    case OpKind::kFcF32: return execute_fc_f32(op, in, n_in, out, n_out, s);
+    case OpKind::kBatchNormF32: return execute_batchnorm(op, in, n_in, out, n_out, s);
+    case OpKind::kActF32: return execute_activation(op, in, n_in, out, n_out, s);
     default: break;
   }
   return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "compiled operator kind %d not executable", static_cast<int>(op->kind));

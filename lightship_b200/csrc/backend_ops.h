@@ -109,6 +109,23 @@ struct Staging {
   lsc_status finish(lsc_status st_in);
 };
 
+// backend_conv.cpp
+lsc_status compile_conv(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_tensor* out, int n_out);
+lsc_status execute_conv(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out,
+                        Staging& s);
+lsc_status compile_matmul_f32(lsc_op* op, const lsc_tensor* in, int n_in, int n_out);
+lsc_status execute_matmul_f32(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out,
+                              int n_out, Staging& s);
+lsc_status compile_fc_f32(lsc_op* op, const lsc_tensor* in, int n_in, int n_out);
+lsc_status execute_fc_f32(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out,
+                          int n_out, Staging& s);
+lsc_status compile_batchnorm(lsc_op* op, const lsc_tensor* in, int n_in, int n_out);
+lsc_status execute_batchnorm(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out,
+                             int n_out, Staging& s);
+lsc_status compile_activation(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, int act);
+lsc_status execute_activation(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out,
+                              int n_out, Staging& s);
+
 lsc_status compile_op(lsc_backend* be, lsc_op* op, const lsc_tensor* in, int n_in,
                       const lsc_tensor* out, int n_out);
 lsc_status execute_op(lsc_backend* be, const lsc_op* op, const lsc_tensor* in, int n_in,

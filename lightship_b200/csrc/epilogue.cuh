@@ -17,8 +17,11 @@ namespace lsc {
 
 __device__ __forceinline__ float act_relu(float x) { return x > 0.0f ? x : 0.0f; }
 
-// Rust f32::clamp(0, 6): NaN and -0.0 pass through unchanged.
+// Rust f32::clamp(0, 6): NaN (with its payload) and -0.0 pass through unchanged.  The NaN
+// test comes first so the compiler cannot lower the clamp to min/max instructions, which
+// return the canonical NaN.
 __device__ __forceinline__ float act_relu6(float x) {
+  if (x != x) return x;
   float r = x;
   if (r < 0.0f) r = 0.0f;
   if (r > 6.0f) r = 6.0f;

@@ -73,6 +73,32 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
                           int rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
                           int64_t ldo, cudaStream_t stream);
 
+// FP32 contractions as split-TF32 (contraction_tf32.cu).  GEMM: A [M,K] and B [N,K] K-major
+// (hi and lo parts; lo unused when split == false), K a multiple of 4, output row-major with
+// stride ldo.  Convolution: NHWC hi/lo input with g.c stored channels (multiple of 4),
+// weights [Cout, KH*KW*C], output NCHW.
+lsc_status launch_gemm_tf32(const float* a_hi, const float* a_lo, const float* b_hi,
+                            const float* b_lo, int64_t m, int64_t n, int64_t k,
+                            const float* bias, int act, float* out, int64_t ldo, bool split,
+                            cudaStream_t stream);
+lsc_status launch_conv_tf32(const float* x_hi, const float* x_lo, const float* w_hi,
+                            const float* w_lo, const ConvGeometry& g, const float* bias, int act,
+                            float* out_nchw, bool split, cudaStream_t stream);
+// Operand preparation (tf32_prep.cu): split into hi/lo parts with padding / transposition.
+lsc_status prep_split_rows(const float* x, int64_t rows, int64_t cols, int64_t ld, float* hi,
+                           float* lo, cudaStream_t st);
+lsc_status prep_split_transpose(const float* x, int64_t k, int64_t n, int64_t ldk, float* hi,
+                                float* lo, cudaStream_t st);
+lsc_status prep_split_nchw_to_nhwc(const float* x, int64_t n, int64_t c, int64_t hw, int64_t cp,
+                                   float* hi, float* lo, cudaStream_t st);
+// Elementwise FP32 operators (elementwise.cu).
+lsc_status launch_batchnorm_f32(const float* x, float* y, int64_t n, int64_t c, int64_t spatial,
+                                const float* gamma, const float* beta, const float* mean,
+                                const float* inv_std, int act, cudaStream_t st);
+lsc_status launch_activation_f32(const float* x, float* y, int64_t n, int act, cudaStream_t st);
+lsc_status launch_add_f32(const float* a, const float* b, float* y, int64_t n, int act,
+                          cudaStream_t st);
+
 // Quantization kernels (quant.cu).  `scales` == nullptr selects the per-tensor form with
 // scale0/zp0; otherwise channel c = (i / inner) % channels.
 lsc_status launch_quantize(const float* x, void* out, int64_t n, int qdtype, const float* scales,
