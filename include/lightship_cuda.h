@@ -87,7 +87,9 @@ typedef enum lsc_op_type {
   LSC_OP_SILU = 6,
   LSC_OP_QUANTIZE = 7,   /* quantize_tensor (quantization/helpers.rs:11-50) */
   LSC_OP_DEQUANTIZE = 8, /* dequantize_tensor (quantization/helpers.rs:53-94) */
-  LSC_OP_QGEMM = 9       /* quantized_gemm_int8 + requant/dequant (cpu/quantized_ops.rs:13-48) */
+  LSC_OP_QGEMM = 9,      /* quantized_gemm_int8 + requant/dequant (cpu/quantized_ops.rs:13-48) */
+  LSC_OP_MAXPOOL2D = 10, /* MaxPool2d on int8 NHWC (operator/pooling.rs:383-455) */
+  LSC_OP_GLOBAL_AVGPOOL2D = 11 /* GlobalAvgPool2d on int8 NHWC (operator/pooling.rs:457-530) */
 } lsc_op_type;
 
 /* FusionType (ir/fusion.rs:8-23); LSC_FUSION_NONE = no FusionInfo */
@@ -176,9 +178,11 @@ typedef struct lsc_op_desc {
   int32_t activation;  /* extra epilogue activation, LSC_ACT_* */
   int32_t rounding;    /* LSC_ROUND_*, -1 = backend default */
   int32_t fp32_mode;   /* LSC_FP32_*, -1 = backend default */
-  float bn_epsilon;    /* BatchNorm epsilon (operator/batchnorm.rs:49 default 1e-5) */
+  float bn_epsilon;    /* BatchNorm epsilon; 0 selects the reference default 1e-5
+                          (operator/batchnorm.rs:49) */
   float output_scale;  /* s_out of a requantized int8 output */
   int32_t output_dtype; /* dtype of outputs[0] for QGEMM / quantized Conv2d */
+  int32_t kernel_h, kernel_w; /* pooling window (Pool2dConfig, operator/pooling.rs) */
 } lsc_op_desc;
 
 /* Backend::allocate result (backend/memory.rs:32-45) */
@@ -246,13 +250,16 @@ lsc_status lsc_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n, i
  *   x [N, H, W, C] int8 with C a multiple of 16 (pad channels with zeros),
  *   w [Cout, KH, KW, C] int8 (K ordered kh, kw, c), scale [Cout], bias [Cout] or NULL,
  *   outputs NHWC [N, OH, OW, Cout] with OH = (H + 2 ph - dh (KH-1) - 1) / sh + 1 (same for W).
+ * `residual` (optional) is an int8 NHWC tensor shaped like the outputs, added before the
+ * activation as (f32)r * residual_scale -- a ResNet block's Add+ReLU (FusionType::AddReLU,
+ * ir/fusion.rs:20) fused into the second convolution.
  * Limits of the im2col load unit: stride <= 8, padding <= 127. */
 lsc_status lsc_conv2d_i8_nhwc(const int8_t* x, const int8_t* w, int64_t n, int64_t h, int64_t wd,
                               int64_t c, int64_t c_out, int64_t kh, int64_t kw, int64_t sh,
                               int64_t sw, int64_t ph, int64_t pw, int64_t dh, int64_t dw,
                               const int32_t* bias, const float* scale, float s_out, int32_t act,
                               int32_t rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
-                              lsc_stream stream);
+                              const int8_t* residual, float residual_scale, lsc_stream stream);
 
 /* quantize_tensor, per-tensor (quantization/helpers.rs:11-50 with quantize_value :139-155):
  *   q = clamp(sat_i32(R(x / scale)) + zero_point, qmin, qmax)   (i32 add wraps)

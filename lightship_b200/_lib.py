@@ -70,7 +70,8 @@ class lsc_op_desc(C.Structure):
                 ("stride_w", C.c_int32), ("pad_h", C.c_int32), ("pad_w", C.c_int32),
                 ("dilation_h", C.c_int32), ("dilation_w", C.c_int32), ("groups", C.c_int32),
                 ("activation", C.c_int32), ("rounding", C.c_int32), ("fp32_mode", C.c_int32),
-                ("bn_epsilon", C.c_float), ("output_scale", C.c_float), ("output_dtype", C.c_int32)]
+                ("bn_epsilon", C.c_float), ("output_scale", C.c_float), ("output_dtype", C.c_int32),
+                ("kernel_h", C.c_int32), ("kernel_w", C.c_int32)]
 
 
 class lsc_memory_block(C.Structure):
@@ -106,7 +107,7 @@ SIGNATURES = {
     "lsc_memcpy_d2h": (ST, [P, P, C.c_uint64, P]),
     "lsc_check_device": (ST, [C.POINTER(C.c_uint32)]),
     "lsc_gemm_i8": (ST, [P, P, I64, I64, I64, P, P, F32, I32, I32, P, P, P, P]),
-    "lsc_conv2d_i8_nhwc": (ST, [P, P] + [I64] * 13 + [P, P, F32, I32, I32, P, P, P, P]),
+    "lsc_conv2d_i8_nhwc": (ST, [P, P] + [I64] * 13 + [P, P, F32, I32, I32, P, P, P, P, F32, P]),
     "lsc_quantize_f32": (ST, [P, P, I64, I32, F32, I32, I32, P]),
     "lsc_quantize_f32_per_channel": (ST, [P, P, I64, I32, P, P, I32, I64, I32, P]),
     "lsc_dequantize": (ST, [P, I32, P, I64, F32, I32, P]),

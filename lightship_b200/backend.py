@@ -67,6 +67,8 @@ class OperatorType(enum.IntEnum):
     Quantize = 7
     Dequantize = 8
     QGemm = 9
+    MaxPool2d = 10
+    GlobalAvgPool2d = 11
 
 
 class FusionType(enum.IntEnum):
@@ -124,6 +126,7 @@ class OperatorDef:
     fp32_mode: Optional[int] = None
     epsilon: float = 1e-5
     output_scale: float = 0.0
+    kernel: tuple = (1, 1)
 
 
 @dataclass
@@ -292,6 +295,7 @@ class CudaBackend:
         d.bn_epsilon = op_def.epsilon
         d.output_scale = op_def.output_scale
         d.output_dtype = int(outputs[0].data_type) if outputs else -1
+        d.kernel_h, d.kernel_w = op_def.kernel
         keep: list = []
         cin = (_lib.lsc_tensor * max(1, len(inputs)))(*[t._to_c(keep) for t in inputs])
         cout = (_lib.lsc_tensor * max(1, len(outputs)))(*[t._to_c(keep) for t in outputs])

@@ -289,17 +289,99 @@ lsc_status execute_conv(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_te
   int8_t* o_i8 = nullptr;
   float* o_f32 = nullptr;
   int32_t* o_i32 = nullptr;
+  float s_out = op->s_out;
   const int64_t m = g.n * g.oh * g.ow;
   for (int i = 0; i < n_out; ++i) {
     void* dptr = nullptr;
     if ((st = s.output(out[i], m * g.c_out * dtype_size(out[i].dtype), &dptr))) return st;
-    if (is_int8(out[i].dtype)) o_i8 = static_cast<int8_t*>(dptr);
-    else if (out[i].dtype == LSC_DTYPE_F32) o_f32 = static_cast<float*>(dptr);
-    else o_i32 = static_cast<int32_t*>(dptr);
+    if (is_int8(out[i].dtype)) {
+      o_i8 = static_cast<int8_t*>(dptr);
+      // a calibrated output scale carried by the output tensor overrides the compiled one
+      if (out[i].quant.count > 0 && out[i].quant.scale && out[i].quant.scale[0] > 0.0f)
+        s_out = out[i].quant.scale[0];
+    } else if (out[i].dtype == LSC_DTYPE_F32) {
+      o_f32 = static_cast<float*>(dptr);
+    } else {
+      o_i32 = static_cast<int32_t*>(dptr);
+    }
     set_shape(out[i], {g.n, g.oh, g.ow, g.c_out});
   }
+  // optional residual (execute-time input 1): int8 NHWC shaped like the output, added before
+  // the activation -- a BasicBlock's Add+ReLU fused into its second convolution
+  const void* rd = nullptr;
+  float r_scale = 1.0f;
+  if (n_in >= 2 && in[1].data) {
+    const lsc_tensor& r = in[1];
+    if (!is_int8(r.dtype)) return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "Conv2d residual must be int8");
+    if (numel(r) != m * g.c_out)
+      return set_error(LSC_ERROR_SHAPE_MISMATCH, "Conv2d residual '%s' must match the output shape", tname(r));
+    if ((st = s.input(r, m * g.c_out, &rd))) return st;
+    r_scale = r.quant.count > 0 && r.quant.scale ? r.quant.scale[0] : 1.0f;
+  }
   return launch_conv_i8(static_cast<const int8_t*>(xd), static_cast<const int8_t*>(op->w), g, op->bias_i32,
-                        op->scale, op->s_out, op->act, op->rounding, o_i8, o_f32, o_i32, s.st);
+                        op->scale, s_out, op->act, op->rounding, o_i8, o_f32, o_i32,
+                        static_cast<const int8_t*>(rd), r_scale, s.st);
+}
+
+// ------------------------------------------------------------------------------ pooling (INT8 NHWC)
+lsc_status compile_pool(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, bool global) {
+  if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Missing input or output");
+  if (!is_int8(in[0].dtype))
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "pooling on the CUDA backend takes int8 NHWC input");
+  const lsc_op_desc& d = op->desc;
+  op->kind = global ? OpKind::kAvgPoolI8 : OpKind::kMaxPoolI8;
+  op->kh = d.kernel_h > 0 ? d.kernel_h : 1;
+  op->kw = d.kernel_w > 0 ? d.kernel_w : 1;
+  if (!global && (d.pad_h < 0 || d.pad_w < 0 || d.pad_h >= op->kh || d.pad_w >= op->kw))
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "MaxPool2d: padding must be smaller than the window");
+  op->sh = d.stride_h > 0 ? d.stride_h : 1;
+  op->sw = d.stride_w > 0 ? d.stride_w : 1;
+  op->ph = d.pad_h;
+  op->pw = d.pad_w;
+  op->s_out = d.output_scale;
+  return LSC_SUCCESS;
+}
+
+lsc_status execute_pool(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out,
+                        int n_out, Staging& s) {
+  if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Missing input or output");
+  const lsc_tensor& x = in[0];
+  if (!is_int8(x.dtype) || x.ndim != 4)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "pooling takes a 4D int8 NHWC input");
+  const int64_t n = x.shape[0], h = x.shape[1], w = x.shape[2], c = x.shape[3];
+  const void* xd = nullptr;
+  lsc_status st = s.input(x, n * h * w * c, &xd);
+  if (st) return st;
+  if (op->kind == OpKind::kMaxPoolI8) {
+    const int64_t oh = (h + 2 * op->ph - op->kh) / op->sh + 1, ow = (w + 2 * op->pw - op->kw) / op->sw + 1;
+    if (oh <= 0 || ow <= 0) return set_error(LSC_ERROR_SHAPE_MISMATCH, "MaxPool2d: window larger than the input");
+    void* yd = nullptr;
+    if ((st = s.output(out[0], n * oh * ow * c, &yd))) return st;
+    set_shape(out[0], {n, oh, ow, c});
+    return launch_maxpool_i8(static_cast<const int8_t*>(xd), static_cast<int8_t*>(yd), n, h, w, c, oh, ow,
+                             static_cast<int>(op->kh), static_cast<int>(op->kw), op->sh, op->sw, op->ph, op->pw, s.st);
+  }
+  const float s_in = x.quant.count > 0 && x.quant.scale ? x.quant.scale[0] : 1.0f;
+  int8_t* o_i8 = nullptr;
+  float* o_f32 = nullptr;
+  float s_out = op->s_out;
+  for (int i = 0; i < n_out; ++i) {
+    void* yd = nullptr;
+    if ((st = s.output(out[i], n * c * dtype_size(out[i].dtype), &yd))) return st;
+    set_shape(out[i], {n, c});
+    if (out[i].dtype == LSC_DTYPE_F32) {
+      o_f32 = static_cast<float*>(yd);
+    } else if (is_int8(out[i].dtype)) {
+      o_i8 = static_cast<int8_t*>(yd);
+      if (out[i].quant.count > 0 && out[i].quant.scale && out[i].quant.scale[0] > 0.0f)
+        s_out = out[i].quant.scale[0];
+      if (!(s_out > 0.0f))
+        return set_error(LSC_ERROR_INVALID_ARGUMENT, "GlobalAvgPool2d: int8 output needs an output scale");
+    } else {
+      return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "GlobalAvgPool2d output must be f32 or int8");
+    }
+  }
+  return launch_avgpool_i8(static_cast<const int8_t*>(xd), n, h * w, c, s_in, s_out, op->rounding, o_i8, o_f32, s.st);
 }
 
 // ------------------------------------------------------------------------------ MatMul / FC

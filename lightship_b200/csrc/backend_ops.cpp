@@ -18,7 +18,7 @@ uint32_t supported_ops_mask() {
   return (1u << LSC_OP_QGEMM) | (1u << LSC_OP_FULLY_CONNECTED) | (1u << LSC_OP_QUANTIZE) |
          (1u << LSC_OP_DEQUANTIZE) | (1u << LSC_OP_CONV2D) | (1u << LSC_OP_MATMUL) |
          (1u << LSC_OP_BATCHNORM) | (1u << LSC_OP_RELU) | (1u << LSC_OP_RELU6) |
-         (1u << LSC_OP_SILU);
+         (1u << LSC_OP_SILU) | (1u << LSC_OP_MAXPOOL2D) | (1u << LSC_OP_GLOBAL_AVGPOOL2D);
 }
 
 namespace {
@@ -143,11 +143,19 @@ lsc_status compile_qgemm(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_t
   op->scale = static_cast<float*>(p);
   if (n_in >= 3 && in[2].data) {
     const lsc_tensor& b = in[2];
-    if (b.dtype != LSC_DTYPE_I32 && b.dtype != LSC_DTYPE_QINT32)
-      return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "bias '%s' must be int32", tname(b));
+    if (b.dtype != LSC_DTYPE_I32 && b.dtype != LSC_DTYPE_QINT32 && b.dtype != LSC_DTYPE_F32)
+      return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "bias '%s' must be int32 or f32", tname(b));
     if (numel(b) != n) return set_error(LSC_ERROR_SHAPE_MISMATCH, "bias '%s' must have %lld entries", tname(b), (long long)n);
     if ((st = read_tensor_bytes(b, n * 4, raw))) return st;
-    if ((st = own_upload(op, raw.data(), n * 4, &p))) return st;
+    if (b.dtype == LSC_DTYPE_F32) {
+      // f32 bias -> int32 in accumulator units: quantize_value(b, s_a * s_w[n], 0, QInt32)
+      const float* bf = reinterpret_cast<const float*>(raw.data());
+      std::vector<int32_t> bi(static_cast<size_t>(n));
+      for (int64_t i = 0; i < n; ++i) bi[i] = sat_i32(roundf(bf[i] / scale[i]));
+      if ((st = own_upload(op, bi.data(), n * 4, &p))) return st;
+    } else if ((st = own_upload(op, raw.data(), n * 4, &p))) {
+      return st;
+    }
     op->bias_i32 = static_cast<int32_t*>(p);
   }
   for (int i = 0; i < n_out; ++i) {
@@ -263,6 +271,16 @@ lsc_status execute_quant(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_t
   void* yd = nullptr;
   lsc_status st = s.input(x, n * dtype_size(in_dt), &xd);
   if (st) return st;
+  if (quantize && op->kp > 0) {
+    // f32 NCHW -> int8 NHWC with the channels padded to op->kp (a quantized CNN's input)
+    if (x.ndim != 4) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Quantize to NHWC needs a 4D NCHW input");
+    const int64_t nb = x.shape[0], c = x.shape[1], hw = x.shape[2] * x.shape[3];
+    if (c > op->kp) return set_error(LSC_ERROR_SHAPE_MISMATCH, "Quantize to NHWC: %lld channels exceed %lld", (long long)c, (long long)op->kp);
+    if ((st = s.output(y, nb * hw * op->kp, &yd))) return st;
+    set_shape(y, {nb, x.shape[2], x.shape[3], op->kp});
+    return launch_quantize_nchw_to_nhwc_i8(static_cast<const float*>(xd), static_cast<int8_t*>(yd), nb, c, hw,
+                                           op->kp, op->q_scale0, op->rounding, s.st);
+  }
   if ((st = s.output(y, n * dtype_size(out_dt), &yd))) return st;
   y.ndim = x.ndim;
   for (int i = 0; i < x.ndim; ++i) y.shape[i] = x.shape[i];
@@ -301,6 +319,8 @@ lsc_status compile_op(lsc_backend* be, lsc_op* op, const lsc_tensor* in, int n_i
     case LSC_OP_BATCHNORM:
       if (n_in >= 1 && in[0].dtype == LSC_DTYPE_F32) return compile_batchnorm(op, in, n_in, n_out);
       break;
+    case LSC_OP_MAXPOOL2D: return compile_pool(op, in, n_in, n_out, false);
+    case LSC_OP_GLOBAL_AVGPOOL2D: return compile_pool(op, in, n_in, n_out, true);
     case LSC_OP_RELU: return compile_activation(op, in, n_in, n_out, LSC_ACT_RELU);
     case LSC_OP_RELU6: return compile_activation(op, in, n_in, n_out, LSC_ACT_RELU6);
     case LSC_OP_SILU: return compile_activation(op, in, n_in, n_out, LSC_ACT_SILU);
@@ -313,6 +333,15 @@ lsc_status compile_op(lsc_backend* be, lsc_op* op, const lsc_tensor* in, int n_i
       if (dtype_size(op->qdtype) == 0 || op->qdtype == LSC_DTYPE_F32 || op->qdtype == LSC_DTYPE_F16 ||
           op->qdtype == LSC_DTYPE_F64 || op->qdtype == LSC_DTYPE_I16 || op->qdtype == LSC_DTYPE_I64)
         return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "Quantize: output dtype %d", op->qdtype);
+      op->kp = 0;
+      if (in[0].ndim == 4 && in[0].layout != LSC_LAYOUT_NHWC && out[0].layout == LSC_LAYOUT_NHWC) {
+        // relayout to NHWC int8; the output's declared shape gives the stored channel count
+        if (!is_int8(op->qdtype) || out[0].ndim != 4 || out[0].quant.count > 1)
+          return set_error(LSC_ERROR_UNSUPPORTED_LAYOUT, "Quantize to NHWC: per-tensor int8 output [N,H,W,C] only");
+        op->kp = out[0].shape[3];
+        if (op->kp % 16 != 0)
+          return set_error(LSC_ERROR_INVALID_ARGUMENT, "Quantize to NHWC: stored channels must be a multiple of 16");
+      }
       return take_qparams(op, out[0]);
     }
     case LSC_OP_DEQUANTIZE: {
@@ -344,6 +373,8 @@ lsc_status execute_op(lsc_backend* be, const lsc_op* op, const lsc_tensor* in, i
     case OpKind::kFcF32: return execute_fc_f32(op, in, n_in, out, n_out, s);
     case OpKind::kBatchNormF32: return execute_batchnorm(op, in, n_in, out, n_out, s);
     case OpKind::kActF32: return execute_activation(op, in, n_in, out, n_out, s);
+    case OpKind::kMaxPoolI8:
+    case OpKind::kAvgPoolI8: return execute_pool(op, in, n_in, out, n_out, s);
     default: break;
   }
   return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "compiled operator kind %d not executable", static_cast<int>(op->kind));

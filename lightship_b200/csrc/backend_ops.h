@@ -33,6 +33,8 @@ enum class OpKind {
   kConvF32,        // NCHW convolution (+ folded BN, bias, activation)
   kBatchNormF32,   // per-channel affine (+ ReLU)
   kActF32,         // ReLU / ReLU6 / SiLU
+  kMaxPoolI8,      // MaxPool2d on int8 NHWC
+  kAvgPoolI8,      // GlobalAvgPool2d on int8 NHWC
 };
 
 struct lsc_op {
@@ -122,6 +124,9 @@ lsc_status execute_fc_f32(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_
 lsc_status compile_batchnorm(lsc_op* op, const lsc_tensor* in, int n_in, int n_out);
 lsc_status execute_batchnorm(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out,
                              int n_out, Staging& s);
+lsc_status compile_pool(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, bool global);
+lsc_status execute_pool(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out,
+                        Staging& s);
 lsc_status compile_activation(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, int act);
 lsc_status execute_activation(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out,
                               int n_out, Staging& s);

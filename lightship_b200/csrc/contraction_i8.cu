@@ -42,6 +42,10 @@ struct I8Params {
   int64_t ldo;
   int32_t vec_ok;  // 16-byte vector stores are legal for full column chunks
   uint32_t* err;
+  // optional int8 residual added before the activation (same layout as the outputs):
+  // y = dequant(acc) + (f32)r * res_scale
+  const int8_t* residual;
+  float res_scale;
   // convolution (ACB > 0)
   int32_t ow, ohw;           // output width, OH*OW
   int32_t sw, sh, pw, ph;    // stride / padding
@@ -76,6 +80,7 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
                                                int row, int col0) {
   if (row >= p.m) return;
   const bool full = (col0 + 32 <= p.n);
+  const int64_t base = static_cast<int64_t>(row) * p.ldo + col0;
   int32_t acc[32];
   float y[32];
   if (full) {
@@ -88,10 +93,10 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
       acc[j + 1] = static_cast<int32_t>(r[j + 1] + static_cast<uint32_t>(b.y));
       acc[j + 2] = static_cast<int32_t>(r[j + 2] + static_cast<uint32_t>(b.z));
       acc[j + 3] = static_cast<int32_t>(r[j + 3] + static_cast<uint32_t>(b.w));
-      y[j + 0] = apply_act<ACT>(dequant(acc[j + 0], s.x));
-      y[j + 1] = apply_act<ACT>(dequant(acc[j + 1], s.y));
-      y[j + 2] = apply_act<ACT>(dequant(acc[j + 2], s.z));
-      y[j + 3] = apply_act<ACT>(dequant(acc[j + 3], s.w));
+      y[j + 0] = dequant(acc[j + 0], s.x);
+      y[j + 1] = dequant(acc[j + 1], s.y);
+      y[j + 2] = dequant(acc[j + 2], s.z);
+      y[j + 3] = dequant(acc[j + 3], s.w);
     }
   } else {
 #pragma unroll
@@ -100,14 +105,32 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
       if (c < p.n) {
         const int32_t b = p.bias ? __ldg(p.bias + c) : 0;
         acc[j] = static_cast<int32_t>(r[j] + static_cast<uint32_t>(b));
-        y[j] = apply_act<ACT>(dequant(acc[j], __ldg(p.scale + c)));
+        y[j] = dequant(acc[j], __ldg(p.scale + c));
       } else {
         acc[j] = 0;
         y[j] = 0.0f;
       }
     }
   }
-  const int64_t base = static_cast<int64_t>(row) * p.ldo + col0;
+  if (p.residual) {
+    if (full && p.vec_ok) {
+      const uint4 r0 = __ldg(reinterpret_cast<const uint4*>(p.residual + base));
+      const uint4 r1 = __ldg(reinterpret_cast<const uint4*>(p.residual + base) + 1);
+      const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int32_t q = static_cast<int8_t>((rw[j >> 2] >> (8 * (j & 3))) & 0xFFu);
+        y[j] = __fadd_rn(y[j], __fmul_rn(__int2float_rn(q), p.res_scale));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.n)
+          y[j] = __fadd_rn(y[j], __fmul_rn(__int2float_rn(p.residual[base + j]), p.res_scale));
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) y[j] = apply_act<ACT>(y[j]);
   if (full && p.vec_ok) {
     if (p.out_i8) {
       uint32_t pk[8];
@@ -493,7 +516,7 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
 lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& g,
                           const int32_t* bias, const float* scale, float s_out, int act,
                           int rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
-                          cudaStream_t stream) {
+                          const int8_t* residual, float res_scale, cudaStream_t stream) {
   const int64_t m = g.n * g.oh * g.ow;
   lsc_status st = check_common(m, g.c_out, act, rounding, scale, out_i8, out_f32, out_i32, "conv_i8");
   if (st) return st;
@@ -563,6 +586,9 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
   p.chunks_per_tap = static_cast<int32_t>(g.c / acb);
   p.total_chunks = static_cast<int32_t>(total_chunks);
   fill_outputs(p, bias, scale, s_out, rounding, out_i8, out_f32, out_i32, g.c_out, ds->err_word);
+  p.residual = residual;
+  p.res_scale = res_scale;
+  if (reinterpret_cast<uintptr_t>(residual) & 15) p.vec_ok = 0;
   switch (acb) {
     case 128: return launch_bn<128>(bn, ta, tw, p, act, ds->sm_count, stream);
     case 64: return launch_bn<64>(bn, ta, tw, p, act, ds->sm_count, stream);
@@ -579,7 +605,8 @@ extern "C" lsc_status lsc_conv2d_i8_nhwc(const int8_t* x, const int8_t* w, int64
                                          int64_t pw, int64_t dh, int64_t dw, const int32_t* bias,
                                          const float* scale, float s_out, int32_t act,
                                          int32_t rounding, int8_t* out_i8, float* out_f32,
-                                         int32_t* out_i32, lsc_stream stream) {
+                                         int32_t* out_i32, const int8_t* residual,
+                                         float residual_scale, lsc_stream stream) {
   lsc::ConvGeometry g{};
   g.n = n;
   g.h = h;
@@ -599,5 +626,5 @@ extern "C" lsc_status lsc_conv2d_i8_nhwc(const int8_t* x, const int8_t* w, int64
   g.oh = (h + 2 * ph - dh * (kh - 1) - 1) / sh + 1;
   g.ow = (wd + 2 * pw - dw * (kw - 1) - 1) / sw + 1;
   return lsc::launch_conv_i8(x, w, g, bias, scale, s_out, act, rounding, out_i8, out_f32,
-                             out_i32, static_cast<cudaStream_t>(stream));
+                             out_i32, residual, residual_scale, static_cast<cudaStream_t>(stream));
 }

@@ -60,11 +60,12 @@ struct ConvGeometry {
 };
 
 // INT8 NHWC convolution as an implicit GEMM (contraction_i8.cu): x [N,H,W,C] int8,
-// w [Cout, KH*KW*C] int8 (K ordered kh, kw, c), outputs NHWC [N,OH,OW,Cout].
+// w [Cout, KH*KW*C] int8 (K ordered kh, kw, c), outputs NHWC [N,OH,OW,Cout].  `residual`
+// (optional, int8 NHWC like the outputs) is added as (f32)r * res_scale before the activation.
 lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& g,
                           const int32_t* bias, const float* scale, float s_out, int act,
                           int rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
-                          cudaStream_t stream);
+                          const int8_t* residual, float res_scale, cudaStream_t stream);
 
 // INT8 GEMM + requant/dequant epilogue (contraction_i8.cu).  ldo = row stride of the outputs in
 // elements.  Validates its arguments.
@@ -98,6 +99,16 @@ lsc_status launch_batchnorm_f32(const float* x, float* y, int64_t n, int64_t c, 
 lsc_status launch_activation_f32(const float* x, float* y, int64_t n, int act, cudaStream_t st);
 lsc_status launch_add_f32(const float* a, const float* b, float* y, int64_t n, int act,
                           cudaStream_t st);
+
+// INT8 NHWC glue (pool.cu).
+lsc_status launch_quantize_nchw_to_nhwc_i8(const float* x, int8_t* y, int64_t n, int64_t c,
+                                           int64_t hw, int64_t cp, float scale, int rounding,
+                                           cudaStream_t st);
+lsc_status launch_maxpool_i8(const int8_t* x, int8_t* y, int64_t n, int64_t h, int64_t w, int64_t c,
+                             int64_t oh, int64_t ow, int kh, int kw, int sh, int sw, int ph, int pw,
+                             cudaStream_t st);
+lsc_status launch_avgpool_i8(const int8_t* x, int64_t n, int64_t hw, int64_t c, float s_in, float s_out,
+                             int rounding, int8_t* y_i8, float* y_f32, cudaStream_t st);
 
 // Quantization kernels (quant.cu).  `scales` == nullptr selects the per-tensor form with
 // scale0/zp0; otherwise channel c = (i / inner) % channels.

@@ -54,7 +54,7 @@ def gemm_i8(a, w, scale, bias=None, s_out=1.0, act=_lib.ACT_NONE,
 
 def conv2d_i8_nhwc(x, w, scale, bias=None, stride=(1, 1), pad=(0, 0), dilation=(1, 1),
                    s_out=1.0, act=_lib.ACT_NONE, rounding=_lib.ROUND_HALF_AWAY,
-                   out_i8=True, out_f32=False, out_i32=False):
+                   out_i8=True, out_f32=False, out_i32=False, residual=None, residual_scale=1.0):
     """INT8 NHWC convolution (implicit GEMM on the tensor cores, im2col by the TMA unit).
 
     x: [N,H,W,C] int8 (C a multiple of 16), w: [Cout,KH,KW,C] int8, scale: [Cout] f32,
@@ -64,6 +64,7 @@ def conv2d_i8_nhwc(x, w, scale, bias=None, stride=(1, 1), pad=(0, 0), dilation=(
     _need(w, torch.int8, "w")
     _need(scale, torch.float32, "scale")
     _need(bias, torch.int32, "bias")
+    _need(residual, torch.int8, "residual")
     n, h, wd, c = x.shape
     co, kh, kw, cw = w.shape
     if cw != c:
@@ -78,7 +79,7 @@ def conv2d_i8_nhwc(x, w, scale, bias=None, stride=(1, 1), pad=(0, 0), dilation=(
     check(lib().lsc_conv2d_i8_nhwc(_ptr(x), _ptr(w), n, h, wd, c, co, kh, kw, stride[0], stride[1],
                                    pad[0], pad[1], dilation[0], dilation[1], _ptr(bias), _ptr(scale),
                                    float(s_out), act, rounding, _ptr(q), _ptr(y), _ptr(acc),
-                                   _stream(dev)))
+                                   _ptr(residual), float(residual_scale), _stream(dev)))
     return q, y, acc
 
 

@@ -43,6 +43,13 @@ inline int8_t rust_f32_to_i8(float v) {
   return (int8_t)(int)v;
 }
 
+void conv_i8_chain_impl(const int8_t* x, const int8_t* w, int64_t n, int64_t h, int64_t wd,
+                        int64_t c_in, int64_t c_out, int64_t kh, int64_t kw, int64_t sh,
+                        int64_t sw, int64_t ph, int64_t pw, int64_t dh, int64_t dw,
+                        int64_t groups, const int32_t* bias, const float* scale, int act,
+                        float s_out, int rounding, const int8_t* residual, float r_scale,
+                        int8_t* out_i8, float* out_f32, int32_t* out_acc, int threads);
+
 inline int threads_or_default(int t) {
 #ifdef _OPENMP
   return t > 0 ? t : omp_get_max_threads();
@@ -435,9 +442,11 @@ void orc_gemm_i8_tn(const int8_t* a, const int8_t* w, int32_t* c, int64_t m, int
 
 namespace {
 inline void epilogue_one(int32_t acc, int32_t bias, float scale, int act, float s_out,
-                         int rounding, int8_t* oi8, float* of32, int32_t* oacc) {
+                         int rounding, int8_t* oi8, float* of32, int32_t* oacc,
+                         const int8_t* res = nullptr, float r_scale = 1.0f) {
   acc = (int32_t)((uint32_t)acc + (uint32_t)bias);  // i32 add (wrapping)
   float y = (float)acc * scale;                      // dequantize, quantized_ops.rs:36-40
+  if (res) y = y + orc_dequantize_value(*res, r_scale, 0);  // residual, dequantized
   y = orc_act(y, act);
   if (of32) *of32 = y;
   if (oacc) *oacc = acc;
@@ -483,6 +492,82 @@ void orc_conv2d_i8_nhwc_chain(const int8_t* x, const int8_t* w, int64_t n, int64
                               int64_t dw, int64_t groups, const int32_t* bias,
                               const float* scale, int act, float s_out, int rounding,
                               int8_t* out_i8, float* out_f32, int32_t* out_acc, int threads) {
+  conv_i8_chain_impl(x, w, n, h, wd, c_in, c_out, kh, kw, sh, sw, ph, pw, dh, dw, groups, bias,
+                     scale, act, s_out, rounding, nullptr, 1.0f, out_i8, out_f32, out_acc, threads);
+}
+
+void orc_conv2d_i8_nhwc_chain_res(const int8_t* x, const int8_t* w, int64_t n, int64_t h,
+                                  int64_t wd, int64_t c_in, int64_t c_out, int64_t kh, int64_t kw,
+                                  int64_t sh, int64_t sw, int64_t ph, int64_t pw, int64_t dh,
+                                  int64_t dw, const int32_t* bias, const float* scale, int act,
+                                  float s_out, int rounding, const int8_t* residual,
+                                  float r_scale, int8_t* out_i8, float* out_f32, int32_t* out_acc,
+                                  int threads) {
+  conv_i8_chain_impl(x, w, n, h, wd, c_in, c_out, kh, kw, sh, sw, ph, pw, dh, dw, 1, bias, scale,
+                     act, s_out, rounding, residual, r_scale, out_i8, out_f32, out_acc, threads);
+}
+
+// quantize_value (helpers.rs:139-155) per element with R selectable, NCHW -> NHWC, zero pad.
+void orc_quantize_nchw_to_nhwc(const float* x, int8_t* y, int64_t n, int64_t c, int64_t hw,
+                               int64_t cp, float scale, int rounding) {
+  for (int64_t b = 0; b < n; ++b)
+    for (int64_t p = 0; p < hw; ++p)
+      for (int64_t ch = 0; ch < cp; ++ch) {
+        int8_t q = 0;
+        if (ch < c) {
+          const int32_t r = rust_f32_to_i32(orc_round(x[(b * c + ch) * hw + p] / scale, rounding));
+          q = (int8_t)(r < -128 ? -128 : (r > 127 ? 127 : r));
+        }
+        y[(b * hw + p) * cp + ch] = q;
+      }
+}
+
+void orc_maxpool_i8_nhwc(const int8_t* x, int8_t* y, int64_t n, int64_t h, int64_t w, int64_t c,
+                         int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw) {
+  const int64_t oh = (h + 2 * ph - kh) / sh + 1, ow = (w + 2 * pw - kw) / sw + 1;
+  for (int64_t b = 0; b < n; ++b)
+    for (int64_t oy = 0; oy < oh; ++oy)
+      for (int64_t ox = 0; ox < ow; ++ox)
+        for (int64_t ch = 0; ch < c; ++ch) {
+          int m = -128;
+          for (int64_t r = 0; r < kh; ++r) {
+            const int64_t iy = oy * sh - ph + r;
+            if (iy < 0 || iy >= h) continue;
+            for (int64_t s = 0; s < kw; ++s) {
+              const int64_t ix = ox * sw - pw + s;
+              if (ix < 0 || ix >= w) continue;
+              const int v = x[((b * h + iy) * w + ix) * c + ch];
+              m = v > m ? v : m;
+            }
+          }
+          y[((b * oh + oy) * ow + ox) * c + ch] = (int8_t)m;
+        }
+}
+
+void orc_avgpool_i8_nhwc(const int8_t* x, int64_t n, int64_t hw, int64_t c, float s_in,
+                         float s_out, int rounding, int8_t* y_i8, float* y_f32) {
+  for (int64_t b = 0; b < n; ++b)
+    for (int64_t ch = 0; ch < c; ++ch) {
+      int32_t sum = 0;
+      for (int64_t p = 0; p < hw; ++p) sum += x[(b * hw + p) * c + ch];
+      const float v = ((float)sum * s_in) / (float)hw;
+      if (y_f32) y_f32[b * c + ch] = v;
+      if (y_i8) {
+        const int32_t r = rust_f32_to_i32(orc_round(v / s_out, rounding));
+        y_i8[b * c + ch] = (int8_t)(r < -128 ? -128 : (r > 127 ? 127 : r));
+      }
+    }
+}
+
+}  // extern "C"
+
+namespace {
+void conv_i8_chain_impl(const int8_t* x, const int8_t* w, int64_t n, int64_t h, int64_t wd,
+                        int64_t c_in, int64_t c_out, int64_t kh, int64_t kw, int64_t sh,
+                        int64_t sw, int64_t ph, int64_t pw, int64_t dh, int64_t dw,
+                        int64_t groups, const int32_t* bias, const float* scale, int act,
+                        float s_out, int rounding, const int8_t* residual, float r_scale,
+                        int8_t* out_i8, float* out_f32, int32_t* out_acc, int threads) {
   const int64_t oh = orc_conv_out_dim(h, kh, sh, ph, dh), ow = orc_conv_out_dim(wd, kw, sw, pw, dw);
   if (oh <= 0 || ow <= 0) return;
   const int64_t cpg = c_in / groups, opg = c_out / groups;
@@ -508,8 +593,7 @@ void orc_conv2d_i8_nhwc_chain(const int8_t* x, const int8_t* w, int64_t n, int64
           const int64_t e = ((b * oh + yy) * ow + xx) * c_out + o;
           epilogue_one(s, bias ? bias[o] : 0, scale[o], act, s_out, rounding,
                        out_i8 ? out_i8 + e : nullptr, out_f32 ? out_f32 + e : nullptr,
-                       out_acc ? out_acc + e : nullptr);
+                       out_acc ? out_acc + e : nullptr, residual ? residual + e : nullptr, r_scale);
         }
 }
-
-}  // extern "C"
+}  // namespace

@@ -138,6 +138,27 @@ void orc_conv2d_i8_nhwc_chain(const int8_t* x, const int8_t* w, int64_t n, int64
                               const float* scale, int act, float s_out, int rounding,
                               int8_t* out_i8, float* out_f32, int32_t* out_acc, int threads);
 
+/* The same with a residual added before the activation: y = dequant(acc) + (f32)r * r_scale,
+ * r int8 NHWC shaped like the output (a ResNet BasicBlock's Add + ReLU after its second conv;
+ * dequantize_value with zero point 0, helpers.rs:158-160). */
+void orc_conv2d_i8_nhwc_chain_res(const int8_t* x, const int8_t* w, int64_t n, int64_t h,
+                                  int64_t wd, int64_t c_in, int64_t c_out, int64_t kh, int64_t kw,
+                                  int64_t sh, int64_t sw, int64_t ph, int64_t pw, int64_t dh,
+                                  int64_t dw, const int32_t* bias, const float* scale, int act,
+                                  float s_out, int rounding, const int8_t* residual,
+                                  float r_scale, int8_t* out_i8, float* out_f32, int32_t* out_acc,
+                                  int threads);
+/* f32 NCHW -> int8 NHWC with channels padded to cp (quantize_value, helpers.rs:139-155, with R) */
+void orc_quantize_nchw_to_nhwc(const float* x, int8_t* y, int64_t n, int64_t c, int64_t hw,
+                               int64_t cp, float scale, int rounding);
+/* MaxPool2d on int8 NHWC codes, padding taps skipped (operator/pooling.rs:383-455) */
+void orc_maxpool_i8_nhwc(const int8_t* x, int8_t* y, int64_t n, int64_t h, int64_t w, int64_t c,
+                         int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw);
+/* GlobalAvgPool2d on int8 NHWC (operator/pooling.rs:457-530): y = ((f32)sum_q * s_in) / (H*W),
+ * then requantized with s_out (y_i8) and/or kept (y_f32) */
+void orc_avgpool_i8_nhwc(const int8_t* x, int64_t n, int64_t hw, int64_t c, float s_in,
+                         float s_out, int rounding, int8_t* y_i8, float* y_f32);
+
 #ifdef __cplusplus
 }
 #endif

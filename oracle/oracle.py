@@ -67,6 +67,11 @@ def _declare(l):
         "orc_requant": [P, I64, I64, P, P, C.c_int, F32, C.c_int, P, P, P],
         "orc_gemm_i8_chain": [P, P, I64, I64, I64, P, P, C.c_int, F32, C.c_int, P, P, P, C.c_int],
         "orc_conv2d_i8_nhwc_chain": [P, P] + [I64] * 14 + [P, P, C.c_int, F32, C.c_int, P, P, P, C.c_int],
+        "orc_conv2d_i8_nhwc_chain_res": [P, P] + [I64] * 13 + [P, P, C.c_int, F32, C.c_int, P, F32, P, P, P,
+                                                                C.c_int],
+        "orc_quantize_nchw_to_nhwc": [P, P, I64, I64, I64, I64, F32, C.c_int],
+        "orc_maxpool_i8_nhwc": [P, P] + [I64] * 10,
+        "orc_avgpool_i8_nhwc": [P, I64, I64, I64, F32, F32, C.c_int, P, P],
     }
     for name, args in sig.items():
         f = getattr(l, name)
@@ -273,8 +278,10 @@ def gemm_i8_chain(a, w, bias, scale, act=ACT_NONE, s_out=1.0, rounding=ROUND_HAL
 
 
 def conv2d_i8_nhwc_chain(x, w, bias, scale, stride=(1, 1), pad=(0, 0), dilation=(1, 1), groups=1,
-                         act=ACT_NONE, s_out=1.0, rounding=ROUND_HALF_AWAY, threads=0):
-    """x: [N,H,W,Cin] int8; w: [Cout,KH,KW,Cin/groups] int8; returns NHWC outputs."""
+                         act=ACT_NONE, s_out=1.0, rounding=ROUND_HALF_AWAY, threads=0,
+                         residual=None, residual_scale=1.0):
+    """x: [N,H,W,Cin] int8; w: [Cout,KH,KW,Cin/groups] int8; returns NHWC outputs.
+    `residual` (int8, output-shaped) is added before the activation (groups must be 1)."""
     x, w = _c(x, np.int8), _c(w, np.int8)
     n, h, wd, ci = x.shape
     co, kh, kw, _ = w.shape
@@ -283,8 +290,42 @@ def conv2d_i8_nhwc_chain(x, w, bias, scale, stride=(1, 1), pad=(0, 0), dilation=
     oi8 = np.empty((n, oh, ow, co), np.int8)
     of32 = np.empty((n, oh, ow, co), np.float32)
     oacc = np.empty((n, oh, ow, co), np.int32)
-    lib().orc_conv2d_i8_nhwc_chain(_p(x), _p(w), n, h, wd, ci, co, kh, kw, stride[0], stride[1], pad[0],
-                                   pad[1], dilation[0], dilation[1], groups, _p(_c(bias, np.int32)),
-                                   _p(_c(scale, np.float32)), act, s_out, rounding, _p(oi8), _p(of32),
-                                   _p(oacc), threads)
+    if residual is None:
+        lib().orc_conv2d_i8_nhwc_chain(_p(x), _p(w), n, h, wd, ci, co, kh, kw, stride[0], stride[1], pad[0],
+                                       pad[1], dilation[0], dilation[1], groups, _p(_c(bias, np.int32)),
+                                       _p(_c(scale, np.float32)), act, s_out, rounding, _p(oi8), _p(of32),
+                                       _p(oacc), threads)
+    else:
+        r = _c(residual, np.int8)
+        assert r.shape == oi8.shape and groups == 1
+        lib().orc_conv2d_i8_nhwc_chain_res(_p(x), _p(w), n, h, wd, ci, co, kh, kw, stride[0], stride[1],
+                                           pad[0], pad[1], dilation[0], dilation[1], _p(_c(bias, np.int32)),
+                                           _p(_c(scale, np.float32)), act, s_out, rounding, _p(r),
+                                           residual_scale, _p(oi8), _p(of32), _p(oacc), threads)
     return oi8, of32, oacc
+
+
+def quantize_nchw_to_nhwc(x, scale, cp, rounding=ROUND_HALF_AWAY):
+    x = _c(x, np.float32)
+    n, c, h, w = x.shape
+    y = np.empty((n, h, w, cp), np.int8)
+    lib().orc_quantize_nchw_to_nhwc(_p(x), _p(y), n, c, h * w, cp, scale, rounding)
+    return y
+
+
+def maxpool_i8_nhwc(x, k=3, s=2, p=1):
+    x = _c(x, np.int8)
+    n, h, w, c = x.shape
+    oh, ow = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+    y = np.empty((n, oh, ow, c), np.int8)
+    lib().orc_maxpool_i8_nhwc(_p(x), _p(y), n, h, w, c, k, k, s, s, p, p)
+    return y
+
+
+def avgpool_i8_nhwc(x, s_in, s_out=1.0, rounding=ROUND_HALF_AWAY):
+    x = _c(x, np.int8)
+    n, h, w, c = x.shape
+    yq = np.empty((n, c), np.int8)
+    yf = np.empty((n, c), np.float32)
+    lib().orc_avgpool_i8_nhwc(_p(x), n, h * w, c, s_in, s_out, rounding, _p(yq), _p(yf))
+    return yq, yf

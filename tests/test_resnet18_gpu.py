@@ -1,0 +1,167 @@
+"""ResNet-18-shaped INT8 network through the Backend API vs the oracle running the same
+quantized network (same f32 parameters, the GPU's calibrated activation scales), bit for bit;
+plus the INT8 glue operators (input quantize to NHWC, MaxPool2d, GlobalAvgPool2d, residual
+Add+ReLU fused into a conv) on their own."""
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def be(cuda):
+    from lightship_b200.backend import CudaBackend, GpuBackendConfig
+    b = CudaBackend(GpuBackendConfig(device_id=0, arena_bytes=1 << 30))
+    yield b
+    b.close()
+
+
+def oracle_resnet18(x, model, rounding):
+    """The quantized network restated with the oracle's functions."""
+    sc = model.scales
+    xq = orc.quantize_nchw_to_nhwc(x, sc["input"], 16, rounding)
+    acts = {"x_q": xq}
+
+    def conv(spec, in_name, residual=None):
+        xin = acts[in_name]
+        s_in = sc["input"] if in_name == "x_q" else sc[in_name]
+        wf, bf = orc.bn_fold(spec.w, spec.bias, *spec.bn)
+        wq, sw = orc.quantize_weights_per_channel(np.ascontiguousarray(wf.transpose(0, 2, 3, 1)))
+        cs = xin.shape[3]
+        wp = np.zeros((spec.cout, spec.k, spec.k, cs), np.int8)
+        wp[..., :spec.cin] = wq
+        scale = (np.float32(s_in) * sw).astype(np.float32)
+        bq = np.array([orc.quantize_value(float(bf[o]), float(scale[o]), 0, orc.QINT32) for o in range(spec.cout)],
+                      np.int32)
+        res = None if residual is None else acts[residual]
+        rs = 1.0 if residual is None else sc[residual]
+        q, _, _ = orc.conv2d_i8_nhwc_chain(xin, wp, bq, scale, (spec.stride,) * 2, (spec.pad,) * 2, (1, 1), 1,
+                                           orc.ACT_RELU if spec.relu else orc.ACT_NONE, sc[spec.name], rounding,
+                                           residual=res, residual_scale=rs)
+        acts[spec.name] = q
+
+    conv(model.convs[0], "x_q")
+    acts["pool"] = orc.maxpool_i8_nhwc(acts["conv1"], 3, 2, 1)
+    sc = dict(sc)
+    prev = "pool"
+    for c1, c2, ds in model.blocks:
+        conv(c1, prev)
+        if ds is not None:
+            conv(ds, prev)
+            res = ds.name
+        else:
+            res = prev
+        conv(c2, c1.name, residual=res)
+        prev = c2.name
+    pooled, _ = orc.avgpool_i8_nhwc(acts[prev], sc[prev], sc["pooled"], rounding)
+    wq, sw = orc.quantize_weights_per_channel(model.fc_w)
+    scale = (np.float32(sc["pooled"]) * sw).astype(np.float32)
+    bq = np.array([orc.quantize_value(float(model.fc_b[o]), float(scale[o]), 0, orc.QINT32)
+                   for o in range(model.num_classes)], np.int32)
+    _, logits, _ = orc.gemm_i8_chain(pooled, wq, bq, scale, orc.ACT_NONE, 1.0, rounding)
+    return logits, acts
+
+
+@pytest.mark.parametrize("rounding", [0, 1])
+def test_resnet18_int8_bit_exact(be, cuda, rounding):
+    import torch
+    from lightship_b200.backend import Rounding
+    from lightship_b200.resnet18 import ResNet18Int8
+    batch = 2
+    model = ResNet18Int8(be, batch, cuda, image=224, seed=3, rounding=Rounding(rounding))
+    rng = np.random.default_rng(99)
+    x = rng.normal(size=(batch, 3, 224, 224)).astype(np.float32)
+    xd = torch.from_numpy(x).to(cuda)
+    model.calibrate(xd)
+    logits = model.forward(xd).cpu().numpy()
+    torch.cuda.synchronize()
+    want, acts = oracle_resnet18(x, model, rounding)
+    for name in ("conv1", "pool", "layer1.0.conv2", "layer2.0.downsample", "layer4.1.conv2"):
+        np.testing.assert_array_equal(model.buf[name].cpu().numpy(), acts[name], err_msg=name)
+    np.testing.assert_array_equal(logits.view(np.uint32), want.view(np.uint32))
+    # the network is not degenerate: activations use the int8 range, logits differ per image
+    assert np.abs(acts["layer4.1.conv2"]).max() >= 64
+    assert not np.array_equal(logits[0], logits[1])
+
+
+def test_resnet18_graph_replay_matches_eager(be, cuda):
+    import torch
+    from lightship_b200.resnet18 import ResNet18Int8
+    batch = 4
+    model = ResNet18Int8(be, batch, cuda, image=224, seed=5)
+    rng = np.random.default_rng(7)
+    x = torch.from_numpy(rng.normal(size=(batch, 3, 224, 224)).astype(np.float32)).to(cuda)
+    model.calibrate(x)
+    eager = model.forward(x).clone()
+    static = x.clone()
+    g = model.capture(static)
+    x2 = torch.from_numpy(rng.normal(size=(batch, 3, 224, 224)).astype(np.float32)).to(cuda)
+    static.copy_(x2)
+    g.replay()
+    torch.cuda.synchronize()
+    replay = model.logits.clone()
+    eager2 = model.forward(x2).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(replay, eager2)
+    assert not torch.equal(eager, eager2)
+
+
+def test_maxpool_and_avgpool_ops(be):
+    from lightship_b200.backend import (DataType, OperatorDef, OperatorType, Quantization, StorageLayout,
+                                        Tensor)
+    rng = np.random.default_rng(1)
+    x = rng.integers(-128, 128, size=(3, 15, 13, 48), dtype=np.int8)
+    xt = Tensor("x", list(x.shape), DataType.QInt8, x, layout=StorageLayout.NHWC, quantization=Quantization([0.03]))
+    y = Tensor("y", [1], DataType.QInt8, np.zeros(3 * 8 * 7 * 48, np.int8))
+    op = be.compile_operator(OperatorDef("mp", OperatorType.MaxPool2d, stride=(2, 2), padding=(1, 1), kernel=(3, 3)),
+                             None, [xt], [y])
+    be.execute(op, [xt], [y])
+    assert y.shape == [3, 8, 7, 48]
+    np.testing.assert_array_equal(y.numpy().reshape(3, 8, 7, 48), orc.maxpool_i8_nhwc(x, 3, 2, 1))
+    for rounding in (0, 1):
+        from lightship_b200.backend import Rounding
+        yq = Tensor("yq", [1], DataType.QInt8, np.zeros(3 * 48, np.int8), quantization=Quantization([0.01]))
+        yf = Tensor("yf", [1], DataType.F32, np.zeros(3 * 48, np.float32))
+        op = be.compile_operator(OperatorDef("gap", OperatorType.GlobalAvgPool2d, rounding=Rounding(rounding)),
+                                 None, [xt], [yq, yf])
+        be.execute(op, [xt], [yq, yf])
+        wq, wf = orc.avgpool_i8_nhwc(x, 0.03, 0.01, rounding)
+        np.testing.assert_array_equal(yf.numpy().reshape(3, 48).view(np.uint32), wf.view(np.uint32))
+        np.testing.assert_array_equal(yq.numpy().reshape(3, 48), wq)
+
+
+def test_quantize_input_to_nhwc(be):
+    from lightship_b200.backend import (DataType, OperatorDef, OperatorType, Quantization, StorageLayout,
+                                        Tensor)
+    rng = np.random.default_rng(2)
+    x = rng.normal(size=(2, 3, 17, 19)).astype(np.float32)
+    xt = Tensor("x", list(x.shape), DataType.F32, x, layout=StorageLayout.NCHW)
+    q = Tensor("q", [2, 17, 19, 16], DataType.QInt8, np.zeros(2 * 17 * 19 * 16, np.int8),
+               layout=StorageLayout.NHWC, quantization=Quantization([0.02]))
+    op = be.compile_operator(OperatorDef("q", OperatorType.Quantize), None, [xt], [q])
+    be.execute(op, [xt], [q])
+    assert q.shape == [2, 17, 19, 16]
+    np.testing.assert_array_equal(q.numpy().reshape(2, 17, 19, 16), orc.quantize_nchw_to_nhwc(x, 0.02, 16))
+
+
+def test_conv_residual_kernel_level(cuda):
+    """lsc_conv2d_i8_nhwc with a residual, including a ragged output tile."""
+    import torch
+    from lightship_b200 import ops
+    rng = np.random.default_rng(4)
+    n, h, c, co = 3, 9, 64, 96
+    x = rng.integers(-127, 128, size=(n, h, h, c), dtype=np.int8)
+    w = rng.integers(-127, 128, size=(co, 3, 3, c), dtype=np.int8)
+    r = rng.integers(-128, 128, size=(n, h, h, co), dtype=np.int8)
+    scale = rng.uniform(1e-5, 1e-4, co).astype(np.float32)
+    want = orc.conv2d_i8_nhwc_chain(x, w, None, scale, (1, 1), (1, 1), (1, 1), 1, orc.ACT_RELU, 0.02,
+                                    orc.ROUND_HALF_AWAY, residual=r, residual_scale=0.015)
+    q, y, _ = ops.conv2d_i8_nhwc(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda),
+                                 torch.from_numpy(scale).to(cuda), None, pad=(1, 1), s_out=0.02,
+                                 act=1, out_i8=True, out_f32=True, residual=torch.from_numpy(r).to(cuda),
+                                 residual_scale=0.015)
+    ops.check_device()
+    np.testing.assert_array_equal(y.cpu().numpy().view(np.uint32), want[1].view(np.uint32))
+    np.testing.assert_array_equal(q.cpu().numpy(), want[0])
