@@ -1,26 +1,33 @@
-"""Benchmark of the CUDA backend's headline workload.
+"""Benchmark of the CUDA backend on the headline workloads.
 
-Workload (one "step"): the INT8 per-channel symmetric GEMM M=N=K=4096 -- int8 A and W
-uniform in [-127, 127], per-output-channel f32 scales U[0.001, 0.02], int32 bias, int32
-accumulate, requantized int8 output (round-half-even, saturate) plus the dequantized f32
-variant, both written by one fused launch of this package's tcgen05 kernel.
+Default workload -- ResNet-18-shaped INT8 CNN, batch 256 split evenly over the GPUs:
+conv1 7x7/2, four stages of BasicBlocks (64/128/256/512), global average pool, FC-1000;
+He-initialised weights with random BatchNorm statistics, BN folded, weights INT8 per output
+channel, ReLU and each block's residual Add+ReLU fused, activations int8 NHWC; input
+224x224x3 ~ N(0, 1) (seeded synthetic data; no dataset).  Activation scales are calibrated
+once on the first per-rank batch; the network then runs as one captured CUDA graph.
 
-* ``value``: whole-job TOPS (2*M*N*K per GPU per step) with operands resident in HBM; the
-  L2 is flushed before every timed launch (256 MiB write) and each launch is timed with CUDA
-  events on the launching stream; the max over ranks is taken.
-* ``e2e``: the same metric through the public Backend API (``CudaBackend.execute`` with host
-  tensors): every step copies A from pinned host memory to the device and both outputs back.
-* ``roofline``: tensor-bound; achieved INT8 TOPS of the kernel against the INT8 peak derived
-  from the measured bf16 burst peak (B200 issues dense INT8 at twice the bf16 rate).
-* ``cpu_baseline`` (rank 0, one GPU): the oracle's restatement of the reference CPU chain
-  (quantized_gemm_int8 triple loop + dequantize/requantize, threaded over M) on a 512-row
-  slice of the same workload, on all host threads.
+* ``value``: whole-job images per second: 256 / (max over ranks of the per-step device time).
+  Each step is one graph replay of the rank's shard, timed with CUDA events on the launching
+  stream; the L2 is flushed (256 MiB write) before every timed step.
+* ``e2e``: the same through the host boundary: each step copies the rank's f32 input shard
+  from pinned host memory (``lsc_memcpy_h2d``), runs the network and copies the logits back
+  (``lsc_memcpy_d2h``).
+* ``roofline``: tensor-bound; the dominant kernel is the INT8 implicit-GEMM convolution
+  (``contraction_i8_kernel``).  achieved = algorithmic conv ops per image x images / summed
+  conv-kernel time (events around every conv launch of one eager pass); peak = 2 x the
+  measured bf16 burst peak (dense INT8 issues at twice the bf16 rate).
+* ``int8_gemm_4096`` (rank 0): the INT8 per-channel GEMM M=N=K=4096 (bias, requant int8
+  half-even + dequant f32, one fused launch) in TOPS with its own roofline fraction.
+* ``cpu_baseline`` (rank 0, one GPU): the oracle's restatement of the same quantized network
+  on the host cores (direct convolutions, OpenMP) on a bounded sample of images.
 
-Multi-GPU: replicas (the GEMM does not shard without a reduction; weak scaling), one rank
-per GPU under torchrun; no collective touches the data path.
+Multi-GPU: one rank per GPU (torchrun), each holding its own weights; no collective touches
+the data path (NCCL is used only for barriers and the max-over-ranks timing reduction).
 
-``--impl reference`` times the reference CPU implementation (the oracle port) on the host
-cores, rank 0 only, and prints the same metric with ``"impl": "reference"``.
+``--impl reference`` times the reference's CPU path (the oracle port; the Rust reference
+cannot be built here) on the host cores, rank 0 only, and prints the same metric.
+``--workload gemm`` makes the 4096^3 INT8 GEMM (TOPS) the headline instead.
 """
 from __future__ import annotations
 
@@ -40,21 +47,16 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-M = N = K = 4096
-OPS_PER_STEP = 2 * M * N * K
-METRIC = "INT8 conv/GEMM TOPS"
-UNIT = "TOPS"
-WORKLOAD = "int8 per-channel GEMM M=N=K=4096, int32 bias, requant int8 (half-even) + dequant f32"
-SEED = 20260415
-S_OUT_SAMPLE_SEED = 7
-
-
-def make_inputs(rng):
-    a = rng.integers(-127, 128, size=(M, K), dtype=np.int8)
-    w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
-    scale = rng.uniform(0.001, 0.02, size=N).astype(np.float32)
-    bias = rng.integers(-100000, 100000, size=N, dtype=np.int32)
-    return a, w, scale, bias
+METRIC = "INT8 conv/GEMM TOPS (% peak); ResNet-18 INT8 img/s at 1/2/4/8 B200"
+GLOBAL_BATCH = 256
+IMAGE = 224
+NET_SEED = 20260415
+DATA_SEED = 1234
+GEMM_M = GEMM_N = GEMM_K = 4096
+GEMM_OPS = 2 * GEMM_M * GEMM_N * GEMM_K
+GEMM_WORKLOAD = "int8 per-channel GEMM M=N=K=4096, int32 bias, requant int8 (half-even) + dequant f32"
+RESNET_WORKLOAD = ("ResNet-18 INT8 (conv1 7x7/2, 4 BasicBlock stages 64/128/256/512, maxpool 3x3/2, "
+                   "global avgpool, FC-1000), 224x224x3 input, batch 256 split over the GPUs")
 
 
 def load_peaks():
@@ -66,9 +68,9 @@ def load_peaks():
     return 1590.0, "fallback"
 
 
-def load_traffic():
-    """dram bytes per launch of the GEMM kernel from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "contraction_i8_gemm_4096.md")
+def load_traffic(profile):
+    """dram bytes per launch of the profiled kernel from a committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", profile)
     if not os.path.exists(p):
         return None
     with open(p) as f:
@@ -95,8 +97,7 @@ class ClockSampler:
 
     def start(self):
         try:
-            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                   "-lms", "50"]
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"]
             if self.uuid:
                 cmd += ["-i", self.uuid]
             self.f = open(self.path, "w")
@@ -135,57 +136,135 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(loaded)}
 
 
-# --------------------------------------------------------------------------- CPU baseline
-def cpu_baseline_rows(rows, a, w_kn, bias, scale, s_out, threads=0):
-    """The reference CPU chain on rows [0, rows) of A: NN triple loop then the epilogue."""
+def network_conv_ops(model):
+    """{conv name: ops per image} from the model's activation shapes."""
+    ops = {}
+    for spec in model.convs:
+        _, oh, ow, _ = model.shapes[spec.name]
+        ops[spec.name] = 2 * spec.cout * oh * ow * spec.k * spec.k * spec.cin
+    return ops
+
+
+# --------------------------------------------------------------------------- CPU side
+def cpu_resnet_sample(images, scales=None, threads=0):
+    """The reference CPU path (oracle port) on `images` images; returns (seconds, logits)."""
+    from lightship_b200.resnet18 import build_params
     from oracle import oracle as orc
+    convs, blocks, fw, fb = build_params(NET_SEED)
+    rng = np.random.default_rng(DATA_SEED)
+    x = rng.normal(size=(images, 3, IMAGE, IMAGE)).astype(np.float32)
     t0 = time.perf_counter()
-    acc = orc.gemm_i8_nn(a[:rows], w_kn, threads)
-    orc.requant(acc, bias, scale, orc.ACT_NONE, s_out, orc.ROUND_HALF_EVEN)
-    return time.perf_counter() - t0
-
-
-def run_cpu_baseline(a, w, bias, scale, s_out, rows=512):
-    w_kn = np.ascontiguousarray(w.T)
-    dt = cpu_baseline_rows(rows, a, w_kn, bias, scale, s_out)
-    ops = 2 * rows * N * K
-    return {"value": ops / dt / 1e12, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-            "sample": f"rows 0..{rows - 1} of the 4096^3 chain (1/{M // rows} of M), reference "
-                      f"loop order (i, j, p) over B[K,N], OpenMP over M, {dt:.2f} s"}
+    logits, sc, _ = orc.resnet18_int8(x, convs, blocks, fw, fb, scales, 0, threads)
+    return time.perf_counter() - t0, logits, sc
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    rng = np.random.default_rng(SEED)
-    a, w, scale, bias = make_inputs(rng)
-    w_kn = np.ascontiguousarray(w.T)
-    s_out = 40.0
-    # size each step so that warmup + steps take about two minutes
-    t_probe = cpu_baseline_rows(16, a, w_kn, bias, scale, s_out)
-    per_row = t_probe / 16
+    if args.workload == "gemm":
+        return run_reference_gemm(args)
+    # calibrate once on two images, then size each step to about two minutes in total
+    _, _, scales = cpu_resnet_sample(2)
+    t1, _, _ = cpu_resnet_sample(1, scales)
     budget = 120.0 / max(1, args.steps + args.warmup)
-    rows = int(max(8, min(M, budget / max(per_row, 1e-9))))
+    images = int(max(1, min(GLOBAL_BATCH, budget / max(t1, 1e-6))))
     for _ in range(args.warmup):
-        cpu_baseline_rows(rows, a, w_kn, bias, scale, s_out)
-    times = [cpu_baseline_rows(rows, a, w_kn, bias, scale, s_out) for _ in range(args.steps)]
+        cpu_resnet_sample(images, scales)
+    times = [cpu_resnet_sample(images, scales)[0] for _ in range(args.steps)]
     t = sum(times) / len(times)
-    value = 2 * rows * N * K / t / 1e12
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "sample_rows_per_step": rows},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"rows 0..{rows - 1} of A per step (1/{M / rows:.1f} of M), "
-                                       "reference loop order, OpenMP over M"},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    value = images / t
+    line = {"metric": METRIC, "value": value, "unit": "img/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": RESNET_WORKLOAD, "images_per_step": images},
+            "cpu_baseline": {"value": value, "unit": "img/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{images} images per step through the oracle's quantized ResNet-18 "
+                                       "(direct int8 convolutions, OpenMP)"},
+            "e2e": {"value": value, "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
 
-# --------------------------------------------------------------------------- GPU arm
+def gemm_inputs():
+    rng = np.random.default_rng(NET_SEED)
+    a = rng.integers(-127, 128, size=(GEMM_M, GEMM_K), dtype=np.int8)
+    w = rng.integers(-127, 128, size=(GEMM_N, GEMM_K), dtype=np.int8)
+    scale = rng.uniform(0.001, 0.02, size=GEMM_N).astype(np.float32)
+    bias = rng.integers(-100000, 100000, size=GEMM_N, dtype=np.int32)
+    return a, w, scale, bias
+
+
+def cpu_gemm_rows(rows, a, w_kn, bias, scale, s_out):
+    """The reference CPU chain on rows [0, rows) of A: NN triple loop then the epilogue."""
+    from oracle import oracle as orc
+    t0 = time.perf_counter()
+    acc = orc.gemm_i8_nn(a[:rows], w_kn)
+    orc.requant(acc, bias, scale, orc.ACT_NONE, s_out, orc.ROUND_HALF_EVEN)
+    return time.perf_counter() - t0
+
+
+def run_reference_gemm(args):
+    a, w, scale, bias = gemm_inputs()
+    w_kn = np.ascontiguousarray(w.T)
+    per_row = cpu_gemm_rows(16, a, w_kn, bias, scale, 40.0) / 16
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    rows = int(max(8, min(GEMM_M, budget / max(per_row, 1e-9))))
+    for _ in range(args.warmup):
+        cpu_gemm_rows(rows, a, w_kn, bias, scale, 40.0)
+    t = sum(cpu_gemm_rows(rows, a, w_kn, bias, scale, 40.0) for _ in range(args.steps)) / args.steps
+    value = 2 * rows * GEMM_N * GEMM_K / t / 1e12
+    line = {"metric": METRIC, "value": value, "unit": "TOPS", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": GEMM_WORKLOAD, "sample_rows_per_step": rows},
+            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"rows 0..{rows - 1} of A per step, reference loop order, OpenMP over M"},
+            "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- GPU side
+def gemm_measure(torch, dev, steps, warmup):
+    """The 4096^3 INT8 chain on this device: (TOPS, ms per launch, s_out)."""
+    from lightship_b200 import _lib
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sptr = C.c_void_p(stream.cuda_stream)
+    a, w, scale, bias = gemm_inputs()
+    ta, tw = torch.from_numpy(a).to(dev), torch.from_numpy(w).to(dev)
+    ts, tb = torch.from_numpy(scale).to(dev), torch.from_numpy(bias).to(dev)
+    q = torch.empty((GEMM_M, GEMM_N), dtype=torch.int8, device=dev)
+    y = torch.empty((GEMM_M, GEMM_N), dtype=torch.float32, device=dev)
+    ws = torch.zeros(4, dtype=torch.int32, device=dev)
+    s_dev = torch.empty(1, dtype=torch.float32, device=dev)
+    z_dev = torch.empty(1, dtype=torch.int32, device=dev)
+    P = lambda t: C.c_void_p(t.data_ptr())
+    _lib.check(lib.lsc_gemm_i8(P(ta), P(tw), GEMM_M, GEMM_N, GEMM_K, P(tb), P(ts), 1.0, 0, 1, None, P(y), None, sptr))
+    _lib.check(lib.lsc_find_scale_zp_f32(P(y), GEMM_M * GEMM_N, 9, 1, P(ws), 16, P(s_dev), P(z_dev), sptr))
+    s_out = float(s_dev.item())
+
+    def launch():
+        _lib.check(lib.lsc_gemm_i8(P(ta), P(tw), GEMM_M, GEMM_N, GEMM_K, P(tb), P(ts), s_out, 0, 1, P(q), P(y),
+                                   None, sptr))
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(warmup):
+        flush.zero_()
+        launch()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize(dev)
+    for s, e in ev:
+        flush.zero_()
+        s.record(stream)
+        launch()
+        e.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = float(np.mean([s.elapsed_time(e) for s, e in ev]))
+    return GEMM_OPS / (ms * 1e-3) / 1e12, ms, s_out
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -197,134 +276,175 @@ def run_gpu(args):
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
 
     from lightship_b200 import _lib, ops
-    from lightship_b200.backend import (CudaBackend, DataType, GpuBackendConfig, OperatorDef,
-                                        OperatorType, Quantization, Rounding, Tensor)
-    lib = _lib.lib()
-    stream = torch.cuda.current_stream(dev)
-    sptr = C.c_void_p(stream.cuda_stream)
-
-    rng = np.random.default_rng(SEED)
-    a, w, scale, bias = make_inputs(rng)
-    ta, tw = torch.from_numpy(a).to(dev), torch.from_numpy(w).to(dev)
-    ts, tb = torch.from_numpy(scale).to(dev), torch.from_numpy(bias).to(dev)
-    q = torch.empty((M, N), dtype=torch.int8, device=dev)
-    y = torch.empty((M, N), dtype=torch.float32, device=dev)
-
-    # output scale: find_scale_zp (symmetric) on the dequantized output, on the device
-    ws = torch.zeros(4, dtype=torch.int32, device=dev)
-    s_dev = torch.empty(1, dtype=torch.float32, device=dev)
-    z_dev = torch.empty(1, dtype=torch.int32, device=dev)
-    _lib.check(lib.lsc_gemm_i8(C.c_void_p(ta.data_ptr()), C.c_void_p(tw.data_ptr()), M, N, K,
-                               C.c_void_p(tb.data_ptr()), C.c_void_p(ts.data_ptr()), 1.0, 0, 1,
-                               None, C.c_void_p(y.data_ptr()), None, sptr))
-    _lib.check(lib.lsc_find_scale_zp_f32(C.c_void_p(y.data_ptr()), M * N, 9, 1, C.c_void_p(ws.data_ptr()),
-                                         16, C.c_void_p(s_dev.data_ptr()), C.c_void_p(z_dev.data_ptr()), sptr))
-    s_out = float(s_dev.item())
-
-    def launch():
-        _lib.check(lib.lsc_gemm_i8(C.c_void_p(ta.data_ptr()), C.c_void_p(tw.data_ptr()), M, N, K,
-                                   C.c_void_p(tb.data_ptr()), C.c_void_p(ts.data_ptr()), s_out, 0, 1,
-                                   C.c_void_p(q.data_ptr()), C.c_void_p(y.data_ptr()), None, sptr))
-
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    bf16_peak, peak_src = load_peaks()
+    int8_peak = 2.0 * bf16_peak
+    peak_source = f"2 x {peak_src} bf16 burst ({bf16_peak} TFLOP/s); nominal dense INT8 4500 TOPS"
     uuid = None
     try:
         uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
     except Exception:
         pass
-    sampler = ClockSampler(uuid)
 
+    if args.workload == "gemm":
+        sampler = ClockSampler(uuid)
+        sampler.start()
+        barrier()
+        tops, ms, s_out = gemm_measure(torch, dev, args.steps, args.warmup)
+        barrier()
+        clocks = sampler.stop()
+        ms_max = max_over_ranks(ms)
+        line = {"metric": METRIC, "value": world * GEMM_OPS / (ms_max * 1e-3) / 1e12, "unit": "TOPS",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic",
+                "config": {"workload": GEMM_WORKLOAD, "parallelism": f"replicas x{world}",
+                           "l2": "flushed (256 MiB write) before every timed launch"},
+                "roofline": {"bound": "tensor", "achieved": tops, "peak": int8_peak, "unit": "TOPS",
+                             "frac": tops / int8_peak, "traffic": load_traffic("contraction_i8_gemm_4096.md"),
+                             "peak_source": peak_source},
+                "gpu_launches": args.steps, "clocks": clocks}
+        if world > 1:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return 0
+
+    # ------------------------------------------------------------------ ResNet-18 INT8
+    from lightship_b200.backend import CudaBackend, GpuBackendConfig
+    from lightship_b200.resnet18 import ResNet18Int8
+    if GLOBAL_BATCH % world:
+        raise SystemExit(f"batch {GLOBAL_BATCH} does not split over {world} GPUs")
+    per = GLOBAL_BATCH // world
+    # the global batch is seeded; each rank takes its contiguous shard
+    rng = np.random.default_rng(DATA_SEED)
+    x_all = rng.normal(size=(GLOBAL_BATCH, 3, IMAGE, IMAGE)).astype(np.float32)
+    x_host = torch.from_numpy(x_all[rank * per:(rank + 1) * per]).pin_memory()
+    del x_all
+    be = CudaBackend(GpuBackendConfig(device_id=local, arena_bytes=256 << 20))
+    model = ResNet18Int8(be, per, dev, image=IMAGE, seed=NET_SEED)
+    x_dev = x_host.to(dev, non_blocking=False)
+    model.calibrate(x_dev)
+    stream = torch.cuda.current_stream(dev)
+
+    # eager pass with events around every conv launch: the conv kernel's share and TOPS
+    conv_ops = network_conv_ops(model)
+    fc_ops = 2 * 512 * model.num_classes
+    img_ops = sum(conv_ops.values()) + fc_ops
+    evs = {}
+    orig_run_conv = model._run_conv
+
+    def timed_conv(spec, *a, **k):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        orig_run_conv(spec, *a, **k)
+        e.record(stream)
+        evs.setdefault(spec.name, []).append((s, e))
+
+    model._run_conv = timed_conv
+    for _ in range(3):
+        model.forward(x_dev)
+    torch.cuda.synchronize(dev)
+    model._run_conv = orig_run_conv
+    conv_ms = sum(np.mean([s.elapsed_time(e) for s, e in v]) for v in evs.values())
+    conv_tops = sum(conv_ops.values()) * per / (conv_ms * 1e-3) / 1e12
+
+    graph = model.capture(x_dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for _ in range(args.warmup):
         flush.zero_()
-        launch()
+        graph.replay()
     torch.cuda.synchronize(dev)
     ops.check_device()
-
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler(uuid)
     sampler.start()
-    if world > 1:
-        dist.barrier()
+    barrier()
     torch.cuda.synchronize(dev)
-    for i in range(args.steps):
+    for s, e in ev:
         flush.zero_()
-        starts[i].record(stream)
-        launch()
-        ends[i].record(stream)
+        s.record(stream)
+        graph.replay()
+        e.record(stream)
     torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
+    barrier()
     clocks = sampler.stop()
     ops.check_device()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    ms = float(np.mean(step_ms))
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = world * OPS_PER_STEP / (ms_max * 1e-3) / 1e12
+    ms = float(np.mean([s.elapsed_time(e) for s, e in ev]))
+    ms_max = max_over_ranks(ms)
+    value = GLOBAL_BATCH / (ms_max * 1e-3)
 
-    # ---- end to end through the Backend API with host tensors
-    be = CudaBackend(GpuBackendConfig(device_id=local, rounding=Rounding.HalfEven))
-    w_t = Tensor("W", [N, K], DataType.QInt8, w, quantization=Quantization(list(map(float, scale))))
-    b_t = Tensor("bias", [N], DataType.QInt32, bias)
-    a_host = torch.from_numpy(a).pin_memory()
-    q_host = torch.empty((M, N), dtype=torch.int8).pin_memory()
-    y_host = torch.empty((M, N), dtype=torch.float32).pin_memory()
-    a_t = Tensor("A", [M, K], DataType.QInt8, a_host, quantization=Quantization([1.0]))
-    q_t = Tensor("Q", [1], DataType.QInt8, q_host)
-    y_t = Tensor("Y", [1], DataType.F32, y_host)
-    opdef = OperatorDef("fc_int8", OperatorType.FullyConnected, rounding=Rounding.HalfEven,
-                        output_scale=s_out)
-    compiled = be.compile_operator(opdef, None, [a_t, w_t, b_t], [q_t, y_t])
+    # end to end: pinned host input -> device, the network, logits -> host
+    lib = _lib.lib()
+    logits_host = torch.empty((per, model.num_classes), dtype=torch.float32).pin_memory()
+    in_bytes = x_host.numel() * 4
+    out_bytes = logits_host.numel() * 4
+    sptr = C.c_void_p(stream.cuda_stream)
     e2e_steps = max(3, min(args.steps, 20))
-    for _ in range(2):
-        be.execute(compiled, [a_t], [q_t, y_t], stream=stream.cuda_stream)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    e_start = torch.cuda.Event(enable_timing=True)
-    e_end = torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    for _ in range(e2e_steps):
-        be.execute(compiled, [a_t], [q_t, y_t], stream=stream.cuda_stream)
-    e_end.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = e_start.elapsed_time(e_end) / e2e_steps
-    te = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * OPS_PER_STEP / (float(te.item()) * 1e-3) / 1e12
-    # spot check of the e2e result against the device-resident run
-    launch()
-    torch.cuda.synchronize(dev)
-    e2e_ok = bool(torch.equal(q_host, q.cpu())) and bool(torch.equal(y_host.view(torch.int32), y.cpu().view(torch.int32)))
 
-    bf16_peak, peak_src = load_peaks()
-    int8_peak = 2.0 * bf16_peak
-    achieved = OPS_PER_STEP / (ms * 1e-3) / 1e12
+    def e2e_step():
+        _lib.check(lib.lsc_memcpy_h2d(C.c_void_p(x_dev.data_ptr()), C.c_void_p(x_host.data_ptr()), in_bytes, sptr))
+        graph.replay()
+        _lib.check(lib.lsc_memcpy_d2h(C.c_void_p(logits_host.data_ptr()), C.c_void_p(model.logits.data_ptr()),
+                                      out_bytes, sptr))
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ee.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(es.elapsed_time(ee) / e2e_steps)
+    e2e_value = GLOBAL_BATCH / (e2e_ms * 1e-3)
+    e2e_ok = bool(torch.equal(logits_host, model.logits.cpu()))
+
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "parallelism": f"replicas x{world}",
-                   "l2": "flushed (256 MiB write) before every timed launch", "seed": SEED},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
-                     "frac": achieved / int8_peak, "traffic": load_traffic(),
-                     "peak_source": f"2 x {peak_src} bf16 burst ({bf16_peak} TFLOP/s); nominal dense INT8 4500 TOPS",
-                     "frac_of_nominal": achieved / 4500.0},
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": M * K,
-                "d2h_bytes_per_step": M * N * 5, "api": "CudaBackend.execute(FullyConnected int8) host tensors",
+        "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": RESNET_WORKLOAD, "global_batch": GLOBAL_BATCH, "per_gpu_batch": per,
+                   "image": IMAGE, "parallelism": f"batch split x{world} (no collective)",
+                   "l2": "flushed (256 MiB write) before every timed step", "seed": NET_SEED},
+        "network_tops": img_ops * GLOBAL_BATCH / (ms_max * 1e-3) / 1e12,
+        "roofline": {"bound": "tensor", "kernel": "contraction_i8_kernel (INT8 implicit-GEMM conv)",
+                     "achieved": conv_tops, "peak": int8_peak, "unit": "TOPS", "frac": conv_tops / int8_peak,
+                     "traffic": load_traffic("contraction_i8_conv_resnet18.md"), "peak_source": peak_source,
+                     "conv_share_of_step": conv_ms / ms if ms > 0 else None},
+        "e2e": {"value": e2e_value, "unit": "img/s", "h2d_bytes_per_step": in_bytes * world,
+                "d2h_bytes_per_step": out_bytes * world, "api": "lsc_memcpy_h2d + network + lsc_memcpy_d2h",
                 "matches_device_run": e2e_ok},
-        "gpu_launches": args.steps,
+        "gpu_launches": model.kernel_launches() * args.steps,
         "clocks": clocks,
-        "s_out": s_out,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = run_cpu_baseline(a, w, bias, scale, s_out)
+    if rank == 0:
+        tops, gms, _ = gemm_measure(torch, dev, max(50, min(args.steps * 4, 1000)), 10)
+        line["int8_gemm_4096"] = {"value": tops, "unit": "TOPS", "ms_per_launch": gms, "workload": GEMM_WORKLOAD,
+                                  "roofline_frac": tops / int8_peak,
+                                  "traffic": load_traffic("contraction_i8_gemm_4096.md")}
+        if world == 1 and not args.no_cpu_baseline:
+            imgs = 24
+            dt, _, _ = cpu_resnet_sample(imgs, dict(model.scales))
+            line["cpu_baseline"] = {"value": imgs / dt, "unit": "img/s", "cores": os.cpu_count(), "kind": "port",
+                                    "sample": f"{imgs} images through the oracle's quantized ResNet-18 "
+                                              f"(direct int8 convolutions, OpenMP), {dt:.2f} s"}
+    del graph
+    model.graph = None
     be.close()
     if world > 1:
         dist.barrier()
@@ -337,9 +457,10 @@ def run_gpu(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["lightship", "reference"], default="lightship")
+    ap.add_argument("--workload", choices=["resnet18", "gemm"], default="resnet18")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

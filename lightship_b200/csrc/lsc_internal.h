@@ -104,6 +104,9 @@ lsc_status launch_add_f32(const float* a, const float* b, float* y, int64_t n, i
 lsc_status launch_quantize_nchw_to_nhwc_i8(const float* x, int8_t* y, int64_t n, int64_t c,
                                            int64_t hw, int64_t cp, float scale, int rounding,
                                            cudaStream_t st);
+lsc_status launch_quantize_nchw_to_s2d_i8(const float* x, int8_t* y, int64_t n, int64_t c, int64_t h,
+                                          int64_t w, int64_t ph, int64_t pw, int64_t blk, int64_t cp,
+                                          float scale, int rounding, cudaStream_t st);
 lsc_status launch_maxpool_i8(const int8_t* x, int8_t* y, int64_t n, int64_t h, int64_t w, int64_t c,
                              int64_t oh, int64_t ow, int kh, int kw, int sh, int sw, int ph, int pw,
                              cudaStream_t st);

@@ -53,6 +53,43 @@ __global__ void quantize_nchw_to_nhwc_kernel(const float* __restrict__ x, int8_t
   }
 }
 
+// Space-to-depth variant: zero-pad the NCHW input by (ph, pw), then fold each b x b block of
+// pixels into channels: out[img, y, x, (dy*b + dx)*C + c] = q(x[img, c, b*y+dy-ph, b*x+dx-pw]).
+// A stride-b convolution over the padded input equals a stride-1 convolution over this
+// tensor with the filter re-indexed the same way, so a 7x7 stride-2 stem on 3 channels becomes
+// a 4x4 stride-1 conv on 12 (stored 16) channels with contiguous, full-sector loads.
+template <int RND>
+__global__ void quantize_nchw_to_s2d_kernel(const float* __restrict__ x, int8_t* __restrict__ y,
+                                            int64_t n, int64_t c, int64_t h, int64_t w,
+                                            int64_t ph, int64_t pw, int64_t blk, int64_t hs,
+                                            int64_t ws, int64_t cp, float scale) {
+  const int64_t groups = cp / 16;
+  const int64_t total = n * hs * ws * groups;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t g = i % groups;
+    int64_t t = i / groups;
+    const int64_t xs = t % ws;
+    t /= ws;
+    const int64_t ys = t % hs;
+    const int64_t img = t / hs;
+    uint32_t wd[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int64_t ch = g * 16 + j;
+      int8_t q = 0;
+      if (ch < blk * blk * c) {
+        const int64_t cc = ch % c, blkidx = ch / c;
+        const int64_t iy = ys * blk + blkidx / blk - ph, ix = xs * blk + blkidx % blk - pw;
+        if (iy >= 0 && iy < h && ix >= 0 && ix < w)
+          q = quantize_i8<RND>(__ldg(x + ((img * c + cc) * h + iy) * w + ix), scale);
+      }
+      wd[j >> 2] |= (static_cast<uint32_t>(static_cast<uint8_t>(q))) << (8 * (j & 3));
+    }
+    reinterpret_cast<uint4*>(y + ((img * hs + ys) * ws + xs) * cp)[g] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  }
+}
+
 __device__ __forceinline__ uint32_t vmax_s8x4(uint32_t a, uint32_t b) { return __vmaxs4(a, b); }
 
 __global__ void maxpool_i8_kernel(const int8_t* __restrict__ x, int8_t* __restrict__ y, int64_t n,
@@ -130,6 +167,31 @@ lsc_status launch_quantize_nchw_to_nhwc_i8(const float* x, int8_t* y, int64_t n,
     quantize_nchw_to_nhwc_kernel<LSC_ROUND_HALF_EVEN><<<grid_p(total, ds->sm_count), 256, 0, st>>>(x, y, n, c, hw, cp, scale);
   else
     quantize_nchw_to_nhwc_kernel<LSC_ROUND_HALF_AWAY><<<grid_p(total, ds->sm_count), 256, 0, st>>>(x, y, n, c, hw, cp, scale);
+  LSC_CUDA_TRY(cudaGetLastError());
+  return LSC_SUCCESS;
+}
+
+lsc_status launch_quantize_nchw_to_s2d_i8(const float* x, int8_t* y, int64_t n, int64_t c, int64_t h,
+                                          int64_t w, int64_t ph, int64_t pw, int64_t blk, int64_t cp,
+                                          float scale, int rounding, cudaStream_t st) {
+  if (blk < 2 || ph < 0 || pw < 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "space-to-depth: bad block/padding");
+  if (cp % 16 != 0 || cp < blk * blk * c)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "space-to-depth: stored channels must be a multiple of 16 and >= %lld",
+                     (long long)(blk * blk * c));
+  if ((h + 2 * ph) % blk || (w + 2 * pw) % blk)
+    return set_error(LSC_ERROR_SHAPE_MISMATCH, "space-to-depth: padded size not divisible by the block");
+  if (reinterpret_cast<uintptr_t>(y) & 15) return set_error(LSC_ERROR_INVALID_ARGUMENT, "space-to-depth: output must be 16-byte aligned");
+  const int64_t hs = (h + 2 * ph) / blk, ws = (w + 2 * pw) / blk;
+  const int64_t total = n * hs * ws * (cp / 16);
+  if (total == 0) return LSC_SUCCESS;
+  DeviceState* ds = current_device_state();
+  if (!ds) return LSC_ERROR_DEVICE_ERROR;
+  if (rounding == LSC_ROUND_HALF_EVEN)
+    quantize_nchw_to_s2d_kernel<LSC_ROUND_HALF_EVEN><<<grid_p(total, ds->sm_count), 256, 0, st>>>(
+        x, y, n, c, h, w, ph, pw, blk, hs, ws, cp, scale);
+  else
+    quantize_nchw_to_s2d_kernel<LSC_ROUND_HALF_AWAY><<<grid_p(total, ds->sm_count), 256, 0, st>>>(
+        x, y, n, c, h, w, ph, pw, blk, hs, ws, cp, scale);
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }

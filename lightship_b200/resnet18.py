@@ -77,6 +77,27 @@ def _out_hw(h, k, s, p):
     return (h + 2 * p - k) // s + 1
 
 
+def stem_space_to_depth(spec: ConvSpec) -> ConvSpec:
+    """The stride-2 stem as a stride-1 conv over the space-to-depth input.
+
+    With the input zero-padded by `pad` and every 2x2 pixel block folded into channels
+    (channel (dy*2 + dx)*C + c), tap (r, s) = (2a + dy, 2b + dx) of the original filter moves
+    to tap (a, b), channel (dy*2 + dx)*C + c of a ceil(k/2) x ceil(k/2) filter; taps past the
+    original k are zero.  The integer sums are unchanged, and BN folding and per-channel
+    quantization see the same non-zero weights, so the result is bit-identical."""
+    co, c, k, _ = spec.w.shape
+    kk = (k + 1) // 2
+    w2 = np.zeros((co, 4 * c, kk, kk), np.float32)
+    for dy in range(2):
+        for dx in range(2):
+            for a in range(kk):
+                for b in range(kk):
+                    r, s = 2 * a + dy, 2 * b + dx
+                    if r < k and s < k:
+                        w2[:, (dy * 2 + dx) * c:(dy * 2 + dx + 1) * c, a, b] = spec.w[:, :, r, s]
+    return ConvSpec(spec.name, 4 * c, spec.cout, kk, 1, 0, spec.relu, w2, spec.bias, spec.bn)
+
+
 class ResNet18Int8:
     """The network compiled on one device; ``forward`` takes an f32 NCHW batch on that device."""
 
@@ -97,7 +118,10 @@ class ResNet18Int8:
         # static activation buffers (int8 NHWC)
         b = batch
         h = _out_hw(image, 7, 2, 3)
-        self.buf = {"x_q": torch.empty((b, image, image, STEM_CHANNELS), dtype=torch.int8, device=device),
+        # the stem runs as a stride-1 conv over the space-to-depth input (see stem_space_to_depth)
+        self.stem = stem_space_to_depth(self.convs[0])
+        hs = (image + 2 * self.convs[0].pad) // 2
+        self.buf = {"x_q": torch.empty((b, hs, hs, STEM_CHANNELS), dtype=torch.int8, device=device),
                     "conv1": torch.empty((b, h, h, 64), dtype=torch.int8, device=device)}
         hp = _out_hw(h, 3, 2, 1)
         self.buf["pool"] = torch.empty((b, hp, hp, 64), dtype=torch.int8, device=device)
@@ -167,8 +191,10 @@ class ResNet18Int8:
         qin = Tensor("xq", list(self.buf["x_q"].shape), DataType.QInt8, self.buf["x_q"],
                      layout=StorageLayout.NHWC, quantization=Quantization([s_in]))
         xt = Tensor("x", list(x_f32.shape), DataType.F32, x_f32, layout=StorageLayout.NCHW)
+        pad = self.convs[0].pad
         self.ops["quant_in"] = self.be.compile_operator(
-            OperatorDef("quantize_input", OperatorType.Quantize, rounding=self.rounding), None, [xt], [qin])
+            OperatorDef("quantize_input", OperatorType.Quantize, rounding=self.rounding, stride=(2, 2),
+                        padding=(pad, pad)), None, [xt], [qin])
         self.be.execute(self.ops["quant_in"], [xt], [qin], stream=self._stream())
 
         def layer(spec, in_name, residual=None):
@@ -180,7 +206,7 @@ class ResNet18Int8:
             self.scales[spec.name] = self._scale_of(f32.reshape(-1))
             self._run_conv(spec, in_name, in_scale, self.scales[spec.name], residual)
 
-        layer(self.convs[0], "x_q")
+        layer(self.stem, "x_q")
         self._compile_pool()
         self._run_pool()
         self.scales["pool"] = self.scales["conv1"]
@@ -242,7 +268,7 @@ class ResNet18Int8:
                      layout=StorageLayout.NHWC, quantization=Quantization([self.scales["input"]]))
         self.be.execute(self.ops["quant_in"], [xt], [qin], stream=self._stream())
         sc = self.scales
-        self._run_conv(self.convs[0], "x_q", sc["input"], sc["conv1"])
+        self._run_conv(self.stem, "x_q", sc["input"], sc["conv1"])
         self._run_pool()
         prev = "pool"
         for c1, c2, ds in self.blocks:

@@ -305,6 +305,67 @@ def conv2d_i8_nhwc_chain(x, w, bias, scale, stride=(1, 1), pad=(0, 0), dilation=
     return oi8, of32, oacc
 
 
+def resnet18_int8(x, convs, blocks, fc_w, fc_b, scales=None, rounding=ROUND_HALF_AWAY, threads=0):
+    """The quantized ResNet-18 restated with this module's functions.
+
+    x: f32 NCHW batch.  convs/blocks: the network's conv specs (name, cin, cout, k, stride,
+    pad, relu, w OIHW f32, bias, bn=(gamma, beta, mean, var)) with blocks = [(conv1, conv2,
+    downsample or None)].  With scales=None the activation scales are calibrated on this
+    batch the way a deployment calibrates them: each layer's dequantized f32 output goes
+    through find_scale_zp (symmetric, QInt8).  Returns (logits f32, scales, activations).
+    """
+    calibrate = scales is None
+    sc = {} if calibrate else dict(scales)
+    if calibrate:
+        sc["input"], _ = find_scale_zp(x, QINT8, True)
+    acts = {"x_q": quantize_nchw_to_nhwc(x, sc["input"], 16, rounding)}
+
+    def conv(spec, in_name, residual=None):
+        xin = acts[in_name]
+        s_in = sc["input"] if in_name == "x_q" else sc[in_name]
+        wf, bf = bn_fold(spec.w, spec.bias, *spec.bn)
+        wq, sw = quantize_weights_per_channel(np.ascontiguousarray(wf.transpose(0, 2, 3, 1)))
+        cs = xin.shape[3]
+        wp = np.zeros((spec.cout, spec.k, spec.k, cs), np.int8)
+        wp[..., :spec.cin] = wq
+        scale = (np.float32(s_in) * sw).astype(np.float32)
+        bq = np.array([quantize_value(float(bf[o]), float(scale[o]), 0, QINT32) for o in range(spec.cout)],
+                      np.int32)
+        res = None if residual is None else acts[residual]
+        rs = 1.0 if residual is None else sc[residual]
+        act_kind = ACT_RELU if spec.relu else ACT_NONE
+        args = (xin, wp, bq, scale, (spec.stride,) * 2, (spec.pad,) * 2, (1, 1), 1, act_kind)
+        if calibrate:
+            _, y, _ = conv2d_i8_nhwc_chain(*args, 1.0, rounding, threads, residual=res, residual_scale=rs)
+            sc[spec.name], _ = find_scale_zp(y, QINT8, True)
+        q, _, _ = conv2d_i8_nhwc_chain(*args, sc[spec.name], rounding, threads, residual=res, residual_scale=rs)
+        acts[spec.name] = q
+
+    conv(convs[0], "x_q")
+    acts["pool"] = maxpool_i8_nhwc(acts[convs[0].name], 3, 2, 1)
+    sc["pool"] = sc[convs[0].name]
+    prev = "pool"
+    for c1, c2, ds in blocks:
+        conv(c1, prev)
+        if ds is not None:
+            conv(ds, prev)
+            res = ds.name
+        else:
+            res = prev
+        conv(c2, c1.name, residual=res)
+        prev = c2.name
+    if calibrate:
+        _, pf = avgpool_i8_nhwc(acts[prev], sc[prev], 1.0, rounding)
+        sc["pooled"], _ = find_scale_zp(pf, QINT8, True)
+    pooled, _ = avgpool_i8_nhwc(acts[prev], sc[prev], sc["pooled"], rounding)
+    wq, sw = quantize_weights_per_channel(fc_w)
+    scale = (np.float32(sc["pooled"]) * sw).astype(np.float32)
+    bq = np.array([quantize_value(float(fc_b[o]), float(scale[o]), 0, QINT32) for o in range(fc_w.shape[0])],
+                  np.int32)
+    _, logits, _ = gemm_i8_chain(pooled, wq, bq, scale, ACT_NONE, 1.0, rounding, threads, want=("f32",))
+    return logits, sc, acts
+
+
 def quantize_nchw_to_nhwc(x, scale, cp, rounding=ROUND_HALF_AWAY):
     x = _c(x, np.float32)
     n, c, h, w = x.shape

@@ -81,6 +81,11 @@ def test_resnet18_int8_bit_exact(be, cuda, rounding):
     for name in ("conv1", "pool", "layer1.0.conv2", "layer2.0.downsample", "layer4.1.conv2"):
         np.testing.assert_array_equal(model.buf[name].cpu().numpy(), acts[name], err_msg=name)
     np.testing.assert_array_equal(logits.view(np.uint32), want.view(np.uint32))
+    # the oracle calibrating on its own reaches the same scales and logits
+    own_logits, own_scales, _ = orc.resnet18_int8(x, model.convs, model.blocks, model.fc_w, model.fc_b,
+                                                  None, rounding)
+    assert own_scales == model.scales
+    np.testing.assert_array_equal(own_logits.view(np.uint32), want.view(np.uint32))
     # the network is not degenerate: activations use the int8 range, logits differ per image
     assert np.abs(acts["layer4.1.conv2"]).max() >= 64
     assert not np.array_equal(logits[0], logits[1])
@@ -144,6 +149,29 @@ def test_quantize_input_to_nhwc(be):
     be.execute(op, [xt], [q])
     assert q.shape == [2, 17, 19, 16]
     np.testing.assert_array_equal(q.numpy().reshape(2, 17, 19, 16), orc.quantize_nchw_to_nhwc(x, 0.02, 16))
+
+
+def test_quantize_input_space_to_depth(be):
+    """Quantize with stride 2: pad by 3, fold 2x2 pixel blocks into channels."""
+    from lightship_b200.backend import (DataType, OperatorDef, OperatorType, Quantization, StorageLayout,
+                                        Tensor)
+    rng = np.random.default_rng(6)
+    x = rng.normal(size=(2, 3, 26, 30)).astype(np.float32)
+    hs, ws = (26 + 6) // 2, (30 + 6) // 2
+    xt = Tensor("x", list(x.shape), DataType.F32, x, layout=StorageLayout.NCHW)
+    q = Tensor("q", [2, hs, ws, 16], DataType.QInt8, np.zeros(2 * hs * ws * 16, np.int8),
+               layout=StorageLayout.NHWC, quantization=Quantization([0.03]))
+    op = be.compile_operator(OperatorDef("q", OperatorType.Quantize, stride=(2, 2), padding=(3, 3)), None, [xt], [q])
+    be.execute(op, [xt], [q])
+    assert q.shape == [2, hs, ws, 16]
+    xp = np.zeros((2, 3, 32, 36), np.float32)
+    xp[:, :, 3:29, 3:33] = x
+    qq = orc.quantize_nchw_to_nhwc(xp, 0.03, 3)  # [2, 32, 36, 3]
+    want = np.zeros((2, hs, ws, 16), np.int8)
+    for dy in range(2):
+        for dx in range(2):
+            want[..., (dy * 2 + dx) * 3:(dy * 2 + dx + 1) * 3] = qq[:, dy::2, dx::2, :]
+    np.testing.assert_array_equal(q.numpy().reshape(want.shape), want)
 
 
 def test_conv_residual_kernel_level(cuda):
