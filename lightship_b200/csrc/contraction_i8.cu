@@ -15,10 +15,11 @@
 //               double-buffered s32 accumulator in TMEM (2 x BN columns) and commits each
 //               stage back to the producer and each finished tile to the epilogue.
 //   warps 2-9   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
-//               32*(w%4)..+31, half of the tile's columns), bias, per-channel scale,
-//               activation, requantize, vectorised global stores.  The accumulator buffer is
-//               released right after its last TMEM read so the next tile's MMAs overlap
-//               this tile's epilogue math.
+//               32*(w%4)..+31 and half of the tile's columns, 32 at a time), bias,
+//               per-channel scale, activation, requantize, vectorised global stores.  The
+//               accumulator buffer is released right after its last TMEM read so the next
+//               tile's MMAs overlap this tile's epilogue math.
+#include <math.h>
 #include <stdio.h>
 
 #include <mutex>
@@ -35,6 +36,7 @@ struct I8Params {
   const int32_t* bias;
   const float* scale;
   float s_out;
+  float inv_s_out;  // RN(1 / s_out) when s_out and its reciprocal are normal floats, else 0
   int32_t rounding;
   int8_t* out_i8;
   float* out_f32;
@@ -64,112 +66,109 @@ struct I8Cfg {
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulator buffers; power of 2 >= 32
+  // EPI_WARPS epilogue warps: EPI_WARPS / 4 per TMEM lane quarter, each taking that share of
+  // the tile's columns in chunks of EPI_W
   static constexpr int EPI_WARPS = 8;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  static constexpr int COLS_PER_EPI_WARP = BN / 2;
+  static constexpr int COLS_PER_EPI_WARP = BN / (EPI_WARPS / 4);
+  static constexpr int EPI_W = 32;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+  // per epilogue warp: the scale and bias of the columns it handles in the current N tile
+  static constexpr int EPI_COL_BYTES = EPI_WARPS * COLS_PER_EPI_WARP * 8;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + EPI_COL_BYTES;
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
-  static_assert(STAGES * STAGE_BYTES + 1024 + BAR_BYTES <= 232448, "shared memory budget");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   static_assert((2 * STAGES + 5) * 8 + 8 <= BAR_BYTES, "barrier area");
 };
 
-// Epilogue for 32 consecutive columns of one output row held by this thread.
-template <int ACT>
-__device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t (&r)[32],
-                                               int row, int col0) {
+// Epilogue for W consecutive columns of one output row held by this thread; cs / cb are the
+// chunk's per-column scales and biases staged in shared memory (zero past the last column).
+// Each output is stored as soon as it is final (i32, then f32, then int8) so the
+// accumulator, f32 and int8 arrays are never live together.
+template <int ACT, int W>
+__device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t (&r)[W],
+                                               const float* cs, const int32_t* cb, int row, int col0) {
+  static_assert(W % 16 == 0, "chunks are whole 16-byte int8 vectors");
   if (row >= p.m) return;
-  const bool full = (col0 + 32 <= p.n);
+  const bool vec = (col0 + W <= p.n) && p.vec_ok;
   const int64_t base = static_cast<int64_t>(row) * p.ldo + col0;
-  int32_t acc[32];
-  float y[32];
-  if (full) {
+  int32_t acc[W];
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      int4 b = make_int4(0, 0, 0, 0);
-      if (p.bias) b = __ldg(reinterpret_cast<const int4*>(p.bias + col0 + j));
-      const float4 s = __ldg(reinterpret_cast<const float4*>(p.scale + col0 + j));
-      acc[j + 0] = static_cast<int32_t>(r[j + 0] + static_cast<uint32_t>(b.x));
-      acc[j + 1] = static_cast<int32_t>(r[j + 1] + static_cast<uint32_t>(b.y));
-      acc[j + 2] = static_cast<int32_t>(r[j + 2] + static_cast<uint32_t>(b.z));
-      acc[j + 3] = static_cast<int32_t>(r[j + 3] + static_cast<uint32_t>(b.w));
-      y[j + 0] = dequant(acc[j + 0], s.x);
-      y[j + 1] = dequant(acc[j + 1], s.y);
-      y[j + 2] = dequant(acc[j + 2], s.z);
-      y[j + 3] = dequant(acc[j + 3], s.w);
-    }
-  } else {
+  for (int j = 0; j < W; j += 4) {
+    const int4 b = *reinterpret_cast<const int4*>(cb + j);
+    acc[j + 0] = static_cast<int32_t>(r[j + 0] + static_cast<uint32_t>(b.x));
+    acc[j + 1] = static_cast<int32_t>(r[j + 1] + static_cast<uint32_t>(b.y));
+    acc[j + 2] = static_cast<int32_t>(r[j + 2] + static_cast<uint32_t>(b.z));
+    acc[j + 3] = static_cast<int32_t>(r[j + 3] + static_cast<uint32_t>(b.w));
+  }
+  if (p.out_i32) {
+    if (vec) {
+      int4* dst = reinterpret_cast<int4*>(p.out_i32 + base);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int c = col0 + j;
-      if (c < p.n) {
-        const int32_t b = p.bias ? __ldg(p.bias + c) : 0;
-        acc[j] = static_cast<int32_t>(r[j] + static_cast<uint32_t>(b));
-        y[j] = dequant(acc[j], __ldg(p.scale + c));
-      } else {
-        acc[j] = 0;
-        y[j] = 0.0f;
-      }
+      for (int j = 0; j < W / 4; ++j) dst[j] = make_int4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < W; ++j)
+        if (col0 + j < p.n) p.out_i32[base + j] = acc[j];
     }
   }
-  if (p.residual) {
-    if (full && p.vec_ok) {
-      const uint4 r0 = __ldg(reinterpret_cast<const uint4*>(p.residual + base));
-      const uint4 r1 = __ldg(reinterpret_cast<const uint4*>(p.residual + base) + 1);
-      const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+  if (!p.out_f32 && !p.out_i8) return;
+  float y[W];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int32_t q = static_cast<int8_t>((rw[j >> 2] >> (8 * (j & 3))) & 0xFFu);
-        y[j] = __fadd_rn(y[j], __fmul_rn(__int2float_rn(q), p.res_scale));
+  for (int j = 0; j < W; j += 4) {
+    const float4 s = *reinterpret_cast<const float4*>(cs + j);
+    y[j + 0] = dequant(acc[j + 0], s.x);
+    y[j + 1] = dequant(acc[j + 1], s.y);
+    y[j + 2] = dequant(acc[j + 2], s.z);
+    y[j + 3] = dequant(acc[j + 3], s.w);
+  }
+  if (p.residual) {
+    if (vec) {
+#pragma unroll
+      for (int v = 0; v < W / 16; ++v) {
+        const uint4 rv = __ldg(reinterpret_cast<const uint4*>(p.residual + base) + v);
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int32_t q = static_cast<int8_t>((rw[j >> 2] >> (8 * (j & 3))) & 0xFFu);
+          y[16 * v + j] = __fadd_rn(y[16 * v + j], __fmul_rn(__int2float_rn(q), p.res_scale));
+        }
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
+      for (int j = 0; j < W; ++j)
         if (col0 + j < p.n)
           y[j] = __fadd_rn(y[j], __fmul_rn(__int2float_rn(p.residual[base + j]), p.res_scale));
     }
   }
+  // A ReLU feeding only the int8 output is applied inside the requantization's clamp.
+  const bool relu_folded = ACT == LSC_ACT_RELU && !p.out_f32 && p.inv_s_out > 0.0f;
+  if (!relu_folded) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) y[j] = apply_act<ACT>(y[j]);
-  if (full && p.vec_ok) {
-    if (p.out_i8) {
-      uint32_t pk[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        uint32_t w = 0;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int32_t q = p.rounding == LSC_ROUND_HALF_EVEN
-                                ? requant_i8<LSC_ROUND_HALF_EVEN>(y[4 * j + t], p.s_out)
-                                : requant_i8<LSC_ROUND_HALF_AWAY>(y[4 * j + t], p.s_out);
-          w |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * t);
-        }
-        pk[j] = w;
-      }
-      uint4* dst = reinterpret_cast<uint4*>(p.out_i8 + base);
-      dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-    }
-    if (p.out_f32) {
+    for (int j = 0; j < W; ++j) y[j] = apply_act<ACT>(y[j]);
+  }
+  if (p.out_f32) {
+    if (vec) {
       float4* dst = reinterpret_cast<float4*>(p.out_f32 + base);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dst[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
-    }
-    if (p.out_i32) {
-      int4* dst = reinterpret_cast<int4*>(p.out_i32 + base);
+      for (int j = 0; j < W / 4; ++j) dst[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+    } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dst[j] = make_int4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+      for (int j = 0; j < W; ++j)
+        if (col0 + j < p.n) p.out_f32[base + j] = y[j];
     }
-  } else {
+  }
+  if (p.out_i8) {
+    uint32_t pk[W / 4];
+    requant_pack<W>(y, p.s_out, p.inv_s_out, relu_folded, p.rounding, pk);
+    if (vec) {
+      uint4* dst = reinterpret_cast<uint4*>(p.out_i8 + base);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (col0 + j >= p.n) break;
-      if (p.out_i8)
-        p.out_i8[base + j] = static_cast<int8_t>(
-            p.rounding == LSC_ROUND_HALF_EVEN ? requant_i8<LSC_ROUND_HALF_EVEN>(y[j], p.s_out)
-                                              : requant_i8<LSC_ROUND_HALF_AWAY>(y[j], p.s_out));
-      if (p.out_f32) p.out_f32[base + j] = y[j];
-      if (p.out_i32) p.out_i32[base + j] = acc[j];
+      for (int v = 0; v < W / 16; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < W; ++j)
+        if (col0 + j < p.n) p.out_i8[base + j] = static_cast<int8_t>((pk[j >> 2] >> (8 * (j & 3))) & 0xFFu);
     }
   }
 }
@@ -209,6 +208,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  uint8_t* epi_cols = smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -354,33 +354,49 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
     }
   } else {
     // --------------------------------------------------------------- epilogue
-    const int epi = warp - 2;       // 0..7
+    const int epi = warp - 2;       // 0..EPI_WARPS-1
     const int quarter = warp & 3;   // TMEM lane quarter this warp may read
-    const int half = epi >> 2;      // which half of the tile's columns
+    const int part = epi >> 2;      // which share of the tile's columns
     const int row_in_tile = quarter * 32 + lane;
+    // this warp's column scales / biases: [COLS_PER_EPI_WARP] floats then as many int32
+    float* w_scale = reinterpret_cast<float*>(epi_cols + epi * (C::COLS_PER_EPI_WARP * 8));
+    int32_t* w_bias = reinterpret_cast<int32_t*>(w_scale + C::COLS_PER_EPI_WARP);
+    int staged_nb = -1;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int mb = tile % m_tiles, nb = tile / m_tiles;
+      if (nb != staged_nb) {
+        __syncwarp();
+        for (int i = lane; i < C::COLS_PER_EPI_WARP; i += 32) {
+          const int col = nb * C::BN + part * C::COLS_PER_EPI_WARP + i;
+          w_scale[i] = col < p.n ? __ldg(p.scale + col) : 0.0f;
+          w_bias[i] = (p.bias && col < p.n) ? __ldg(p.bias + col) : 0;
+        }
+        __syncwarp();
+        staged_nb = nb;
+      }
       const int buf = local & 1;
       const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
       if (!mbar_wait(&tfull[buf], buf_phase, abort_flag, p.err)) break;
       tc_fence_after();
       const int row = mb * C::BM + row_in_tile;
-      constexpr int CHUNKS = C::COLS_PER_EPI_WARP / 32;
+      constexpr int CHUNKS = C::COLS_PER_EPI_WARP / C::EPI_W;
 #pragma unroll 1
       for (int c = 0; c < CHUNKS; ++c) {
-        const int tcol = half * C::COLS_PER_EPI_WARP + c * 32;
+        const int tcol = part * C::COLS_PER_EPI_WARP + c * C::EPI_W;
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                static_cast<uint32_t>(buf * C::BN + tcol);
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr, r);
+        uint32_t r[C::EPI_W];
+        if constexpr (C::EPI_W == 32) tmem_ld_32x32b_x32(taddr, r);
+        else tmem_ld_32x32b_x16(taddr, r);
         tmem_ld_wait();
         if (c == CHUNKS - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[buf]);
         }
-        epilogue_chunk<ACT>(p, r, row, nb * C::BN + tcol);
+        epilogue_chunk<ACT, C::EPI_W>(p, r, w_scale + c * C::EPI_W, w_bias + c * C::EPI_W, row,
+                                      nb * C::BN + tcol);
       }
     }
   }
@@ -457,6 +473,8 @@ void fill_outputs(I8Params& p, const int32_t* bias, const float* scale, float s_
   p.bias = bias;
   p.scale = scale;
   p.s_out = s_out;
+  const float inv = 1.0f / s_out;
+  p.inv_s_out = (std::isnormal(s_out) && std::isnormal(inv)) ? inv : 0.0f;
   p.rounding = rounding;
   p.out_i8 = out_i8;
   p.out_f32 = out_f32;

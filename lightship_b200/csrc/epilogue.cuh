@@ -58,6 +58,83 @@ __device__ __forceinline__ int32_t requant_i8(float y, float s_out) {
   return __float2int_rz(r);
 }
 
+// max that returns NaN when either operand is NaN (fmaxf returns the other one).
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// a and b saturated to int8 and packed: b in bits 7:0, a in bits 15:8, c's low 16 bits in
+// bits 31:16.
+__device__ __forceinline__ uint32_t pack_sat_s8(int32_t a, int32_t b, uint32_t c) {
+  uint32_t d;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// requant_i8 for W values, packed four to a word (value j in byte j%4 of pk[j/4]), without
+// the per-element IEEE division; same results.
+//
+// t = RN(y * inv_s) with inv_s = RN(1 / s_out) differs from the correctly rounded quotient
+// RN(y / s_out) by at most 1.5 * 2^-23 * |t| (to first order).  t is clamped below at `lo`
+// (-256, or 0 when a ReLU is folded in: with s_out > 0, R(max(y, 0) / s_out) =
+// max(R(y / s_out), 0)), and adding 1.5 * 2^23 rounds it to an integer held in the float's
+// low mantissa bits; the float stays positive, so its bit pattern minus that of 1.5 * 2^23 is
+// an integer ordered like t (exactly rint(t) while t < 2^22) and the saturating pack clamps
+// it to [-128, 127].  d = tc - rint(tc) is the distance to that integer, so 0.5 - |d| is the
+// distance to the nearest half-integer; when RN(|d| + |tc| * 2^-22) < 0.5 (round-to-nearest
+// is monotonic, so the unrounded sum is below 0.5 too) that distance exceeds the error above,
+// the correctly rounded quotient lies strictly on the same side of the half-integer, and it
+// rounds to the same integer in either rounding mode (the modes differ only at exact ties).
+// The other elements -- near a half-integer, |t| >= 2^21, NaN (kept by the NaN-propagating
+// clamp) -- are redone with the division: on random data a few in 10^5.  inv_s = 0 marks an
+// s_out without a normal reciprocal: then every element takes the division.  A ReLU is
+// folded only with s_out > 0.
+template <int W, int RND>
+__device__ __forceinline__ void requant_pack_rnd(const float (&y)[W], float s_out, float inv_s,
+                                                 bool relu_folded, uint32_t (&pk)[W / 4]) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  constexpr int32_t kMagicBits = 0x4B400000;
+  constexpr float kErr = 2.384185791015625e-7f;  // 2^-22
+  const float lo = relu_folded ? 0.0f : -256.0f;
+  bool slow = inv_s == 0.0f;
+#pragma unroll
+  for (int w = 0; w < W / 4; ++w) {
+    int32_t v[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float tc = fmax_nan(__fmul_rn(y[4 * w + t], inv_s), lo);
+      const float tm = __fadd_rn(tc, kMagic);
+      const float d = __fsub_rn(tc, __fsub_rn(tm, kMagic));
+      slow |= !(__fmaf_rn(fabsf(tc), kErr, fabsf(d)) < 0.5f);
+      v[t] = __float_as_int(tm) - kMagicBits;
+    }
+    pk[w] = pack_sat_s8(v[1], v[0], pack_sat_s8(v[3], v[2], 0u));
+  }
+  if (__builtin_expect(slow, 0)) {
+    const bool all = inv_s == 0.0f;
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      const float tc = fmax_nan(__fmul_rn(y[j], inv_s), lo);
+      const float d = __fsub_rn(tc, __fsub_rn(__fadd_rn(tc, kMagic), kMagic));
+      if (all || !(__fmaf_rn(fabsf(tc), kErr, fabsf(d)) < 0.5f)) {
+        const float yj = relu_folded ? act_relu(y[j]) : y[j];
+        const uint32_t q = static_cast<uint32_t>(requant_i8<RND>(yj, s_out)) & 0xFFu;
+        const int sh = 8 * (j & 3);
+        pk[j >> 2] = (pk[j >> 2] & ~(0xFFu << sh)) | (q << sh);
+      }
+    }
+  }
+}
+
+template <int W>
+__device__ __forceinline__ void requant_pack(const float (&y)[W], float s_out, float inv_s,
+                                             bool relu_folded, int rounding, uint32_t (&pk)[W / 4]) {
+  if (rounding == LSC_ROUND_HALF_EVEN) requant_pack_rnd<W, LSC_ROUND_HALF_EVEN>(y, s_out, inv_s, relu_folded, pk);
+  else requant_pack_rnd<W, LSC_ROUND_HALF_AWAY>(y, s_out, inv_s, relu_folded, pk);
+}
+
 __device__ __forceinline__ float dequant(int32_t acc, float scale) {
   return __fmul_rn(__int2float_rn(acc), scale);
 }

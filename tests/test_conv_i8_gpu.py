@@ -72,6 +72,15 @@ def test_conv_i8_non_square_filter_and_rounding(cuda):
     _conv_case(cuda, 1, 9, 20, 32, 16, 3, 1, 1, kw=1, rounding=orc.ROUND_HALF_AWAY, act=orc.ACT_RELU6)
 
 
+@pytest.mark.parametrize("n,h,w,c,co,k,p,d", [(5, 12, 10, 64, 40, 3, 1, 1), (2, 9, 14, 32, 24, 5, 2, 1),
+                                              (3, 16, 16, 16, 64, 3, 2, 2), (2, 32, 32, 128, 72, 1, 0, 1),
+                                              (1, 115, 115, 16, 64, 4, 0, 1)])
+def test_conv_i8_stride1_tiles(cuda, n, h, w, c, co, k, p, d):
+    """Stride-1 shapes whose 128-row tiles straddle output rows and images, including
+    dilation, padding and the space-to-depth stem geometry (115x115x16, 4x4)."""
+    _conv_case(cuda, n, h, w, c, co, k, 1, p, d, act=orc.ACT_RELU)
+
+
 def test_conv_i8_large_batch_ragged_tiles(cuda):
     """M = 5*13*13 = 845 output pixels: tiles straddle images and the last tile is ragged."""
     _conv_case(cuda, 5, 13, 13, 128, 256, 3, 1, 1, act=orc.ACT_RELU)

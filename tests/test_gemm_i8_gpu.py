@@ -113,3 +113,22 @@ def test_gemm_i8_full_size_4096(cuda):
     want = orc.gemm_i8_chain(a, w, b, scale, orc.ACT_NONE, s_out, orc.ROUND_HALF_EVEN)
     got = _run(cuda, a, w, b, scale, orc.ACT_NONE, s_out, orc.ROUND_HALF_EVEN)
     _compare(got, want)
+
+
+@pytest.mark.parametrize("s_out", [0.1, 0.3, 0.7, 1.1e-38, 3.0e38])
+def test_gemm_i8_requant_near_ties(cuda, s_out):
+    """s_out values with inexact reciprocals and per-channel scales s_out * {1/2, 3/2, 5/2,
+    1/3}: y / s_out lands within a few ulps of a half-integer for most odd accumulators, so
+    the reciprocal-multiply requantization must fall back to the division there.  The last
+    two s_out values (denormal reciprocal, denormal-adjacent scale) take the division for
+    every element."""
+    rng = np.random.default_rng(11)
+    a, w, b, _ = _case(rng, 256, 256, 64, bias=False)
+    a //= 16
+    w //= 16
+    mult = np.array([0.5, 1.5, 2.5, 1.0 / 3.0], np.float64)
+    scale = (np.float64(np.float32(s_out)) * mult[np.arange(256) % 4]).astype(np.float32)
+    for rounding in (orc.ROUND_HALF_AWAY, orc.ROUND_HALF_EVEN):
+        want = orc.gemm_i8_chain(a, w, None, scale, orc.ACT_RELU, s_out, rounding)
+        got = _run(cuda, a, w, None, scale, orc.ACT_RELU, s_out, rounding)
+        _compare(got, want)
