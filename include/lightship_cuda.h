@@ -183,6 +183,11 @@ typedef struct lsc_op_desc {
   float output_scale;  /* s_out of a requantized int8 output */
   int32_t output_dtype; /* dtype of outputs[0] for QGEMM / quantized Conv2d */
   int32_t kernel_h, kernel_w; /* pooling window (Pool2dConfig, operator/pooling.rs) */
+  /* Conv2d end padding relative to pad_h / pad_w: bottom = pad_h + pad_h_end_delta, right =
+     pad_w + pad_w_end_delta (0 = symmetric, as Conv2dConfig's padding; a negative total crops).
+     No counterpart in the reference: lets an INT8 input carry a row pitch padded for the
+     pixel-grouped convolution. */
+  int32_t pad_h_end_delta, pad_w_end_delta;
 } lsc_op_desc;
 
 /* Backend::allocate result (backend/memory.rs:32-45) */

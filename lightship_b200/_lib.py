@@ -71,7 +71,8 @@ class lsc_op_desc(C.Structure):
                 ("dilation_h", C.c_int32), ("dilation_w", C.c_int32), ("groups", C.c_int32),
                 ("activation", C.c_int32), ("rounding", C.c_int32), ("fp32_mode", C.c_int32),
                 ("bn_epsilon", C.c_float), ("output_scale", C.c_float), ("output_dtype", C.c_int32),
-                ("kernel_h", C.c_int32), ("kernel_w", C.c_int32)]
+                ("kernel_h", C.c_int32), ("kernel_w", C.c_int32),
+                ("pad_h_end_delta", C.c_int32), ("pad_w_end_delta", C.c_int32)]
 
 
 class lsc_memory_block(C.Structure):

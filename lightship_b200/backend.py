@@ -127,6 +127,8 @@ class OperatorDef:
     epsilon: float = 1e-5
     output_scale: float = 0.0
     kernel: tuple = (1, 1)
+    # Conv2d end (bottom, right) padding minus `padding`; no counterpart in the reference
+    padding_end_delta: tuple = (0, 0)
 
 
 @dataclass
@@ -296,6 +298,7 @@ class CudaBackend:
         d.output_scale = op_def.output_scale
         d.output_dtype = int(outputs[0].data_type) if outputs else -1
         d.kernel_h, d.kernel_w = op_def.kernel
+        d.pad_h_end_delta, d.pad_w_end_delta = op_def.padding_end_delta
         keep: list = []
         cin = (_lib.lsc_tensor * max(1, len(inputs)))(*[t._to_c(keep) for t in inputs])
         cout = (_lib.lsc_tensor * max(1, len(outputs)))(*[t._to_c(keep) for t in outputs])

@@ -125,11 +125,58 @@ lsc_status geometry_from(const lsc_op* op, const lsc_tensor& x, bool nhwc, ConvG
   g.pw = op->pw;
   g.dh = op->dh;
   g.dw = op->dw;
-  const int64_t nh = g.h + 2 * g.ph - g.dh * (g.kh - 1) - 1, nw = g.w + 2 * g.pw - g.dw * (g.kw - 1) - 1;
+  g.ph_b = op->ph_end;
+  g.pw_r = op->pw_end;
+  const int64_t nh = g.h + g.ph + g.ph_b - g.dh * (g.kh - 1) - 1;
+  const int64_t nw = g.w + g.pw + g.pw_r - g.dw * (g.kw - 1) - 1;
   if (nh < 0 || nw < 0) return set_error(LSC_ERROR_SHAPE_MISMATCH, "Conv2d: input smaller than the filter");
   g.oh = nh / g.sh + 1;
   g.ow = nw / g.sw + 1;
   return LSC_SUCCESS;
+}
+
+// Pixel grouping of a stride-1 INT8 convolution.  Output group x' (pixels G*x'..G*x'+G-1)
+// reads input columns G*x' - pw .. G*x' + G - 2 - pw + KW, i.e. input groups
+// x' - ceil(pw/G) .. x' + floor((G + KW - 2 - pw) / G): a kw_g-tap convolution over the
+// grouped view with left padding pw_g = ceil(pw/G).
+struct PixelGroup {
+  int g = 1, kw_g = 0, pw_g = 0;
+};
+
+PixelGroup pixel_group_for(int64_t g, int64_t kw, int64_t pw) {
+  PixelGroup r;
+  r.g = static_cast<int>(g);
+  r.pw_g = static_cast<int>((pw + g - 1) / g);
+  r.kw_g = static_cast<int>((g + kw - 2 - pw) / g + r.pw_g + 1);
+  return r;
+}
+
+// Largest G in {8, 4, 2} whose grouped pixel fits one 128-byte im2col request, that at most
+// doubles the MMA work (kw_g * G <= 2 * KW; the grouped filter is zero outside each output
+// pixel's own taps) and that divides the input and output widths.  1 = no grouping.
+int choose_pixel_group(const ConvGeometry& g) {
+  if (g.sw != 1 || g.dw != 1 || g.kw < 2) return 1;
+  for (int cand : {8, 4, 2}) {
+    if (cand * g.c > 128 || g.w % cand || g.ow % cand) continue;
+    const PixelGroup pg = pixel_group_for(cand, g.kw, g.pw);
+    if (pg.kw_g * cand <= 2 * g.kw) return cand;
+  }
+  return 1;
+}
+
+// The grouped view of geometry g for group G (false when the widths do not divide).
+bool grouped_geometry(const lsc_op* op, const ConvGeometry& g, ConvGeometry& gg) {
+  const int G = op->group_px;
+  if (G <= 1 || g.sw != 1 || g.dw != 1 || g.w % G || g.ow % G) return false;
+  gg = g;
+  gg.w = g.w / G;
+  gg.c = g.c * G;
+  gg.c_out = g.c_out * G;
+  gg.kw = op->kw_g;
+  gg.pw = op->pw_g;
+  gg.ow = g.ow / G;
+  gg.pw_r = gg.ow - gg.w - gg.pw + gg.kw - 1;
+  return true;
 }
 
 }  // namespace
@@ -151,6 +198,8 @@ lsc_status compile_conv(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_te
   op->sw = d.stride_w > 0 ? d.stride_w : 1;
   op->ph = d.pad_h;
   op->pw = d.pad_w;
+  op->ph_end = d.pad_h + d.pad_h_end_delta;
+  op->pw_end = d.pad_w + d.pad_w_end_delta;
   op->dh = d.dilation_h > 0 ? d.dilation_h : 1;
   op->dw = d.dilation_w > 0 ? d.dilation_w : 1;
   op->act = fusion_act(d);
@@ -175,6 +224,8 @@ lsc_status compile_conv(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_te
   lsc_status st;
   if (!int8) {
     // FP32: NCHW activations; stored channels padded to a multiple of 4
+    if (d.pad_h_end_delta != 0 || d.pad_w_end_delta != 0)
+      return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "FP32 Conv2d takes symmetric padding only");
     if (x.ndim == 4 && x.shape[1] != ci)
       return set_error(LSC_ERROR_SHAPE_MISMATCH, "Conv2d: input has %lld channels, filter expects %lld",
                        (long long)x.shape[1], (long long)ci);
@@ -229,11 +280,45 @@ lsc_status compile_conv(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_te
   if ((st = own_upload(op, qp.data(), co * taps * cs, &op->w))) return st;
   if ((st = own_upload(op, scale.data(), co * 4, &p))) return st;
   op->scale = static_cast<float*>(p);
+  std::vector<int32_t> bi;
   if (has_bias) {
-    std::vector<int32_t> bi(static_cast<size_t>(co));
+    bi.resize(static_cast<size_t>(co));
     for (int64_t o = 0; o < co; ++o) bi[o] = sat_i32(roundf(b[o] / scale[o]));
     if ((st = own_upload(op, bi.data(), co * 4, &p))) return st;
     op->bias_i32 = static_cast<int32_t*>(p);
+  }
+  // pixel-grouped filter for the compile-time input width
+  ConvGeometry g0{};
+  if ((st = geometry_from(op, x, true, g0))) return st;
+  const int G = choose_pixel_group(g0);
+  if (G > 1) {
+    const PixelGroup pg = pixel_group_for(G, op->kw, op->pw);
+    op->group_px = G;
+    op->kw_g = pg.kw_g;
+    op->pw_g = pg.pw_g;
+    const int64_t kg = op->kh * pg.kw_g * G * cs;  // grouped K per output column
+    std::vector<int8_t> wg(static_cast<size_t>(G * co * kg), 0);
+    for (int gi = 0; gi < G; ++gi)
+      for (int64_t o = 0; o < co; ++o)
+        for (int64_t ky = 0; ky < op->kh; ++ky)
+          for (int kx_g = 0; kx_g < pg.kw_g; ++kx_g)
+            for (int sp = 0; sp < G; ++sp) {
+              const int64_t kx = static_cast<int64_t>(G) * (kx_g - pg.pw_g) + sp - gi + op->pw;
+              if (kx < 0 || kx >= op->kw) continue;
+              memcpy(&wg[static_cast<size_t>((gi * co + o) * kg + ((ky * pg.kw_g + kx_g) * G + sp) * cs)],
+                     &qp[static_cast<size_t>(((o * op->kh + ky) * op->kw + kx) * cs)], static_cast<size_t>(cs));
+            }
+    if ((st = own_upload(op, wg.data(), static_cast<int64_t>(wg.size()), &op->w_grouped))) return st;
+    std::vector<float> sg(static_cast<size_t>(G * co));
+    for (int gi = 0; gi < G; ++gi) memcpy(&sg[gi * co], scale.data(), static_cast<size_t>(co) * 4);
+    if ((st = own_upload(op, sg.data(), G * co * 4, &p))) return st;
+    op->scale_grouped = static_cast<float*>(p);
+    if (has_bias) {
+      std::vector<int32_t> bg(static_cast<size_t>(G * co));
+      for (int gi = 0; gi < G; ++gi) memcpy(&bg[gi * co], bi.data(), static_cast<size_t>(co) * 4);
+      if ((st = own_upload(op, bg.data(), G * co * 4, &p))) return st;
+      op->bias_grouped = static_cast<int32_t*>(p);
+    }
   }
   op->s_out = 1.0f;
   for (int i = 0; i < n_out; ++i) {
@@ -318,6 +403,11 @@ lsc_status execute_conv(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_te
     if ((st = s.input(r, m * g.c_out, &rd))) return st;
     r_scale = r.quant.count > 0 && r.quant.scale ? r.quant.scale[0] : 1.0f;
   }
+  ConvGeometry gg{};
+  if (grouped_geometry(op, g, gg))
+    return launch_conv_i8(static_cast<const int8_t*>(xd), static_cast<const int8_t*>(op->w_grouped), gg,
+                          op->bias_grouped, op->scale_grouped, s_out, op->act, op->rounding, o_i8, o_f32, o_i32,
+                          static_cast<const int8_t*>(rd), r_scale, s.st);
   return launch_conv_i8(static_cast<const int8_t*>(xd), static_cast<const int8_t*>(op->w), g, op->bias_i32,
                         op->scale, s_out, op->act, op->rounding, o_i8, o_f32, o_i32,
                         static_cast<const int8_t*>(rd), r_scale, s.st);

@@ -276,12 +276,13 @@ lsc_status execute_quant(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_t
     if (x.ndim != 4) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Quantize to NHWC needs a 4D NCHW input");
     const int64_t nb = x.shape[0], c = x.shape[1], hw = x.shape[2] * x.shape[3];
     if (op->sh > 1) {
-      const int64_t b = op->sh, hs = (x.shape[2] + 2 * op->ph) / b, ws = (x.shape[3] + 2 * op->pw) / b;
+      const int64_t b = op->sh, hs = (x.shape[2] + op->ph + op->ph_end) / b;
+      const int64_t ws = (x.shape[3] + op->pw + op->pw_end) / b;
       if ((st = s.output(y, nb * hs * ws * op->kp, &yd))) return st;
       set_shape(y, {nb, hs, ws, op->kp});
       return launch_quantize_nchw_to_s2d_i8(static_cast<const float*>(xd), static_cast<int8_t*>(yd), nb, c,
-                                            x.shape[2], x.shape[3], op->ph, op->pw, b, op->kp, op->q_scale0,
-                                            op->rounding, s.st);
+                                            x.shape[2], x.shape[3], op->ph, op->pw, op->ph_end, op->pw_end, b,
+                                            op->kp, op->q_scale0, op->rounding, s.st);
     }
     if (c > op->kp) return set_error(LSC_ERROR_SHAPE_MISMATCH, "Quantize to NHWC: %lld channels exceed %lld", (long long)c, (long long)op->kp);
     if ((st = s.output(y, nb * hw * op->kp, &yd))) return st;
@@ -349,10 +350,13 @@ lsc_status compile_op(lsc_backend* be, lsc_op* op, const lsc_tensor* in, int n_i
         op->kp = out[0].shape[3];
         if (op->kp % 16 != 0)
           return set_error(LSC_ERROR_INVALID_ARGUMENT, "Quantize to NHWC: stored channels must be a multiple of 16");
-        // stride_h = stride_w = b > 1: space-to-depth by b after zero-padding (pad_h, pad_w)
+        // stride_h = stride_w = b > 1: space-to-depth by b after zero-padding (pad_h, pad_w
+        // before; pad + pad_end_delta after)
         op->sh = op->desc.stride_h > 1 ? op->desc.stride_h : 1;
         op->ph = op->sh > 1 ? op->desc.pad_h : 0;
         op->pw = op->sh > 1 ? op->desc.pad_w : 0;
+        op->ph_end = op->sh > 1 ? op->desc.pad_h + op->desc.pad_h_end_delta : 0;
+        op->pw_end = op->sh > 1 ? op->desc.pad_w + op->desc.pad_w_end_delta : 0;
         if (op->sh > 1 && op->desc.stride_w != op->sh)
           return set_error(LSC_ERROR_INVALID_ARGUMENT, "Quantize space-to-depth needs equal strides");
       }

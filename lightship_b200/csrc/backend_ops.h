@@ -57,6 +57,16 @@ struct lsc_op {
   // convolution geometry
   int64_t c_in = 0, kh = 1, kw = 1;
   int32_t sh = 1, sw = 1, ph = 0, pw = 0, dh = 1, dw = 1, groups = 1;
+  int32_t ph_end = 0, pw_end = 0;  // bottom / right padding
+
+  // pixel-grouped form of a stride-1 INT8 convolution (group_px > 1): the NHWC input viewed
+  // as [N, H, W/G, G*C] and the filter expanded to [G*Cout, KH, kw_g, G*C], so that each
+  // im2col request moves G pixels; output column (g, o) is pixel G*x + g, channel o, which
+  // is the NHWC output's own layout.  Used when W and OW are multiples of G at execute time.
+  int32_t group_px = 1, kw_g = 0, pw_g = 0;
+  void* w_grouped = nullptr;
+  int32_t* bias_grouped = nullptr;
+  float* scale_grouped = nullptr;
 
   // quantize / dequantize / batchnorm parameters
   int32_t qdtype = LSC_DTYPE_QINT8;

@@ -539,16 +539,17 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
   lsc_status st = check_common(m, g.c_out, act, rounding, scale, out_i8, out_f32, out_i32, "conv_i8");
   if (st) return st;
   if (g.n < 0 || g.h <= 0 || g.w <= 0 || g.c <= 0 || g.kh <= 0 || g.kw <= 0 || g.sh <= 0 ||
-      g.sw <= 0 || g.dh <= 0 || g.dw <= 0 || g.ph < 0 || g.pw < 0)
+      g.sw <= 0 || g.dh <= 0 || g.dw <= 0 || g.ph < 0 || g.pw < 0 || g.ph_b < -g.h || g.pw_r < -g.w)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "conv_i8: bad geometry");
-  if (g.oh != (g.h + 2 * g.ph - g.dh * (g.kh - 1) - 1) / g.sh + 1 ||
-      g.ow != (g.w + 2 * g.pw - g.dw * (g.kw - 1) - 1) / g.sw + 1 || g.oh <= 0 || g.ow <= 0)
+  const int64_t span_h = g.h + g.ph + g.ph_b - g.dh * (g.kh - 1) - 1;
+  const int64_t span_w = g.w + g.pw + g.pw_r - g.dw * (g.kw - 1) - 1;
+  if (span_h < 0 || span_w < 0 || g.oh != span_h / g.sh + 1 || g.ow != span_w / g.sw + 1)
     return set_error(LSC_ERROR_SHAPE_MISMATCH, "conv_i8: output size does not match the geometry");
   if (g.c % 16 != 0)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "conv_i8: stored channels must be a multiple of 16 (got %lld)",
                      (long long)g.c);
-  if (g.sh > 8 || g.sw > 8 || g.ph > 127 || g.pw > 127 ||
-      g.ph - (g.kh - 1) * g.dh < -128 || g.pw - (g.kw - 1) * g.dw < -128 ||
+  if (g.sh > 8 || g.sw > 8 || g.ph > 128 || g.pw > 128 || g.ph_b > 127 || g.pw_r > 127 ||
+      g.ph_b - (g.kh - 1) * g.dh < -128 || g.pw_r - (g.kw - 1) * g.dw < -128 ||
       (g.kh - 1) * g.dh > 65535 || (g.kw - 1) * g.dw > 65535)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "conv_i8: stride/padding/filter outside the im2col unit's range");
   if (m == 0 || g.c_out == 0) return LSC_SUCCESS;
@@ -569,8 +570,8 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
   const uint64_t strides[3] = {static_cast<uint64_t>(g.c), static_cast<uint64_t>(g.w * g.c),
                                static_cast<uint64_t>(g.h * g.w * g.c)};
   const int lower[2] = {static_cast<int>(-g.pw), static_cast<int>(-g.ph)};
-  const int upper[2] = {static_cast<int>(g.pw - (g.kw - 1) * g.dw),
-                        static_cast<int>(g.ph - (g.kh - 1) * g.dh)};
+  const int upper[2] = {static_cast<int>(g.pw_r - (g.kw - 1) * g.dw),
+                        static_cast<int>(g.ph_b - (g.kh - 1) * g.dh)};
   const uint32_t estr[4] = {1, static_cast<uint32_t>(g.sw), static_cast<uint32_t>(g.sh), 1};
   const CUtensorMapSwizzle swz = acb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                  : acb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
@@ -639,6 +640,8 @@ extern "C" lsc_status lsc_conv2d_i8_nhwc(const int8_t* x, const int8_t* w, int64
   g.pw = pw;
   g.dh = dh;
   g.dw = dw;
+  g.ph_b = ph;
+  g.pw_r = pw;
   if (sh <= 0 || sw <= 0)
     return lsc::set_error(LSC_ERROR_INVALID_ARGUMENT, "conv2d_i8: stride must be positive");
   g.oh = (h + 2 * ph - dh * (kh - 1) - 1) / sh + 1;

@@ -57,6 +57,7 @@ struct ConvGeometry {
   int64_t kh, kw;
   int64_t sh, sw, ph, pw, dh, dw;
   int64_t oh, ow;
+  int64_t ph_b, pw_r;       // bottom / right padding (= ph / pw unless asymmetric; < 0 crops)
 };
 
 // INT8 NHWC convolution as an implicit GEMM (contraction_i8.cu): x [N,H,W,C] int8,
@@ -105,8 +106,8 @@ lsc_status launch_quantize_nchw_to_nhwc_i8(const float* x, int8_t* y, int64_t n,
                                            int64_t hw, int64_t cp, float scale, int rounding,
                                            cudaStream_t st);
 lsc_status launch_quantize_nchw_to_s2d_i8(const float* x, int8_t* y, int64_t n, int64_t c, int64_t h,
-                                          int64_t w, int64_t ph, int64_t pw, int64_t blk, int64_t cp,
-                                          float scale, int rounding, cudaStream_t st);
+                                          int64_t w, int64_t ph, int64_t pw, int64_t ph_end, int64_t pw_end,
+                                          int64_t blk, int64_t cp, float scale, int rounding, cudaStream_t st);
 lsc_status launch_maxpool_i8(const int8_t* x, int8_t* y, int64_t n, int64_t h, int64_t w, int64_t c,
                              int64_t oh, int64_t ow, int kh, int kw, int sh, int sw, int ph, int pw,
                              cudaStream_t st);

@@ -172,16 +172,17 @@ lsc_status launch_quantize_nchw_to_nhwc_i8(const float* x, int8_t* y, int64_t n,
 }
 
 lsc_status launch_quantize_nchw_to_s2d_i8(const float* x, int8_t* y, int64_t n, int64_t c, int64_t h,
-                                          int64_t w, int64_t ph, int64_t pw, int64_t blk, int64_t cp,
-                                          float scale, int rounding, cudaStream_t st) {
-  if (blk < 2 || ph < 0 || pw < 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "space-to-depth: bad block/padding");
+                                          int64_t w, int64_t ph, int64_t pw, int64_t ph_end, int64_t pw_end,
+                                          int64_t blk, int64_t cp, float scale, int rounding, cudaStream_t st) {
+  if (blk < 2 || ph < 0 || pw < 0 || ph_end < 0 || pw_end < 0)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "space-to-depth: bad block/padding");
   if (cp % 16 != 0 || cp < blk * blk * c)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "space-to-depth: stored channels must be a multiple of 16 and >= %lld",
                      (long long)(blk * blk * c));
-  if ((h + 2 * ph) % blk || (w + 2 * pw) % blk)
+  if ((h + ph + ph_end) % blk || (w + pw + pw_end) % blk)
     return set_error(LSC_ERROR_SHAPE_MISMATCH, "space-to-depth: padded size not divisible by the block");
   if (reinterpret_cast<uintptr_t>(y) & 15) return set_error(LSC_ERROR_INVALID_ARGUMENT, "space-to-depth: output must be 16-byte aligned");
-  const int64_t hs = (h + 2 * ph) / blk, ws = (w + 2 * pw) / blk;
+  const int64_t hs = (h + ph + ph_end) / blk, ws = (w + pw + pw_end) / blk;
   const int64_t total = n * hs * ws * (cp / 16);
   if (total == 0) return LSC_SUCCESS;
   DeviceState* ds = current_device_state();

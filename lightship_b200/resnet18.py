@@ -121,7 +121,11 @@ class ResNet18Int8:
         # the stem runs as a stride-1 conv over the space-to-depth input (see stem_space_to_depth)
         self.stem = stem_space_to_depth(self.convs[0])
         hs = (image + 2 * self.convs[0].pad) // 2
-        self.buf = {"x_q": torch.empty((b, hs, hs, STEM_CHANNELS), dtype=torch.int8, device=device),
+        # the space-to-depth input is stored with its width rounded up to a multiple of 4 (a
+        # zero column) so the stem conv can run pixel-grouped; the stem crops it again
+        ws = (hs + 3) // 4 * 4
+        self.stem_extra_cols = ws - hs
+        self.buf = {"x_q": torch.empty((b, hs, ws, STEM_CHANNELS), dtype=torch.int8, device=device),
                     "conv1": torch.empty((b, h, h, 64), dtype=torch.int8, device=device)}
         hp = _out_hw(h, 3, 2, 1)
         self.buf["pool"] = torch.empty((b, hp, hp, 64), dtype=torch.int8, device=device)
@@ -164,8 +168,9 @@ class ResNet18Int8:
                Tensor("b", [spec.cout], DataType.F32, spec.bias)]
         ins += [Tensor(n, [spec.cout], DataType.F32, a) for n, a in zip(("gamma", "beta", "mean", "var"), spec.bn)]
         out = self._t("y", self.buf[spec.name], DataType.QInt8, 1.0)
+        crop = self.stem_extra_cols if in_name == "x_q" else 0
         opdef = OperatorDef(spec.name, OperatorType.Conv2d, stride=(spec.stride, spec.stride),
-                            padding=(spec.pad, spec.pad),
+                            padding=(spec.pad, spec.pad), padding_end_delta=(0, -crop),
                             activation=Activation.ReLU if spec.relu else Activation.NONE,
                             rounding=self.rounding, output_scale=1.0)
         return self.be.compile_operator(opdef, FusionInfo.conv_batch_norm(), ins, [out])
@@ -194,7 +199,7 @@ class ResNet18Int8:
         pad = self.convs[0].pad
         self.ops["quant_in"] = self.be.compile_operator(
             OperatorDef("quantize_input", OperatorType.Quantize, rounding=self.rounding, stride=(2, 2),
-                        padding=(pad, pad)), None, [xt], [qin])
+                        padding=(pad, pad), padding_end_delta=(0, 2 * self.stem_extra_cols)), None, [xt], [qin])
         self.be.execute(self.ops["quant_in"], [xt], [qin], stream=self._stream())
 
         def layer(spec, in_name, residual=None):
