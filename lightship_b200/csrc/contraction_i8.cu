@@ -14,11 +14,12 @@
 //   warp 1      MMA issuer: one thread issues tcgen05.mma.kind::i8 (M=128, N=BN, K=32) into a
 //               double-buffered s32 accumulator in TMEM (2 x BN columns) and commits each
 //               stage back to the producer and each finished tile to the epilogue.
-//   warps 2-9   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
-//               32*(w%4)..+31 and half of the tile's columns, 32 at a time), bias,
-//               per-channel scale, activation, requantize, vectorised global stores.  The
-//               accumulator buffer is released right after its last TMEM read so the next
-//               tile's MMAs overlap this tile's epilogue math.
+//   warps 2-17  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+31 and a quarter of the tile's columns, 16 at a time), bias,
+//               per-channel scale, activation, requantize, vectorised global stores.  Four
+//               warps per SM sub-partition keep the TMEM loads and the requantization's
+//               dependent chains overlapped.  The accumulator buffer is released right after
+//               its last TMEM read so the next tile's MMAs overlap this tile's epilogue math.
 #include <math.h>
 #include <stdio.h>
 
@@ -45,7 +46,7 @@ struct I8Params {
   int32_t vec_ok;  // 16-byte vector stores are legal for full column chunks
   uint32_t* err;
   // optional int8 residual added before the activation (same layout as the outputs):
-  // y = dequant(acc) + (f32)r * res_scale
+  // y = (f32)acc * scale + (f32)r * res_scale
   const int8_t* residual;
   float res_scale;
   // convolution (ACB > 0)
@@ -68,10 +69,10 @@ struct I8Cfg {
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulator buffers; power of 2 >= 32
   // EPI_WARPS epilogue warps: EPI_WARPS / 4 per TMEM lane quarter, each taking that share of
   // the tile's columns in chunks of EPI_W
-  static constexpr int EPI_WARPS = 8;
+  static constexpr int EPI_WARPS = 16;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int COLS_PER_EPI_WARP = BN / (EPI_WARPS / 4);
-  static constexpr int EPI_W = 32;
+  static constexpr int EPI_W = 16;
   static constexpr int BAR_BYTES = 256;
   // per epilogue warp: the scale and bias of the columns it handles in the current N tile
   static constexpr int EPI_COL_BYTES = EPI_WARPS * COLS_PER_EPI_WARP * 8;
@@ -117,10 +118,9 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
 #pragma unroll
   for (int j = 0; j < W; j += 4) {
     const float4 s = *reinterpret_cast<const float4*>(cs + j);
-    y[j + 0] = dequant(acc[j + 0], s.x);
-    y[j + 1] = dequant(acc[j + 1], s.y);
-    y[j + 2] = dequant(acc[j + 2], s.z);
-    y[j + 3] = dequant(acc[j + 3], s.w);
+    f2unpack(f2mul(f2pack(__int2float_rn(acc[j]), __int2float_rn(acc[j + 1])), f2pack(s.x, s.y)), y[j], y[j + 1]);
+    f2unpack(f2mul(f2pack(__int2float_rn(acc[j + 2]), __int2float_rn(acc[j + 3])), f2pack(s.z, s.w)), y[j + 2],
+             y[j + 3]);
   }
   if (p.residual) {
     if (vec) {

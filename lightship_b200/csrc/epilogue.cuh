@@ -73,6 +73,31 @@ __device__ __forceinline__ uint32_t pack_sat_s8(int32_t a, int32_t b, uint32_t c
   return d;
 }
 
+// two-lane f32 arithmetic (sm_100): each op rounds both lanes to nearest like its scalar form
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 // requant_i8 for W values, packed four to a word (value j in byte j%4 of pk[j/4]), without
 // the per-element IEEE division; same results.
 //
@@ -99,16 +124,24 @@ __device__ __forceinline__ void requant_pack_rnd(const float (&y)[W], float s_ou
   constexpr float kErr = 2.384185791015625e-7f;  // 2^-22
   const float lo = relu_folded ? 0.0f : -256.0f;
   bool slow = inv_s == 0.0f;
+  const uint64_t inv2 = f2pack(inv_s, inv_s), mag2 = f2pack(kMagic, kMagic);
 #pragma unroll
   for (int w = 0; w < W / 4; ++w) {
     int32_t v[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const float tc = fmax_nan(__fmul_rn(y[4 * w + t], inv_s), lo);
-      const float tm = __fadd_rn(tc, kMagic);
-      const float d = __fsub_rn(tc, __fsub_rn(tm, kMagic));
-      slow |= !(__fmaf_rn(fabsf(tc), kErr, fabsf(d)) < 0.5f);
-      v[t] = __float_as_int(tm) - kMagicBits;
+    for (int t = 0; t < 4; t += 2) {
+      float t0, t1;
+      f2unpack(f2mul(f2pack(y[4 * w + t], y[4 * w + t + 1]), inv2), t0, t1);
+      const float c0 = fmax_nan(t0, lo), c1 = fmax_nan(t1, lo);
+      const uint64_t tc2 = f2pack(c0, c1);
+      const uint64_t tm2 = f2add(tc2, mag2);
+      float d0, d1, m0, m1;
+      f2unpack(f2sub(tc2, f2sub(tm2, mag2)), d0, d1);
+      f2unpack(tm2, m0, m1);
+      slow |= !(__fmaf_rn(fabsf(c0), kErr, fabsf(d0)) < 0.5f);
+      slow |= !(__fmaf_rn(fabsf(c1), kErr, fabsf(d1)) < 0.5f);
+      v[t] = __float_as_int(m0) - kMagicBits;
+      v[t + 1] = __float_as_int(m1) - kMagicBits;
     }
     pk[w] = pack_sat_s8(v[1], v[0], pack_sat_s8(v[3], v[2], 0u));
   }
@@ -135,8 +168,5 @@ __device__ __forceinline__ void requant_pack(const float (&y)[W], float s_out, f
   else requant_pack_rnd<W, LSC_ROUND_HALF_AWAY>(y, s_out, inv_s, relu_folded, pk);
 }
 
-__device__ __forceinline__ float dequant(int32_t acc, float scale) {
-  return __fmul_rn(__int2float_rn(acc), scale);
-}
 
 }  // namespace lsc
