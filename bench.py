@@ -17,8 +17,9 @@ once on the first per-rank batch; the network then runs as one captured CUDA gra
   (``contraction_i8_kernel``).  achieved = algorithmic conv ops per image x images / summed
   conv-kernel time (events around every conv launch of one eager pass); peak = 2 x the
   measured bf16 burst peak (dense INT8 issues at twice the bf16 rate).
-* ``int8_gemm_4096`` (rank 0): the INT8 per-channel GEMM M=N=K=4096 (bias, requant int8
-  half-even + dequant f32, one fused launch) in TOPS with its own roofline fraction.
+* ``int8_gemm_4096`` (rank 0): the INT8 per-channel GEMM M=N=K=4096 with int32 bias, in TOPS
+  with its own roofline fraction: the requantized int8 output (half-even) is the value; the
+  dequantized f32 output and both outputs from one launch are listed under ``variants``.
 * ``cpu_baseline`` (rank 0, one GPU): the oracle's restatement of the same quantized network
   on the host cores (direct convolutions, OpenMP) on a bounded sample of images.
 
@@ -54,7 +55,8 @@ NET_SEED = 20260415
 DATA_SEED = 1234
 GEMM_M = GEMM_N = GEMM_K = 4096
 GEMM_OPS = 2 * GEMM_M * GEMM_N * GEMM_K
-GEMM_WORKLOAD = "int8 per-channel GEMM M=N=K=4096, int32 bias, requant int8 (half-even) + dequant f32"
+GEMM_WORKLOAD = ("int8 per-channel GEMM M=N=K=4096, int32 bias, requant int8 (half-even); dequant f32 "
+                 "variant alongside")
 RESNET_WORKLOAD = ("ResNet-18 INT8 (conv1 7x7/2, 4 BasicBlock stages 64/128/256/512, maxpool 3x3/2, "
                    "global avgpool, FC-1000), 224x224x3 input, batch 256 split over the GPUs")
 
@@ -227,7 +229,12 @@ def run_reference_gemm(args):
 
 # --------------------------------------------------------------------------- GPU side
 def gemm_measure(torch, dev, steps, warmup):
-    """The 4096^3 INT8 chain on this device: (TOPS, ms per launch, s_out)."""
+    """The 4096^3 INT8 chain on this device, timed per output variant.
+
+    Returns {variant: (TOPS, ms per launch)} for "i8" (bias + requantized int8, half-even:
+    the headline), "f32" (bias + dequantized f32) and "i8+f32" (both from one launch), plus
+    the calibrated s_out.  Every timed launch follows an L2 flush (256 MiB write); the launches
+    are queued behind a short device sleep so host-side launch latency is not timed."""
     from lightship_b200 import _lib
     lib = _lib.lib()
     stream = torch.cuda.current_stream(dev)
@@ -240,29 +247,31 @@ def gemm_measure(torch, dev, steps, warmup):
     ws = torch.zeros(4, dtype=torch.int32, device=dev)
     s_dev = torch.empty(1, dtype=torch.float32, device=dev)
     z_dev = torch.empty(1, dtype=torch.int32, device=dev)
-    P = lambda t: C.c_void_p(t.data_ptr())
+    P = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None
     _lib.check(lib.lsc_gemm_i8(P(ta), P(tw), GEMM_M, GEMM_N, GEMM_K, P(tb), P(ts), 1.0, 0, 1, None, P(y), None, sptr))
     _lib.check(lib.lsc_find_scale_zp_f32(P(y), GEMM_M * GEMM_N, 9, 1, P(ws), 16, P(s_dev), P(z_dev), sptr))
     s_out = float(s_dev.item())
-
-    def launch():
-        _lib.check(lib.lsc_gemm_i8(P(ta), P(tw), GEMM_M, GEMM_N, GEMM_K, P(tb), P(ts), s_out, 0, 1, P(q), P(y),
-                                   None, sptr))
-
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    for _ in range(warmup):
-        flush.zero_()
-        launch()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    torch.cuda.synchronize(dev)
-    for s, e in ev:
-        flush.zero_()
-        s.record(stream)
-        launch()
-        e.record(stream)
-    torch.cuda.synchronize(dev)
-    ms = float(np.mean([s.elapsed_time(e) for s, e in ev]))
-    return GEMM_OPS / (ms * 1e-3) / 1e12, ms, s_out
+    res = {}
+    for name, oq, oy in (("i8", q, None), ("f32", None, y), ("i8+f32", q, y)):
+        def launch():
+            _lib.check(lib.lsc_gemm_i8(P(ta), P(tw), GEMM_M, GEMM_N, GEMM_K, P(tb), P(ts), s_out, 0, 1, P(oq), P(oy),
+                                       None, sptr))
+        for _ in range(warmup):
+            flush.zero_()
+            launch()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        torch.cuda.synchronize(dev)
+        torch.cuda._sleep(20_000_000)
+        for s, e in ev:
+            flush.zero_()
+            s.record(stream)
+            launch()
+            e.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = float(np.mean([s.elapsed_time(e) for s, e in ev]))
+        res[name] = (GEMM_OPS / (ms * 1e-3) / 1e12, ms)
+    return res, s_out
 
 
 def run_gpu(args):
@@ -302,7 +311,8 @@ def run_gpu(args):
         sampler = ClockSampler(uuid)
         sampler.start()
         barrier()
-        tops, ms, s_out = gemm_measure(torch, dev, args.steps, args.warmup)
+        variants, s_out = gemm_measure(torch, dev, args.steps, args.warmup)
+        tops, ms = variants["i8"]
         barrier()
         clocks = sampler.stop()
         ms_max = max_over_ranks(ms)
@@ -315,7 +325,9 @@ def run_gpu(args):
                 "roofline": {"bound": "tensor", "achieved": tops, "peak": int8_peak, "unit": "TOPS",
                              "frac": tops / int8_peak, "traffic": load_traffic("contraction_i8_gemm_4096.md"),
                              "peak_source": peak_source},
-                "gpu_launches": args.steps, "clocks": clocks}
+                "variants": {k: {"TOPS": v[0], "ms_per_launch": v[1], "roofline_frac": v[0] / int8_peak}
+                             for k, v in variants.items()},
+                "gpu_launches": 3 * args.steps, "clocks": clocks}
         if world > 1:
             dist.destroy_process_group()
         if rank == 0:
@@ -325,12 +337,13 @@ def run_gpu(args):
     # ------------------------------------------------------------------ ResNet-18 INT8
     from lightship_b200.backend import CudaBackend, GpuBackendConfig
     from lightship_b200.resnet18 import ResNet18Int8
-    if GLOBAL_BATCH % world:
-        raise SystemExit(f"batch {GLOBAL_BATCH} does not split over {world} GPUs")
-    per = GLOBAL_BATCH // world
+    batch = args.batch
+    if batch % world:
+        raise SystemExit(f"batch {batch} does not split over {world} GPUs")
+    per = batch // world
     # the global batch is seeded; each rank takes its contiguous shard
     rng = np.random.default_rng(DATA_SEED)
-    x_all = rng.normal(size=(GLOBAL_BATCH, 3, IMAGE, IMAGE)).astype(np.float32)
+    x_all = rng.normal(size=(batch, 3, IMAGE, IMAGE)).astype(np.float32)
     x_host = torch.from_numpy(x_all[rank * per:(rank + 1) * per]).pin_memory()
     del x_all
     be = CudaBackend(GpuBackendConfig(device_id=local, arena_bytes=256 << 20))
@@ -355,6 +368,9 @@ def run_gpu(args):
 
     model._run_conv = timed_conv
     for _ in range(3):
+        # queue the pass behind a device sleep so the events time the kernels, not host launches
+        torch.cuda.synchronize(dev)
+        torch.cuda._sleep(20_000_000)
         model.forward(x_dev)
     torch.cuda.synchronize(dev)
     model._run_conv = orig_run_conv
@@ -384,7 +400,7 @@ def run_gpu(args):
     ops.check_device()
     ms = float(np.mean([s.elapsed_time(e) for s, e in ev]))
     ms_max = max_over_ranks(ms)
-    value = GLOBAL_BATCH / (ms_max * 1e-3)
+    value = batch / (ms_max * 1e-3)
 
     # end to end: pinned host input -> device, the network, logits -> host
     lib = _lib.lib()
@@ -411,17 +427,17 @@ def run_gpu(args):
     ee.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(es.elapsed_time(ee) / e2e_steps)
-    e2e_value = GLOBAL_BATCH / (e2e_ms * 1e-3)
+    e2e_value = batch / (e2e_ms * 1e-3)
     e2e_ok = bool(torch.equal(logits_host, model.logits.cpu()))
 
     line = {
         "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": RESNET_WORKLOAD, "global_batch": GLOBAL_BATCH, "per_gpu_batch": per,
+        "config": {"workload": RESNET_WORKLOAD, "global_batch": batch, "per_gpu_batch": per,
                    "image": IMAGE, "parallelism": f"batch split x{world} (no collective)",
                    "l2": "flushed (256 MiB write) before every timed step", "seed": NET_SEED},
-        "network_tops": img_ops * GLOBAL_BATCH / (ms_max * 1e-3) / 1e12,
+        "network_tops": img_ops * batch / (ms_max * 1e-3) / 1e12,
         "roofline": {"bound": "tensor", "kernel": "contraction_i8_kernel (INT8 implicit-GEMM conv)",
                      "achieved": conv_tops, "peak": int8_peak, "unit": "TOPS", "frac": conv_tops / int8_peak,
                      "traffic": load_traffic("contraction_i8_conv_resnet18.md"), "peak_source": peak_source,
@@ -432,11 +448,15 @@ def run_gpu(args):
         "gpu_launches": model.kernel_launches() * args.steps,
         "clocks": clocks,
     }
-    if rank == 0:
-        tops, gms, _ = gemm_measure(torch, dev, max(50, min(args.steps * 4, 1000)), 10)
+    if rank == 0 and not args.no_gemm:
+        variants, _ = gemm_measure(torch, dev, max(50, min(args.steps, 200)), 10)
+        tops, gms = variants["i8"]
         line["int8_gemm_4096"] = {"value": tops, "unit": "TOPS", "ms_per_launch": gms, "workload": GEMM_WORKLOAD,
                                   "roofline_frac": tops / int8_peak,
-                                  "traffic": load_traffic("contraction_i8_gemm_4096.md")}
+                                  "traffic": load_traffic("contraction_i8_gemm_4096.md"),
+                                  "variants": {k: {"TOPS": v[0], "ms_per_launch": v[1],
+                                                   "roofline_frac": v[0] / int8_peak} for k, v in variants.items()}}
+    if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             imgs = 24
             dt, _, _ = cpu_resnet_sample(imgs, dict(model.scales))
@@ -462,6 +482,9 @@ def main():
     ap.add_argument("--impl", choices=["lightship", "reference"], default="lightship")
     ap.add_argument("--workload", choices=["resnet18", "gemm"], default="resnet18")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=GLOBAL_BATCH,
+                    help="global ResNet batch (default 256, the benchmark's; smaller only for profiling)")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the 4096^3 GEMM sub-measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -448,11 +448,17 @@ lsc_status launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const
 }
 
 // Column tile width: the widest tile that does not waste most of its columns.
-int pick_bn(int64_t n) {
-  if (n <= 64) return 64;
-  if (n <= 128) return 128;
-  if (n % 256 == 0 || n % 128 != 0) return 256;
-  return 128;
+// Column-tile width: the widest of 256/128/64 that does not waste a partial tile, narrowed
+// while the grid would leave most SMs idle (small M, e.g. a classifier layer).
+int pick_bn(int64_t m, int64_t n, int sm_count) {
+  int bn;
+  if (n <= 64) bn = 64;
+  else if (n <= 128) bn = 128;
+  else if (n % 256 == 0 || n % 128 != 0) bn = 256;
+  else bn = 128;
+  const int64_t m_tiles = (m + 127) / 128;
+  while (bn > 64 && m_tiles * ((n + bn - 1) / bn) * 2 <= sm_count) bn /= 2;
+  return bn;
 }
 
 lsc_status check_common(int64_t m, int64_t n, int act, int rounding, const float* scale,
@@ -514,7 +520,7 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
                      "gemm_i8: needs an sm_100 (B200) device, found sm_%d%d", ds->cc_major,
                      ds->cc_minor);
 
-  const int bn = pick_bn(n);
+  const int bn = pick_bn(m, n, ds->sm_count);
   CUtensorMap ta, tw;
   st = encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, m, k, 128, 128,
                       CU_TENSOR_MAP_SWIZZLE_128B);
@@ -581,7 +587,7 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
   st = encode_tmap_im2col(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, x, dims, strides, lower, upper,
                           static_cast<uint32_t>(acb), 128, estr, swz);
   if (st) return st;
-  const int bn = pick_bn(g.c_out);
+  const int bn = pick_bn(m, g.c_out, ds->sm_count);
   st = encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, static_cast<uint64_t>(k),
                       static_cast<uint64_t>(g.c_out), static_cast<uint64_t>(k), 128, bn,
                       CU_TENSOR_MAP_SWIZZLE_128B);

@@ -161,6 +161,23 @@ __device__ __forceinline__ void requant_pack_rnd(const float (&y)[W], float s_ou
   }
 }
 
+// One value of requant_pack_rnd: the same reciprocal form and exactness test, with the
+// division taken inline when the test fails.  Returns the int8 code in [-128, 127].
+template <int RND>
+__device__ __forceinline__ int32_t requant_one(float y, float s_out, float inv_s) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  constexpr int32_t kMagicBits = 0x4B400000;
+  constexpr float kErr = 2.384185791015625e-7f;  // 2^-22
+  const float tc = fmax_nan(__fmul_rn(y, inv_s), -256.0f);
+  const float tm = __fadd_rn(tc, kMagic);
+  const float d = __fsub_rn(tc, __fsub_rn(tm, kMagic));
+  if (inv_s != 0.0f && __fmaf_rn(fabsf(tc), kErr, fabsf(d)) < 0.5f) {
+    const int32_t v = __float_as_int(tm) - kMagicBits;
+    return v < -128 ? -128 : (v > 127 ? 127 : v);
+  }
+  return requant_i8<RND>(y, s_out);
+}
+
 template <int W>
 __device__ __forceinline__ void requant_pack(const float (&y)[W], float s_out, float inv_s,
                                              bool relu_folded, int rounding, uint32_t (&pk)[W / 4]) {

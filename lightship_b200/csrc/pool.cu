@@ -7,6 +7,10 @@
 //   global average pool     GlobalAvgPool2d (operator/pooling.rs:457-530):
 //                           y = ((f32)sum(q) * s_in) / (H*W), then requantized or kept f32
 // All HBM-bound: 16 channels (16 bytes) per thread, grids a multiple of the SM count.
+#include <math.h>
+
+#include <cmath>
+
 #include "epilogue.cuh"
 #include "lsc_internal.h"
 
@@ -29,27 +33,28 @@ __device__ __forceinline__ int8_t quantize_i8(float v, float s) {
   return static_cast<int8_t>(q);
 }
 
-// one thread per (image, pixel, 16-channel group); reads 16 NCHW planes (strided), writes 16 B
+// grid (pixel blocks, image): one thread per (pixel, 16-channel group), pixel-major so a
+// warp's reads of one NCHW plane are consecutive floats; writes 16 B.  32-bit index math
+// within an image (the launcher checks the image size).
 template <int RND>
 __global__ void quantize_nchw_to_nhwc_kernel(const float* __restrict__ x, int8_t* __restrict__ y,
-                                             int64_t n, int64_t c, int64_t hw, int64_t cp,
-                                             float scale) {
-  const int64_t groups = cp / 16;
-  const int64_t total = n * hw * groups;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t g = i % groups;
-    const int64_t pix = (i / groups) % hw;
-    const int64_t img = i / (groups * hw);
+                                             int c, int hw, int cp, float scale, float inv_s) {
+  const int groups = cp >> 4;
+  const int img = blockIdx.y;
+  const float* xi = x + static_cast<size_t>(img) * c * hw;
+  int8_t* yi = y + static_cast<size_t>(img) * hw * cp;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hw * groups; i += gridDim.x * blockDim.x) {
+    const int pix = i % hw;
+    const int g = i / hw;
     uint32_t w[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      const int64_t ch = g * 16 + j;
+      const int ch = g * 16 + j;
       int8_t q = 0;
-      if (ch < c) q = quantize_i8<RND>(__ldg(x + (img * c + ch) * hw + pix), scale);
+      if (ch < c) q = static_cast<int8_t>(requant_one<RND>(__ldg(xi + static_cast<size_t>(ch) * hw + pix), scale, inv_s));
       w[j >> 2] |= (static_cast<uint32_t>(static_cast<uint8_t>(q))) << (8 * (j & 3));
     }
-    reinterpret_cast<uint4*>(y + (img * hw + pix) * cp)[g] = make_uint4(w[0], w[1], w[2], w[3]);
+    reinterpret_cast<uint4*>(yi + static_cast<size_t>(pix) * cp)[g] = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -58,69 +63,110 @@ __global__ void quantize_nchw_to_nhwc_kernel(const float* __restrict__ x, int8_t
 // A stride-b convolution over the padded input equals a stride-1 convolution over this
 // tensor with the filter re-indexed the same way, so a 7x7 stride-2 stem on 3 channels becomes
 // a 4x4 stride-1 conv on 12 (stored 16) channels with contiguous, full-sector loads.
+// grid (column blocks, output row, image): one thread per (output column, 16-channel group).
 template <int RND>
 __global__ void quantize_nchw_to_s2d_kernel(const float* __restrict__ x, int8_t* __restrict__ y,
-                                            int64_t n, int64_t c, int64_t h, int64_t w,
-                                            int64_t ph, int64_t pw, int64_t blk, int64_t hs,
-                                            int64_t ws, int64_t cp, float scale) {
-  const int64_t groups = cp / 16;
-  const int64_t total = n * hs * ws * groups;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t g = i % groups;
-    int64_t t = i / groups;
-    const int64_t xs = t % ws;
-    t /= ws;
-    const int64_t ys = t % hs;
-    const int64_t img = t / hs;
-    uint32_t wd[4] = {0, 0, 0, 0};
+                                            int c, int h, int w, int ph, int pw, int blk, int hs,
+                                            int ws, int cp, float scale, float inv_s) {
+  const int groups = cp >> 4;
+  const int ys = blockIdx.y, img = blockIdx.z;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= ws * groups) return;
+  const int g = i % groups;
+  const int xs = i / groups;
+  const float* xi = x + static_cast<size_t>(img) * c * h * w;
+  // channel g*16 + j is input channel cc of block position (dy, dx) (channel = (dy*blk + dx)*C + cc)
+  const int bi0 = (g * 16) / c;
+  int cc = g * 16 - bi0 * c, dy = bi0 / blk, dx = bi0 - dy * blk;
+  uint32_t wd[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int64_t ch = g * 16 + j;
-      int8_t q = 0;
-      if (ch < blk * blk * c) {
-        const int64_t cc = ch % c, blkidx = ch / c;
-        const int64_t iy = ys * blk + blkidx / blk - ph, ix = xs * blk + blkidx % blk - pw;
-        if (iy >= 0 && iy < h && ix >= 0 && ix < w)
-          q = quantize_i8<RND>(__ldg(x + ((img * c + cc) * h + iy) * w + ix), scale);
-      }
-      wd[j >> 2] |= (static_cast<uint32_t>(static_cast<uint8_t>(q))) << (8 * (j & 3));
+  for (int j = 0; j < 16; ++j) {
+    int8_t q = 0;
+    if (dy < blk) {
+      const int iy = ys * blk + dy - ph, ix = xs * blk + dx - pw;
+      if (iy >= 0 && iy < h && ix >= 0 && ix < w)
+        q = static_cast<int8_t>(requant_one<RND>(__ldg(xi + (static_cast<size_t>(cc) * h + iy) * w + ix), scale, inv_s));
     }
-    reinterpret_cast<uint4*>(y + ((img * hs + ys) * ws + xs) * cp)[g] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    wd[j >> 2] |= (static_cast<uint32_t>(static_cast<uint8_t>(q))) << (8 * (j & 3));
+    if (++cc == c) {
+      cc = 0;
+      if (++dx == blk) {
+        dx = 0;
+        ++dy;
+      }
+    }
   }
+  reinterpret_cast<uint4*>(y + ((static_cast<size_t>(img) * hs + ys) * ws + xs) * cp)[g] =
+      make_uint4(wd[0], wd[1], wd[2], wd[3]);
+}
+
+// The same for the CNN stem's case, C = 3 input channels, 2x2 blocks, 16 stored channels:
+// everything but the pixel position is a compile-time constant.
+template <int RND>
+__global__ void quantize_nchw_to_s2d_c3b2_kernel(const float* __restrict__ x, int8_t* __restrict__ y,
+                                                 int h, int w, int ph, int pw, int hs, int ws,
+                                                 float scale, float inv_s) {
+  const int ys = blockIdx.y, img = blockIdx.z;
+  const int xs = blockIdx.x * blockDim.x + threadIdx.x;
+  if (xs >= ws) return;
+  const int plane = h * w;
+  const float* xi = x + static_cast<size_t>(img) * 3 * plane;
+  uint32_t wd[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int dy = 0; dy < 2; ++dy) {
+    const int iy = ys * 2 + dy - ph;
+    const bool row_ok = iy >= 0 && iy < h;
+#pragma unroll
+    for (int dx = 0; dx < 2; ++dx) {
+      const int ix = xs * 2 + dx - pw;
+      if (row_ok && ix >= 0 && ix < w) {
+        const float* px = xi + iy * w + ix;
+#pragma unroll
+        for (int cc = 0; cc < 3; ++cc) {
+          const int j = (dy * 2 + dx) * 3 + cc;
+          const int32_t q = requant_one<RND>(__ldg(px + cc * plane), scale, inv_s);
+          wd[j >> 2] |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * (j & 3));
+        }
+      }
+    }
+  }
+  reinterpret_cast<uint4*>(y + ((static_cast<size_t>(img) * hs + ys) * ws + xs) * 16)[0] =
+      make_uint4(wd[0], wd[1], wd[2], wd[3]);
 }
 
 __device__ __forceinline__ uint32_t vmax_s8x4(uint32_t a, uint32_t b) { return __vmaxs4(a, b); }
 
-__global__ void maxpool_i8_kernel(const int8_t* __restrict__ x, int8_t* __restrict__ y, int64_t n,
-                                  int64_t h, int64_t w, int64_t c, int64_t oh, int64_t ow, int kh,
-                                  int kw, int sh, int sw, int ph, int pw) {
-  const int64_t groups = c / 16;
-  const int64_t total = n * oh * ow * groups;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t g = i % groups;
-    int64_t t = i / groups;
-    const int64_t ox = t % ow;
-    t /= ow;
-    const int64_t oy = t % oh;
-    const int64_t img = t / oh;
-    uint4 m = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);  // -128 x 16
-    for (int r = 0; r < kh; ++r) {
-      const int64_t iy = oy * sh - ph + r;
-      if (iy < 0 || iy >= h) continue;
-      for (int s = 0; s < kw; ++s) {
-        const int64_t ix = ox * sw - pw + s;
-        if (ix < 0 || ix >= w) continue;
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + ((img * h + iy) * w + ix) * c) + g);
-        m.x = vmax_s8x4(m.x, v.x);
-        m.y = vmax_s8x4(m.y, v.y);
-        m.z = vmax_s8x4(m.z, v.z);
-        m.w = vmax_s8x4(m.w, v.w);
-      }
+// grid (column blocks, output row, image): one thread per (output column, 16-channel group),
+// group-major so a warp's 16-byte loads of one tap are contiguous.  KH/KW > 0 fix the window
+// at compile time (3x3 and 2x2); 0 takes it from kh/kw.
+template <int KH, int KW>
+__global__ void maxpool_i8_kernel(const int8_t* __restrict__ x, int8_t* __restrict__ y, int h, int w,
+                                  int c, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw) {
+  const int groups = c >> 4;
+  const int oy = blockIdx.y, img = blockIdx.z;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= ow * groups) return;
+  const int g = i % groups;
+  const int ox = i / groups;
+  const int nh = KH > 0 ? KH : kh, nw = KW > 0 ? KW : kw;
+  const uint4* xi = reinterpret_cast<const uint4*>(x + static_cast<size_t>(img) * h * w * c) + g;
+  uint4 m = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);  // -128 x 16
+#pragma unroll
+  for (int r = 0; r < nh; ++r) {
+    const int iy = oy * sh - ph + r;
+    if (iy < 0 || iy >= h) continue;
+#pragma unroll
+    for (int s = 0; s < nw; ++s) {
+      const int ix = ox * sw - pw + s;
+      if (ix < 0 || ix >= w) continue;
+      const uint4 v = __ldg(xi + (iy * w + ix) * groups);
+      m.x = vmax_s8x4(m.x, v.x);
+      m.y = vmax_s8x4(m.y, v.y);
+      m.z = vmax_s8x4(m.z, v.z);
+      m.w = vmax_s8x4(m.w, v.w);
     }
-    reinterpret_cast<uint4*>(y + ((img * oh + oy) * ow + ox) * c)[g] = m;
   }
+  reinterpret_cast<uint4*>(y + ((static_cast<size_t>(img) * oh + oy) * ow + ox) * c)[g] = m;
 }
 
 // one warp per (image, 32-channel slab): lanes own channels, loop over pixels
@@ -144,6 +190,13 @@ __global__ void avgpool_i8_kernel(const int8_t* __restrict__ x, int64_t n, int64
   }
 }
 
+// RN(1 / s) when s and its reciprocal are normal floats (the reciprocal requantization's
+// precondition), else 0, which makes every element take the division.
+float reciprocal_or_zero(float s) {
+  const float inv = 1.0f / s;
+  return (std::isnormal(s) && std::isnormal(inv)) ? inv : 0.0f;
+}
+
 int grid_p(int64_t n, int sm_count) {
   int64_t g = (n + 255) / 256;
   const int64_t cap = static_cast<int64_t>(sm_count) * 8;
@@ -159,14 +212,23 @@ lsc_status launch_quantize_nchw_to_nhwc_i8(const float* x, int8_t* y, int64_t n,
   if (cp % 16 != 0 || cp < c)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "quantize NCHW->NHWC: stored channels must be a multiple of 16 and >= C");
   if (reinterpret_cast<uintptr_t>(y) & 15) return set_error(LSC_ERROR_INVALID_ARGUMENT, "quantize NCHW->NHWC: output must be 16-byte aligned");
-  const int64_t total = n * hw * (cp / 16);
-  if (total == 0) return LSC_SUCCESS;
+  const int64_t per_img = hw * (cp / 16);
+  if (n == 0 || per_img == 0) return LSC_SUCCESS;
+  if (n > 65535 || hw * cp > INT32_MAX || c * hw > INT32_MAX)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "quantize NCHW->NHWC: batch or image too large");
   DeviceState* ds = current_device_state();
   if (!ds) return LSC_ERROR_DEVICE_ERROR;
+  const float inv_s = reciprocal_or_zero(scale);
+  int64_t bx = (per_img + 255) / 256;
+  const int64_t cap = (static_cast<int64_t>(ds->sm_count) * 8 + n - 1) / n;
+  if (bx > cap) bx = cap;
+  const dim3 grid(static_cast<unsigned>(bx < 1 ? 1 : bx), static_cast<unsigned>(n));
   if (rounding == LSC_ROUND_HALF_EVEN)
-    quantize_nchw_to_nhwc_kernel<LSC_ROUND_HALF_EVEN><<<grid_p(total, ds->sm_count), 256, 0, st>>>(x, y, n, c, hw, cp, scale);
+    quantize_nchw_to_nhwc_kernel<LSC_ROUND_HALF_EVEN><<<grid, 256, 0, st>>>(x, y, static_cast<int>(c), static_cast<int>(hw),
+                                                                           static_cast<int>(cp), scale, inv_s);
   else
-    quantize_nchw_to_nhwc_kernel<LSC_ROUND_HALF_AWAY><<<grid_p(total, ds->sm_count), 256, 0, st>>>(x, y, n, c, hw, cp, scale);
+    quantize_nchw_to_nhwc_kernel<LSC_ROUND_HALF_AWAY><<<grid, 256, 0, st>>>(x, y, static_cast<int>(c), static_cast<int>(hw),
+                                                                           static_cast<int>(cp), scale, inv_s);
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }
@@ -183,16 +245,34 @@ lsc_status launch_quantize_nchw_to_s2d_i8(const float* x, int8_t* y, int64_t n, 
     return set_error(LSC_ERROR_SHAPE_MISMATCH, "space-to-depth: padded size not divisible by the block");
   if (reinterpret_cast<uintptr_t>(y) & 15) return set_error(LSC_ERROR_INVALID_ARGUMENT, "space-to-depth: output must be 16-byte aligned");
   const int64_t hs = (h + ph + ph_end) / blk, ws = (w + pw + pw_end) / blk;
-  const int64_t total = n * hs * ws * (cp / 16);
-  if (total == 0) return LSC_SUCCESS;
-  DeviceState* ds = current_device_state();
-  if (!ds) return LSC_ERROR_DEVICE_ERROR;
+  const int64_t per_row = ws * (cp / 16);
+  if (n == 0 || hs == 0 || per_row == 0) return LSC_SUCCESS;
+  if (n > 65535 || hs > 65535 || c * h * w > INT32_MAX || ws * cp > INT32_MAX || blk > 64)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "space-to-depth: batch or image too large");
+  const dim3 grid(static_cast<unsigned>((per_row + 127) / 128), static_cast<unsigned>(hs), static_cast<unsigned>(n));
+  const int ic = static_cast<int>(c), ih = static_cast<int>(h), iw = static_cast<int>(w);
+  const float inv_s = reciprocal_or_zero(scale);
+  if (c == 3 && blk == 2 && cp == 16) {
+    const dim3 g2(static_cast<unsigned>((ws + 127) / 128), static_cast<unsigned>(hs), static_cast<unsigned>(n));
+    if (rounding == LSC_ROUND_HALF_EVEN)
+      quantize_nchw_to_s2d_c3b2_kernel<LSC_ROUND_HALF_EVEN><<<g2, 128, 0, st>>>(
+          x, y, ih, iw, static_cast<int>(ph), static_cast<int>(pw), static_cast<int>(hs), static_cast<int>(ws), scale,
+          inv_s);
+    else
+      quantize_nchw_to_s2d_c3b2_kernel<LSC_ROUND_HALF_AWAY><<<g2, 128, 0, st>>>(
+          x, y, ih, iw, static_cast<int>(ph), static_cast<int>(pw), static_cast<int>(hs), static_cast<int>(ws), scale,
+          inv_s);
+    LSC_CUDA_TRY(cudaGetLastError());
+    return LSC_SUCCESS;
+  }
   if (rounding == LSC_ROUND_HALF_EVEN)
-    quantize_nchw_to_s2d_kernel<LSC_ROUND_HALF_EVEN><<<grid_p(total, ds->sm_count), 256, 0, st>>>(
-        x, y, n, c, h, w, ph, pw, blk, hs, ws, cp, scale);
+    quantize_nchw_to_s2d_kernel<LSC_ROUND_HALF_EVEN><<<grid, 128, 0, st>>>(
+        x, y, ic, ih, iw, static_cast<int>(ph), static_cast<int>(pw), static_cast<int>(blk), static_cast<int>(hs),
+        static_cast<int>(ws), static_cast<int>(cp), scale, inv_s);
   else
-    quantize_nchw_to_s2d_kernel<LSC_ROUND_HALF_AWAY><<<grid_p(total, ds->sm_count), 256, 0, st>>>(
-        x, y, n, c, h, w, ph, pw, blk, hs, ws, cp, scale);
+    quantize_nchw_to_s2d_kernel<LSC_ROUND_HALF_AWAY><<<grid, 128, 0, st>>>(
+        x, y, ic, ih, iw, static_cast<int>(ph), static_cast<int>(pw), static_cast<int>(blk), static_cast<int>(hs),
+        static_cast<int>(ws), static_cast<int>(cp), scale, inv_s);
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }
@@ -203,11 +283,19 @@ lsc_status launch_maxpool_i8(const int8_t* x, int8_t* y, int64_t n, int64_t h, i
   if (c % 16 != 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "maxpool: channels must be a multiple of 16");
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "maxpool: tensors must be 16-byte aligned");
-  const int64_t total = n * oh * ow * (c / 16);
-  if (total == 0) return LSC_SUCCESS;
-  DeviceState* ds = current_device_state();
-  if (!ds) return LSC_ERROR_DEVICE_ERROR;
-  maxpool_i8_kernel<<<grid_p(total, ds->sm_count), 256, 0, st>>>(x, y, n, h, w, c, oh, ow, kh, kw, sh, sw, ph, pw);
+  const int64_t per_row = ow * (c / 16);
+  if (n == 0 || oh == 0 || per_row == 0) return LSC_SUCCESS;
+  if (n > 65535 || oh > 65535 || h * w * c > INT32_MAX || oh * ow * c > INT32_MAX)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "maxpool: batch or image too large");
+  const dim3 grid(static_cast<unsigned>((per_row + 127) / 128), static_cast<unsigned>(oh), static_cast<unsigned>(n));
+  const int ih = static_cast<int>(h), iw = static_cast<int>(w), ic = static_cast<int>(c);
+  const int ioh = static_cast<int>(oh), iow = static_cast<int>(ow);
+  if (kh == 3 && kw == 3)
+    maxpool_i8_kernel<3, 3><<<grid, 128, 0, st>>>(x, y, ih, iw, ic, ioh, iow, kh, kw, sh, sw, ph, pw);
+  else if (kh == 2 && kw == 2)
+    maxpool_i8_kernel<2, 2><<<grid, 128, 0, st>>>(x, y, ih, iw, ic, ioh, iow, kh, kw, sh, sw, ph, pw);
+  else
+    maxpool_i8_kernel<0, 0><<<grid, 128, 0, st>>>(x, y, ih, iw, ic, ioh, iow, kh, kw, sh, sw, ph, pw);
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }

@@ -151,26 +151,30 @@ def test_quantize_input_to_nhwc(be):
     np.testing.assert_array_equal(q.numpy().reshape(2, 17, 19, 16), orc.quantize_nchw_to_nhwc(x, 0.02, 16))
 
 
-def test_quantize_input_space_to_depth(be):
-    """Quantize with stride 2: pad by 3, fold 2x2 pixel blocks into channels."""
+@pytest.mark.parametrize("c,cp,extra", [(3, 16, 0), (3, 16, 1), (5, 32, 0)])
+def test_quantize_input_space_to_depth(be, c, cp, extra):
+    """Quantize with stride 2: pad by 3 (and 2*extra more on the right), fold 2x2 pixel blocks
+    into channels.  C=3 into 16 channels is the stem's specialised kernel; C=5 into 32 the
+    general one."""
     from lightship_b200.backend import (DataType, OperatorDef, OperatorType, Quantization, StorageLayout,
                                         Tensor)
-    rng = np.random.default_rng(6)
-    x = rng.normal(size=(2, 3, 26, 30)).astype(np.float32)
-    hs, ws = (26 + 6) // 2, (30 + 6) // 2
+    rng = np.random.default_rng(6 + c + extra)
+    x = rng.normal(size=(2, c, 26, 30)).astype(np.float32)
+    hs, ws = (26 + 6) // 2, (30 + 6) // 2 + extra
     xt = Tensor("x", list(x.shape), DataType.F32, x, layout=StorageLayout.NCHW)
-    q = Tensor("q", [2, hs, ws, 16], DataType.QInt8, np.zeros(2 * hs * ws * 16, np.int8),
+    q = Tensor("q", [2, hs, ws, cp], DataType.QInt8, np.zeros(2 * hs * ws * cp, np.int8),
                layout=StorageLayout.NHWC, quantization=Quantization([0.03]))
-    op = be.compile_operator(OperatorDef("q", OperatorType.Quantize, stride=(2, 2), padding=(3, 3)), None, [xt], [q])
+    op = be.compile_operator(OperatorDef("q", OperatorType.Quantize, stride=(2, 2), padding=(3, 3),
+                                         padding_end_delta=(0, 2 * extra)), None, [xt], [q])
     be.execute(op, [xt], [q])
-    assert q.shape == [2, hs, ws, 16]
-    xp = np.zeros((2, 3, 32, 36), np.float32)
+    assert q.shape == [2, hs, ws, cp]
+    xp = np.zeros((2, c, 32, 36 + 2 * extra), np.float32)
     xp[:, :, 3:29, 3:33] = x
-    qq = orc.quantize_nchw_to_nhwc(xp, 0.03, 3)  # [2, 32, 36, 3]
-    want = np.zeros((2, hs, ws, 16), np.int8)
+    qq = orc.quantize_nchw_to_nhwc(xp, 0.03, c)  # [2, 32, 36 + 2*extra, c]
+    want = np.zeros((2, hs, ws, cp), np.int8)
     for dy in range(2):
         for dx in range(2):
-            want[..., (dy * 2 + dx) * 3:(dy * 2 + dx + 1) * 3] = qq[:, dy::2, dx::2, :]
+            want[..., (dy * 2 + dx) * c:(dy * 2 + dx + 1) * c] = qq[:, dy::2, dx::2, :]
     np.testing.assert_array_equal(q.numpy().reshape(want.shape), want)
 
 
