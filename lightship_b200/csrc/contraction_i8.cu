@@ -55,7 +55,13 @@ struct I8Params {
   int32_t dw, dh, kw;        // dilation, filter width
   int32_t chunks_per_tap;    // C / ACB
   int32_t total_chunks;      // KH*KW*C / ACB
+  // shared-memory plan (set by launch_cfg): a_stages A (or A+W) ring slots; w_resident = 1
+  // keeps the whole [BN x K] weight tile in shared memory, loaded once per CTA (one N tile)
+  int32_t a_stages;
+  int32_t w_resident;
 };
+
+constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per block (227 KB)
 
 template <int BN_>
 struct I8Cfg {
@@ -73,13 +79,20 @@ struct I8Cfg {
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int COLS_PER_EPI_WARP = BN / (EPI_WARPS / 4);
   static constexpr int EPI_W = 16;
+  static constexpr int MAX_STAGES = 8;  // barrier slots
+  static constexpr int RES_STAGES = 4;  // A ring depth when the weights are resident
   static constexpr int BAR_BYTES = 256;
   // per epilogue warp: the scale and bias of the columns it handles in the current N tile
   static constexpr int EPI_COL_BYTES = EPI_WARPS * COLS_PER_EPI_WARP * 8;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + EPI_COL_BYTES;
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
-  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-  static_assert((2 * STAGES + 5) * 8 + 8 <= BAR_BYTES, "barrier area");
+  static_assert(SMEM_BYTES <= kSmemLimit, "shared memory budget");
+  static_assert((2 * MAX_STAGES + 6) * 8 + 8 <= BAR_BYTES, "barrier area");
+  static_assert(STAGES <= MAX_STAGES, "barrier slots");
+  // shared memory with the weights resident: RES_STAGES A slots, kblocks W tiles
+  static constexpr int res_smem_bytes(int kblocks) {
+    return RES_STAGES * A_BYTES + kblocks * B_BYTES + 1024 + BAR_BYTES + EPI_COL_BYTES;
+  }
 };
 
 // Epilogue for W consecutive columns of one output row held by this thread; cs / cb are the
@@ -198,23 +211,29 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int kblocks = (p.k + C::BK - 1) / C::BK;
+  const int stages = p.a_stages;
+  const bool wres = p.w_resident != 0;
+  // [A ring: stages x A_BYTES][W: stages (ring) or kblocks (resident) x B_BYTES][barriers][epi]
   uint8_t* sA = smem;
-  uint8_t* sW = smem + C::STAGES * C::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* sW = smem + stages * C::A_BYTES;
+  uint8_t* after_w = sW + (wres ? kblocks : stages) * C::B_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(after_w);
   uint64_t* full = bars;
-  uint64_t* empty = bars + C::STAGES;
-  uint64_t* tfull = bars + 2 * C::STAGES;
+  uint64_t* empty = bars + C::MAX_STAGES;
+  uint64_t* tfull = bars + 2 * C::MAX_STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* wfull = drain + 1;  // resident weights landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wfull + 1);
   volatile uint32_t* abort_flag = tmem_slot + 1;
-  uint8_t* epi_cols = smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES;
+  uint8_t* epi_cols = after_w + C::BAR_BYTES;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < C::MAX_STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -223,6 +242,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       mbar_init(&tempty[i], C::EPI_WARPS);
     }
     mbar_init(drain, 1);
+    mbar_init(wfull, 1);
     *abort_flag = 0u;
     fence_barrier_init();
   }
@@ -242,7 +262,6 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
   const int m_tiles = (p.m + C::BM - 1) / C::BM;
   const int n_tiles = (p.n + C::BN - 1) / C::BN;
   const int num_tiles = m_tiles * n_tiles;
-  const int kblocks = (p.k + C::BK - 1) / C::BK;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -250,6 +269,11 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       uint32_t stage = 0, phase = 0;
       int issued = 0;
       bool ok = true;
+      if (wres) {
+        // the whole weight tile (one N tile: nb = 0) once, on its own barrier
+        mbar_arrive_expect_tx(wfull, static_cast<uint32_t>(kblocks * C::B_BYTES));
+        for (int kb = 0; kb < kblocks; ++kb) tma_load_2d(&tmW, wfull, sW + kb * C::B_BYTES, kb * C::BK, 0);
+      }
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int mb = tile % m_tiles, nb = tile / m_tiles;
         // filter-origin coordinates of the tile's first output pixel (convolution only)
@@ -268,7 +292,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          mbar_arrive_expect_tx(&full[stage], wres ? C::A_BYTES : C::STAGE_BYTES);
           uint8_t* a_dst = sA + stage * C::A_BYTES;
           if constexpr (ACB == 0) {
             tma_load_2d(&tmA, &full[stage], a_dst, kb * C::BK, mb * C::BM);
@@ -286,9 +310,9 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
                                  static_cast<uint16_t>(kx * p.dw), static_cast<uint16_t>(ky * p.dh));
             }
           }
-          tma_load_2d(&tmW, &full[stage], sW + stage * C::B_BYTES, kb * C::BK, nb * C::BN);
+          if (!wres) tma_load_2d(&tmW, &full[stage], sW + stage * C::B_BYTES, kb * C::BK, nb * C::BN);
           ++issued;
-          if (++stage == C::STAGES) {
+          if (++stage == static_cast<uint32_t>(stages)) {
             stage = 0;
             phase ^= 1u;
           }
@@ -297,13 +321,14 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       if (!ok) {
         // Let the copies already in flight land before the CTA can exit.
         volatile uint32_t no_abort = 0;
-        const int outstanding = issued < C::STAGES ? issued : C::STAGES;
+        const int outstanding = issued < stages ? issued : stages;
         for (int i = 1; i <= outstanding; ++i) {
           const int idx = issued - i;
-          const int s = idx % C::STAGES;
-          const uint32_t ph = static_cast<uint32_t>((idx / C::STAGES) & 1);
+          const int s = idx % stages;
+          const uint32_t ph = static_cast<uint32_t>((idx / stages) & 1);
           mbar_wait(&full[s], ph, &no_abort, p.err);
         }
+        if (wres) mbar_wait(wfull, 0u, &no_abort, p.err);
       }
     }
   } else if (warp == 1) {
@@ -313,6 +338,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       int local = 0;
       bool ok = true;
       bool any_mma = false;
+      if (wres && !mbar_wait(wfull, 0u, abort_flag, p.err)) ok = false;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
         const int buf = local & 1;
         const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
@@ -329,7 +355,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
           }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
-          const uint32_t w0 = smem_u32(sW + stage * C::B_BYTES);
+          const uint32_t w0 = smem_u32(sW + (wres ? kb : static_cast<int>(stage)) * C::B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < C::BK / 32; ++kk) {
             const uint64_t ad = a_desc<ACB>(a0, kk);
@@ -338,7 +364,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
           }
           any_mma = true;
           mma_commit(&empty[stage]);
-          if (++stage == C::STAGES) {
+          if (++stage == static_cast<uint32_t>(stages)) {
             stage = 0;
             phase ^= 1u;
           }
@@ -416,12 +442,22 @@ lsc_status launch_cfg(const CUtensorMap& ta, const CUtensorMap& tw, const I8Para
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
     attr_err = cudaFuncSetAttribute(contraction_i8_kernel<BN, ACT, ACB>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
   });
   if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(contraction_i8)");
-  const int tiles = ((p.m + C::BM - 1) / C::BM) * ((p.n + C::BN - 1) / C::BN);
+  const int m_tiles = (p.m + C::BM - 1) / C::BM;
+  const int n_tiles = (p.n + C::BN - 1) / C::BN;
+  const int tiles = m_tiles * n_tiles;
   const int grid = tiles < sm_count ? tiles : sm_count;
-  contraction_i8_kernel<BN, ACT, ACB><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tw, p);
+  // Keep the weights resident when there is a single N tile, they fit beside a RES_STAGES A
+  // ring, and each CTA runs several M tiles (so the one-time load is amortised): the W tile
+  // then crosses L2 once per CTA instead of once per M tile.
+  const int kblocks = (p.k + C::BK - 1) / C::BK;
+  I8Params q = p;
+  q.w_resident = (n_tiles == 1 && m_tiles >= 2 * grid && C::res_smem_bytes(kblocks) <= kSmemLimit) ? 1 : 0;
+  q.a_stages = q.w_resident ? C::RES_STAGES : C::STAGES;
+  const int smem = q.w_resident ? C::res_smem_bytes(kblocks) : C::SMEM_BYTES;
+  contraction_i8_kernel<BN, ACT, ACB><<<grid, C::THREADS, smem, stream>>>(ta, tw, q);
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }

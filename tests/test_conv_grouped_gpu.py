@@ -115,5 +115,17 @@ def test_grouped_other_batch_and_act_none(be):
     _run(be, 2, 14, 14, 64, 64, 96, 3, 1, act=orc.ACT_NONE, seed=3, exec_n=5)
 
 
+def test_grouped_weights_resident_layer1_batch32(be):
+    """Batch 32 of the layer1 shape: 392 grouped M tiles, so the grouped filter stays
+    resident in shared memory while the pixel tiles stream."""
+    _run(be, 32, 56, 56, 64, 64, 64, 3, 1, residual=True, seed=11)
+
+
+def test_grouped_weights_resident_stem_batch16(be):
+    """Batch 16 of the space-to-depth stem (115 x 116 x 16, 4x4, cropped to 112 columns):
+    G=4, the 256-column grouped filter resident."""
+    _run(be, 16, 115, 116, 16, 12, 64, 4, 0, crop=1, seed=12)
+
+
 def test_width_not_divisible_runs_plain(be):
     _run(be, 2, 15, 15, 64, 64, 64, 3, 1, seed=4)

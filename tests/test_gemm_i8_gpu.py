@@ -132,3 +132,15 @@ def test_gemm_i8_requant_near_ties(cuda, s_out):
         want = orc.gemm_i8_chain(a, w, None, scale, orc.ACT_RELU, s_out, rounding)
         got = _run(cuda, a, w, None, scale, orc.ACT_RELU, s_out, rounding)
         _compare(got, want)
+
+
+@pytest.mark.parametrize("n,k", [(64, 576), (128, 1152), (256, 512), (96, 64), (200, 320)])
+def test_gemm_i8_weights_resident(cuda, n, k):
+    """M large enough that every CTA runs several M tiles of the single N tile: the weight
+    tile stays in shared memory and only A streams (K = 64 ... 1152, ragged N)."""
+    rng = np.random.default_rng(n + k)
+    a, w, b, scale = _case(rng, 40000, n, k)
+    for act, rounding in ((orc.ACT_RELU, orc.ROUND_HALF_AWAY), (orc.ACT_NONE, orc.ROUND_HALF_EVEN)):
+        want = orc.gemm_i8_chain(a, w, b, scale, act, 3.0, rounding)
+        got = _run(cuda, a, w, b, scale, act, 3.0, rounding)
+        _compare(got, want)
