@@ -274,6 +274,24 @@ def gemm_measure(torch, dev, steps, warmup):
     return res, s_out
 
 
+def shard_bounds(batch, world, rank):
+    """The contiguous slice [lo, hi) of the global batch that rank owns (batch % world == 0)."""
+    if batch % world:
+        raise ValueError(f"batch {batch} does not split over {world} ranks")
+    per = batch // world
+    return rank * per, (rank + 1) * per
+
+
+def reduce_max(v, world, device=None):
+    """Max of a per-rank float over the process group (the step time every rank reports)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -288,10 +306,7 @@ def run_gpu(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
     def max_over_ranks(v):
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return reduce_max(v, world, dev)
 
     def barrier():
         if world > 1:
@@ -340,11 +355,12 @@ def run_gpu(args):
     batch = args.batch
     if batch % world:
         raise SystemExit(f"batch {batch} does not split over {world} GPUs")
-    per = batch // world
+    lo, hi = shard_bounds(batch, world, rank)
+    per = hi - lo
     # the global batch is seeded; each rank takes its contiguous shard
     rng = np.random.default_rng(DATA_SEED)
     x_all = rng.normal(size=(batch, 3, IMAGE, IMAGE)).astype(np.float32)
-    x_host = torch.from_numpy(x_all[rank * per:(rank + 1) * per]).pin_memory()
+    x_host = torch.from_numpy(x_all[lo:hi]).pin_memory()
     del x_all
     be = CudaBackend(GpuBackendConfig(device_id=local, arena_bytes=256 << 20))
     model = ResNet18Int8(be, per, dev, image=IMAGE, seed=NET_SEED)
@@ -440,7 +456,7 @@ def run_gpu(args):
         "network_tops": img_ops * batch / (ms_max * 1e-3) / 1e12,
         "roofline": {"bound": "tensor", "kernel": "contraction_i8_kernel (INT8 implicit-GEMM conv)",
                      "achieved": conv_tops, "peak": int8_peak, "unit": "TOPS", "frac": conv_tops / int8_peak,
-                     "traffic": load_traffic("contraction_i8_conv_resnet18.md"), "peak_source": peak_source,
+                     "traffic": load_traffic("contraction_i8_conv_layer1_b256.md"), "peak_source": peak_source,
                      "conv_share_of_step": conv_ms / ms if ms > 0 else None},
         "e2e": {"value": e2e_value, "unit": "img/s", "h2d_bytes_per_step": in_bytes * world,
                 "d2h_bytes_per_step": out_bytes * world, "api": "lsc_memcpy_h2d + network + lsc_memcpy_d2h",
