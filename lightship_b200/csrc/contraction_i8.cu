@@ -95,6 +95,22 @@ struct I8Cfg {
   }
 };
 
+// CTA-pair GEMM: 6 stages x (16 KB A + 16 KB W) per CTA; EPI_WARPS epilogue warps over the
+// 256 accumulator columns in EPI_W-column chunks
+struct PairCfg {
+  static constexpr int STAGES = 6;
+  static constexpr int EPI_WARPS = 16;
+  static constexpr int EPI_W = 16;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int COLS_PER_EPI_WARP = 256 / (EPI_WARPS / 4);
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int EPI_COL_BYTES = EPI_WARPS * COLS_PER_EPI_WARP * 8;
+  static constexpr int SMEM_BYTES = STAGES * (2 * 128 * 128) + 1024 + BAR_BYTES + EPI_COL_BYTES;
+  static_assert(SMEM_BYTES <= kSmemLimit, "shared memory budget");
+  static_assert((2 * STAGES + 5) * 8 + 8 <= BAR_BYTES, "barrier area");
+};
+
+
 // Epilogue for W consecutive columns of one output row held by this thread; cs / cb are the
 // chunk's per-column scales and biases staged in shared memory (zero past the last column).
 // Each output is stored as soon as it is final (i32, then f32, then int8) so the
@@ -413,8 +429,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                static_cast<uint32_t>(buf * C::BN + tcol);
         uint32_t r[C::EPI_W];
-        if constexpr (C::EPI_W == 32) tmem_ld_32x32b_x32(taddr, r);
-        else tmem_ld_32x32b_x16(taddr, r);
+        tmem_ld_cols(taddr, r);
         tmem_ld_wait();
         if (c == CHUNKS - 1) {
           tc_fence_before();
@@ -431,6 +446,222 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// CTA-pair GEMM (cluster of 2, tcgen05 cta_group::2) for large dense contractions.
+//
+// A pair owns a 256 x 256 output tile.  Each CTA fetches its own 128 rows of A and its own
+// 128 of the tile's 256 W rows (no multicast), so a pair moves 512 rows of operands per
+// 65,536 outputs where two independent 128 x 256 CTAs move 768.  The even CTA issues
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32) over both CTAs' shared memory; each
+// CTA's TMEM receives its 128 rows x 256 columns, double-buffered (512 columns).
+//   producer (warp 0, both CTAs): waits on its own `empty` slot, loads A and W halves with
+//     completion counted on the even CTA's `full` barrier (the even producer posts the
+//     pair's byte count);
+//   MMA (warp 1, even CTA): waits `full`, issues 4 MMAs per stage, commits the stage to
+//     both CTAs' `empty` and the finished tile to both CTAs' `tfull` (multicast commit);
+//   epilogue (warps 2-17, both CTAs): as the single-CTA kernel on the CTA's own rows; the
+//     last TMEM read of a tile arrives on the even CTA's `tempty` (2 x 16 arrivals).
+// All waits are bounded; both CTAs meet at a cluster barrier before TMEM is released.
+template <int PN, int ACT>
+__global__ void __launch_bounds__(PairCfg::THREADS, 1)
+    contraction_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                               const __grid_constant__ CUtensorMap tmW, const I8Params p) {
+  using C = I8Cfg<256>;  // BK
+  using P = PairCfg;
+  constexpr int ROWS = 128;                   // A rows per CTA
+  constexpr int WROWS = PN / 2;               // W rows per CTA (the pair tile is 256 x PN)
+  constexpr int STAGES = PairCfg::STAGES;
+  constexpr int A_BYTES = ROWS * C::BK;
+  constexpr int W_BYTES = 128 * C::BK;        // stage slot (WROWS rows used)
+  constexpr uint32_t IDESC = idesc_i8(256, PN);
+  constexpr int COLS = PN / (P::EPI_WARPS / 4);  // accumulator columns per epilogue warp
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sW = smem + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + STAGES * W_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+  uint8_t* epi_cols = reinterpret_cast<uint8_t*>(bars) + P::BAR_BYTES;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool even = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 2 * P::EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * PN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any remote arrive / complete_tx
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t full_even = mapa_shared(smem_u32(full), 0);
+  const uint32_t tempty_even = mapa_shared(smem_u32(tempty), 0);
+
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int m_tiles = (p.m + 255) / 256;
+  const int n_tiles = (p.n + PN - 1) / PN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kblocks = (p.k + C::BK - 1) / C::BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- TMA producer
+      uint32_t stage = 0, phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const int mb = tile % m_tiles, nb = tile / m_tiles;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          if (even) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + WROWS * C::BK));
+          const uint32_t fb = full_even + stage * 8;
+          tma_load_2d_pair(&tmA, fb, sA + stage * A_BYTES, kb * C::BK, mb * 256 + static_cast<int>(rank) * ROWS);
+          tma_load_2d_pair(&tmW, fb, sW + stage * W_BYTES, kb * C::BK, nb * PN + static_cast<int>(rank) * WROWS);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && even) {
+        // Let the pair's copies in flight land (they complete on these barriers).
+        volatile uint32_t no_abort = 0;
+        const int outstanding = issued < STAGES ? issued : STAGES;
+        for (int i = 1; i <= outstanding; ++i) {
+          const int idx = issued - i;
+          mbar_wait(&full[idx % STAGES], static_cast<uint32_t>((idx / STAGES) & 1), &no_abort, p.err);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && even) {
+      // ------------------------------------------------------------- MMA issuer (even CTA)
+      uint32_t stage = 0, phase = 0;
+      int local = 0;
+      bool ok = true;
+      bool any_mma = false;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!mbar_wait(&tempty[buf], buf_phase ^ 1u, abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * PN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+          const uint32_t w0 = smem_u32(sW + stage * W_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < C::BK / 32; ++kk)
+            mma_i8_pair(d_tmem, smem_desc_sw128_kmajor(a0 + kk * 32), smem_desc_sw128_kmajor(w0 + kk * 32), IDESC,
+                        (kb | kk) != 0 ? 1u : 0u);
+          any_mma = true;
+          mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) mma_commit_pair(&tfull[buf], 0x3);
+      }
+      if (!ok && any_mma) {
+        volatile uint32_t no_abort = 0;
+        mma_commit_pair(drain, 0x1);
+        mbar_wait(drain, 0u, &no_abort, p.err);
+      }
+    }
+  } else {
+    // --------------------------------------------------------------- epilogue (own rows)
+    const int epi = warp - 2;
+    const int quarter = warp & 3;
+    const int part = epi >> 2;
+    const int row_in_tile = quarter * 32 + lane;
+    float* w_scale = reinterpret_cast<float*>(epi_cols + epi * (COLS * 8));
+    int32_t* w_bias = reinterpret_cast<int32_t*>(w_scale + COLS);
+    int staged_nb = -1;
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
+      const int mb = tile % m_tiles, nb = tile / m_tiles;
+      if (nb != staged_nb) {
+        __syncwarp();
+        for (int i = lane; i < COLS; i += 32) {
+          const int col = nb * PN + part * COLS + i;
+          w_scale[i] = col < p.n ? __ldg(p.scale + col) : 0.0f;
+          w_bias[i] = (p.bias && col < p.n) ? __ldg(p.bias + col) : 0;
+        }
+        __syncwarp();
+        staged_nb = nb;
+      }
+      const int buf = local & 1;
+      const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
+      if (!mbar_wait(&tfull[buf], buf_phase, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int row = mb * 256 + static_cast<int>(rank) * ROWS + row_in_tile;
+      constexpr int CHUNKS = COLS / P::EPI_W;
+#pragma unroll 1
+      for (int c = 0; c < CHUNKS; ++c) {
+        const int tcol = part * COLS + c * P::EPI_W;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(buf * PN + tcol);
+        uint32_t r[P::EPI_W];
+        tmem_ld_cols(taddr, r);
+        tmem_ld_wait();
+        if (c == CHUNKS - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty_even + buf * 8);
+        }
+        epilogue_chunk<ACT, P::EPI_W>(p, r, w_scale + c * P::EPI_W, w_bias + c * P::EPI_W, row, nb * PN + tcol);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * PN);
   }
 }
 
@@ -473,6 +704,61 @@ lsc_status launch_act(const CUtensorMap& ta, const CUtensorMap& tw, const I8Para
   }
 }
 
+// Launch of the CTA-pair kernel: clusters of 2, one pair per two SMs up to the number of
+// pairs the device can hold at once (persistent over 256 x 256 tiles).
+template <int PN, int ACT>
+lsc_status launch_pair_act(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p, int sm_count,
+                           cudaStream_t stream) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  static int max_pairs = 0;
+  std::call_once(once, [sm_count] {
+    attr_err = cudaFuncSetAttribute(contraction_i8_pair_kernel<PN, ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    PairCfg::SMEM_BYTES);
+    if (attr_err != cudaSuccess) return;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(sm_count & ~1));
+    cfg.blockDim = dim3(PairCfg::THREADS);
+    cfg.dynamicSmemBytes = PairCfg::SMEM_BYTES;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    attr_err = cudaOccupancyMaxActiveClusters(&max_pairs, contraction_i8_pair_kernel<PN, ACT>, &cfg);
+  });
+  if (attr_err != cudaSuccess) return cuda_error(attr_err, "contraction_i8_pair setup");
+  if (max_pairs < 1) return set_error(LSC_ERROR_EXECUTION_FAILED, "gemm_i8: no CTA pair fits on the device");
+  const int tiles = ((p.m + 255) / 256) * ((p.n + PN - 1) / PN);
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(PairCfg::THREADS);
+  cfg.dynamicSmemBytes = PairCfg::SMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  LSC_CUDA_TRY(cudaLaunchKernelEx(&cfg, contraction_i8_pair_kernel<PN, ACT>, ta, tw, p));
+  return LSC_SUCCESS;
+}
+
+lsc_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p, int act, int sm_count,
+                       cudaStream_t stream) {
+  switch (act) {
+    case LSC_ACT_RELU: return launch_pair_act<256, LSC_ACT_RELU>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_RELU6: return launch_pair_act<256, LSC_ACT_RELU6>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_SILU: return launch_pair_act<256, LSC_ACT_SILU>(ta, tw, p, sm_count, stream);
+    default: return launch_pair_act<256, LSC_ACT_NONE>(ta, tw, p, sm_count, stream);
+  }
+}
+
 template <int ACB>
 lsc_status launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p,
                      int act, int sm_count, cudaStream_t stream) {
@@ -495,6 +781,16 @@ int pick_bn(int64_t m, int64_t n, int sm_count) {
   const int64_t m_tiles = (m + 127) / 128;
   while (bn > 64 && m_tiles * ((n + bn - 1) / bn) * 2 <= sm_count) bn /= 2;
   return bn;
+}
+
+// CTA-pair tile width for a GEMM (256), or 0 for single CTAs.  Pairs need N > 256 (a single
+// N tile runs best weight-resident on single CTAs) and at least 32 pair tiles; measured on
+// B200, a 256 x 256 pair tile beats both single-CTA tiles and 256 x 128 pair tiles even when
+// there are fewer tiles than pairs (4096 x 1024 x 4096: 20.9 us against 30.1 us).
+int pair_tile_n(int64_t m, int64_t n) {
+  if (n <= 256 || m < 256) return 0;
+  const int64_t t256 = ((m + 255) / 256) * ((n + 255) / 256);
+  return t256 >= 32 ? 256 : 0;
 }
 
 lsc_status check_common(int64_t m, int64_t n, int act, int rounding, const float* scale,
@@ -556,7 +852,11 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
                      "gemm_i8: needs an sm_100 (B200) device, found sm_%d%d", ds->cc_major,
                      ds->cc_minor);
 
-  const int bn = pick_bn(m, n, ds->sm_count);
+  // CTA pairs for GEMMs wide and tall enough to give every pair of SMs 256 x 256 tiles;
+  // single CTAs (128 x BN tiles) otherwise.
+  const int pn = pair_tile_n(m, n);
+  const bool pair = pn > 0;
+  const int bn = pair ? pn / 2 : pick_bn(m, n, ds->sm_count);  // W box rows (a pair CTA holds PN/2)
   CUtensorMap ta, tw;
   st = encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, m, k, 128, 128,
                       CU_TENSOR_MAP_SWIZZLE_128B);
@@ -570,6 +870,7 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
   p.n = static_cast<int32_t>(n);
   p.k = static_cast<int32_t>(k);
   fill_outputs(p, bias, scale, s_out, rounding, out_i8, out_f32, out_i32, ldo, ds->err_word);
+  if (pair) return launch_pair(ta, tw, p, act, ds->sm_count, stream);
   return launch_bn<0>(bn, ta, tw, p, act, ds->sm_count, stream);
 }
 

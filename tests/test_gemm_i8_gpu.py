@@ -144,3 +144,17 @@ def test_gemm_i8_weights_resident(cuda, n, k):
         want = orc.gemm_i8_chain(a, w, b, scale, act, 3.0, rounding)
         got = _run(cuda, a, w, b, scale, act, 3.0, rounding)
         _compare(got, want)
+
+
+@pytest.mark.parametrize("m,n,k", [(9000, 600, 1040), (4352, 768, 256), (2100, 1100, 4096), (19000, 256, 96)])
+def test_gemm_i8_cta_pairs(cuda, m, n, k):
+    """Shapes that run on CTA pairs (cta_group::2, 256 x 256 tiles; fewer tiles than SM
+    pairs included) and a single-N-tile shape that stays on single CTAs: ragged M, N and K,
+    all three outputs, every activation / rounding combination of the chain."""
+    rng = np.random.default_rng(m + n + k)
+    a, w, b, scale = _case(rng, m, n, k)
+    for act, rounding in ((orc.ACT_NONE, orc.ROUND_HALF_EVEN), (orc.ACT_RELU, orc.ROUND_HALF_AWAY),
+                          (orc.ACT_RELU6, orc.ROUND_HALF_EVEN)):
+        want = orc.gemm_i8_chain(a, w, b, scale, act, 5.0, rounding)
+        got = _run(cuda, a, w, b, scale, act, 5.0, rounding)
+        _compare(got, want)
