@@ -89,7 +89,10 @@ typedef enum lsc_op_type {
   LSC_OP_DEQUANTIZE = 8, /* dequantize_tensor (quantization/helpers.rs:53-94) */
   LSC_OP_QGEMM = 9,      /* quantized_gemm_int8 + requant/dequant (cpu/quantized_ops.rs:13-48) */
   LSC_OP_MAXPOOL2D = 10, /* MaxPool2d on int8 NHWC (operator/pooling.rs:383-455) */
-  LSC_OP_GLOBAL_AVGPOOL2D = 11 /* GlobalAvgPool2d on int8 NHWC (operator/pooling.rs:457-530) */
+  LSC_OP_GLOBAL_AVGPOOL2D = 11, /* GlobalAvgPool2d on int8 NHWC (operator/pooling.rs:457-530) */
+  LSC_OP_GELU = 12,      /* Gelu::compute, tanh form (operator/gelu.rs:77-103) */
+  LSC_OP_LAYERNORM = 13, /* LayerNorm over the last axis (operator/layernorm.rs:140-205) */
+  LSC_OP_SOFTMAX = 14    /* Softmax over the last axis (operator/softmax.rs:106-169) */
 } lsc_op_type;
 
 /* FusionType (ir/fusion.rs:8-23); LSC_FUSION_NONE = no FusionInfo */
@@ -109,6 +112,8 @@ typedef enum lsc_fusion_type {
 #define LSC_ACT_RELU 1  /* x > 0 ? x : 0           platform/simd.rs:552-556 */
 #define LSC_ACT_RELU6 2 /* f32::clamp(x, 0, 6)     platform/simd.rs:558-562 */
 #define LSC_ACT_SILU 3  /* x / (1 + exp(-x)), +-20 cut-offs  operator/silu.rs:47-61 */
+#define LSC_ACT_GELU 4  /* 0.5x(1 + t(0.79788456(x + 0.044715x^3))), t the reference's polynomial
+                           tanh (x - x^3/3 + x^5/5 - x^7/7, +-1 past +-5)  operator/gelu.rs:77-103 */
 
 /* rounding of the requantize step */
 #define LSC_ROUND_HALF_AWAY 0 /* Rust f32::round (cpu/quantized_ops.rs:45, helpers.rs:153) */

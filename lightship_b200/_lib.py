@@ -27,7 +27,7 @@ ERROR_EXECUTION_FAILED = 13
 ERROR_UNSUPPORTED_LAYOUT = 14
 ERROR_TIMEOUT = 15
 
-ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SILU = 0, 1, 2, 3
+ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SILU, ACT_GELU = 0, 1, 2, 3, 4
 ROUND_HALF_AWAY, ROUND_HALF_EVEN = 0, 1
 FP32_3XTF32, FP32_TF32 = 0, 1
 MEM_HOST, MEM_DEVICE = 0, 1

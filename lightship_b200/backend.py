@@ -69,6 +69,9 @@ class OperatorType(enum.IntEnum):
     QGemm = 9
     MaxPool2d = 10
     GlobalAvgPool2d = 11
+    GELU = 12
+    LayerNorm = 13
+    Softmax = 14
 
 
 class FusionType(enum.IntEnum):
@@ -86,6 +89,7 @@ class Activation(enum.IntEnum):
     ReLU = 1
     ReLU6 = 2
     SiLU = 3
+    GELU = 4
 
 
 class Rounding(enum.IntEnum):

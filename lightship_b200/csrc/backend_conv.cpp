@@ -670,4 +670,73 @@ lsc_status execute_activation(const lsc_op* op, const lsc_tensor* in, int n_in, 
   return launch_activation_f32(static_cast<const float*>(xd), static_cast<float*>(yd), total, op->act, s.st);
 }
 
+// ------------------------------------------------------------------------------ LayerNorm / Softmax
+// LayerNorm (operator/layernorm.rs:59-205): inputs (x, gamma?, beta?) with gamma / beta of the
+// last axis's length, epsilon from bn_epsilon (0 -> the reference's 1e-5).  Softmax
+// (operator/softmax.rs:37-169): the last axis (SoftmaxAxis::Last, the reference's default).
+// Both keep the input's storage type (f32 or f16) and shape.
+lsc_status compile_layernorm(lsc_op* op, const lsc_tensor* in, int n_in, int n_out) {
+  if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "LayerNorm: missing input or output");
+  const lsc_tensor& x = in[0];
+  if (x.dtype != LSC_DTYPE_F32 && x.dtype != LSC_DTYPE_F16)
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "LayerNorm requires F32 or F16 input");
+  if (x.ndim < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "LayerNorm requires at least 1D input");
+  op->kind = OpKind::kLayerNorm;
+  op->qdtype = x.dtype;
+  const int64_t d = x.shape[x.ndim - 1];
+  op->n = d;
+  op->s_out = bn_eps(op->desc);
+  lsc_status st;
+  void* p = nullptr;
+  if (n_in >= 2 && in[1].data) {
+    std::vector<float> g;
+    if ((st = read_f32(in[1], d, g)) || (st = own_upload(op, g.data(), d * 4, &p))) return st;
+    op->scale = static_cast<float*>(p);
+  }
+  if (n_in >= 3 && in[2].data) {
+    std::vector<float> b;
+    if ((st = read_f32(in[2], d, b)) || (st = own_upload(op, b.data(), d * 4, &p))) return st;
+    op->bias_f32 = static_cast<float*>(p);
+  }
+  return LSC_SUCCESS;
+}
+
+lsc_status compile_softmax(lsc_op* op, const lsc_tensor* in, int n_in, int n_out) {
+  if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Softmax: missing input or output");
+  const lsc_tensor& x = in[0];
+  if (x.dtype != LSC_DTYPE_F32 && x.dtype != LSC_DTYPE_F16)
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "Softmax requires F32 or F16 input");
+  op->kind = OpKind::kSoftmax;
+  op->qdtype = x.dtype;
+  return LSC_SUCCESS;
+}
+
+lsc_status execute_rownorm(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out,
+                           Staging& s) {
+  if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "missing input or output");
+  const lsc_tensor& x = in[0];
+  const bool ln = op->kind == OpKind::kLayerNorm;
+  if (x.dtype != op->qdtype)
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "%s: input dtype %d, compiled for %d", ln ? "LayerNorm" : "Softmax",
+                     x.dtype, op->qdtype);
+  if (x.ndim < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "input must be at least 1D");
+  const int64_t d = x.shape[x.ndim - 1];
+  if (ln && d != op->n)
+    return set_error(LSC_ERROR_SHAPE_MISMATCH, "LayerNorm: last axis %lld, compiled for %lld", (long long)d,
+                     (long long)op->n);
+  const int64_t total = numel(x);
+  if (total < 0) return set_error(LSC_ERROR_SHAPE_MISMATCH, "bad shape");
+  const int64_t esz = dtype_size(x.dtype);
+  if (out[0].dtype != x.dtype) return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "output dtype must match the input");
+  const void* xd = nullptr;
+  void* yd = nullptr;
+  lsc_status st;
+  if ((st = s.input(x, total * esz, &xd)) || (st = s.output(out[0], total * esz, &yd))) return st;
+  out[0].ndim = x.ndim;
+  for (int i = 0; i < x.ndim; ++i) out[0].shape[i] = x.shape[i];
+  const int64_t rows = d > 0 ? total / d : 0;
+  if (ln) return launch_layernorm(xd, yd, x.dtype, rows, d, op->scale, op->bias_f32, op->s_out, s.st);
+  return launch_softmax(xd, yd, x.dtype, rows, d, s.st);
+}
+
 }  // namespace lsc

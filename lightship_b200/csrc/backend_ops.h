@@ -30,6 +30,8 @@ enum class OpKind {
   kDequantize,     // q -> f32
   kMatMulF32,      // C = A[M,K] B[K,N]
   kFcF32,          // Y = X W^T (+ bias)
+  kLayerNorm,      // LayerNorm over the last axis (f32 / f16)
+  kSoftmax,        // Softmax over the last axis (f32 / f16)
   kConvF32,        // NCHW convolution (+ folded BN, bias, activation)
   kBatchNormF32,   // per-channel affine (+ ReLU)
   kActF32,         // ReLU / ReLU6 / SiLU
@@ -138,6 +140,10 @@ lsc_status compile_pool(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, b
 lsc_status execute_pool(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out,
                         Staging& s);
 lsc_status compile_activation(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, int act);
+lsc_status compile_layernorm(lsc_op* op, const lsc_tensor* in, int n_in, int n_out);
+lsc_status compile_softmax(lsc_op* op, const lsc_tensor* in, int n_in, int n_out);
+lsc_status execute_rownorm(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out,
+                           Staging& s);
 lsc_status execute_activation(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out,
                               int n_out, Staging& s);
 

@@ -700,6 +700,7 @@ lsc_status launch_act(const CUtensorMap& ta, const CUtensorMap& tw, const I8Para
     case LSC_ACT_RELU: return launch_cfg<BN, LSC_ACT_RELU, ACB>(ta, tw, p, sm_count, stream);
     case LSC_ACT_RELU6: return launch_cfg<BN, LSC_ACT_RELU6, ACB>(ta, tw, p, sm_count, stream);
     case LSC_ACT_SILU: return launch_cfg<BN, LSC_ACT_SILU, ACB>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_GELU: return launch_cfg<BN, LSC_ACT_GELU, ACB>(ta, tw, p, sm_count, stream);
     default: return launch_cfg<BN, LSC_ACT_NONE, ACB>(ta, tw, p, sm_count, stream);
   }
 }
@@ -755,6 +756,7 @@ lsc_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tw, const I8Par
     case LSC_ACT_RELU: return launch_pair_act<256, LSC_ACT_RELU>(ta, tw, p, sm_count, stream);
     case LSC_ACT_RELU6: return launch_pair_act<256, LSC_ACT_RELU6>(ta, tw, p, sm_count, stream);
     case LSC_ACT_SILU: return launch_pair_act<256, LSC_ACT_SILU>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_GELU: return launch_pair_act<256, LSC_ACT_GELU>(ta, tw, p, sm_count, stream);
     default: return launch_pair_act<256, LSC_ACT_NONE>(ta, tw, p, sm_count, stream);
   }
 }
@@ -799,7 +801,7 @@ lsc_status check_common(int64_t m, int64_t n, int act, int rounding, const float
   if (!out_i8 && !out_f32 && !out_i32)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: no output given", who);
   if (m > 0 && n > 0 && !scale) return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: null scale", who);
-  if (act < LSC_ACT_NONE || act > LSC_ACT_SILU)
+  if (act < LSC_ACT_NONE || act > LSC_ACT_GELU)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: bad activation %d", who, act);
   if (rounding != LSC_ROUND_HALF_AWAY && rounding != LSC_ROUND_HALF_EVEN)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: bad rounding %d", who, rounding);

@@ -72,6 +72,7 @@ __device__ __forceinline__ float act_rt(float x, int act) {
     case LSC_ACT_RELU: return act_relu(x);
     case LSC_ACT_RELU6: return act_relu6(x);
     case LSC_ACT_SILU: return act_silu(x);
+    case LSC_ACT_GELU: return act_gelu(x);
     default: return x;
   }
 }
@@ -365,7 +366,7 @@ lsc_status launch_gemm_tf32(const float* a_hi, const float* a_lo, const float* b
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_tf32: K must be a positive multiple of 4");
   if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_tf32: size too large");
-  if (act < LSC_ACT_NONE || act > LSC_ACT_SILU) return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_tf32: bad activation");
+  if (act < LSC_ACT_NONE || act > LSC_ACT_GELU) return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_tf32: bad activation");
   lsc_status st;
   if ((st = check_ptr16(a_hi, "A")) || (st = check_ptr16(b_hi, "B")) ||
       (split && ((st = check_ptr16(a_lo, "A lo")) || (st = check_ptr16(b_lo, "B lo")))))
@@ -418,7 +419,7 @@ lsc_status launch_conv_tf32(const float* x_hi, const float* x_lo, const float* w
   if ((st = check_ptr16(x_hi, "x")) || (st = check_ptr16(w_hi, "w")) ||
       (split && ((st = check_ptr16(x_lo, "x lo")) || (st = check_ptr16(w_lo, "w lo")))))
     return st;
-  if (act < LSC_ACT_NONE || act > LSC_ACT_SILU) return set_error(LSC_ERROR_INVALID_ARGUMENT, "conv_tf32: bad activation");
+  if (act < LSC_ACT_NONE || act > LSC_ACT_GELU) return set_error(LSC_ERROR_INVALID_ARGUMENT, "conv_tf32: bad activation");
   DeviceState* ds = current_device_state();
   if (!ds) return LSC_ERROR_DEVICE_ERROR;
   if (ds->cc_major != 10) return set_error(LSC_ERROR_BACKEND_NOT_AVAILABLE, "conv_tf32: needs sm_100");

@@ -4,7 +4,8 @@
 //                        (lightship-core/src/operator/batchnorm.rs:154-215; inv_std is computed
 //                        on the host with the same f32 operations), optional ReLU
 //                        (FusionType::BatchNormReLU, backend/cpu.rs:404-439)
-//   ReLU / ReLU6 / SiLU  (platform/simd.rs:552-562, operator/silu.rs:47-61)
+//   ReLU / ReLU6 / SiLU / GELU (platform/simd.rs:552-562, operator/silu.rs:47-61,
+//                        operator/gelu.rs:77-103)
 //   Add (+ReLU)          (backend/cpu.rs:468-517; FusionType::AddReLU)
 // Every operation is an explicitly rounded intrinsic, so results match the reference bit
 // for bit.  16-byte vector loads where alignment allows; grids are a multiple of the SM count.
@@ -19,6 +20,7 @@ __device__ __forceinline__ float act_any(float x, int act) {
     case LSC_ACT_RELU: return act_relu(x);
     case LSC_ACT_RELU6: return act_relu6(x);
     case LSC_ACT_SILU: return act_silu(x);
+    case LSC_ACT_GELU: return act_gelu(x);
     default: return x;
   }
 }

@@ -39,11 +39,33 @@ __device__ __forceinline__ float act_silu(float x) {
   return __fdiv_rn(x, __fadd_rn(1.0f, e));
 }
 
+// The reference's tanh for GELU: the odd series x - x^3/3 + x^5/5 - x^7/7 below |x| <= 5,
+// +-1 beyond (gelu.rs:91-103), evaluated in its order with IEEE division.
+__device__ __forceinline__ float gelu_tanh_poly(float x) {
+  if (x > 5.0f) return 1.0f;
+  if (x < -5.0f) return -1.0f;
+  const float x2 = __fmul_rn(x, x);
+  const float x3 = __fmul_rn(x2, x);
+  const float x5 = __fmul_rn(x3, x2);
+  const float x7 = __fmul_rn(x5, x2);
+  float r = __fsub_rn(x, __fdiv_rn(x3, 3.0f));
+  r = __fadd_rn(r, __fdiv_rn(x5, 5.0f));
+  return __fsub_rn(r, __fdiv_rn(x7, 7.0f));
+}
+
+// Gelu::tanh_gelu (gelu.rs:77-85): 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3))).
+__device__ __forceinline__ float act_gelu(float x) {
+  const float x_cube = __fmul_rn(__fmul_rn(x, x), x);
+  const float arg = __fmul_rn(0.7978845608f, __fadd_rn(x, __fmul_rn(0.044715f, x_cube)));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, gelu_tanh_poly(arg)));
+}
+
 template <int ACT>
 __device__ __forceinline__ float apply_act(float x) {
   if constexpr (ACT == LSC_ACT_RELU) return act_relu(x);
   else if constexpr (ACT == LSC_ACT_RELU6) return act_relu6(x);
   else if constexpr (ACT == LSC_ACT_SILU) return act_silu(x);
+  else if constexpr (ACT == LSC_ACT_GELU) return act_gelu(x);
   else return x;
 }
 

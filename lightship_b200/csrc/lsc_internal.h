@@ -105,6 +105,11 @@ lsc_status launch_add_f32(const float* a, const float* b, float* y, int64_t n, i
 lsc_status launch_quantize_nchw_to_nhwc_i8(const float* x, int8_t* y, int64_t n, int64_t c,
                                            int64_t hw, int64_t cp, float scale, int rounding,
                                            cudaStream_t st);
+// Row-wise LayerNorm / Softmax over the last axis of [rows, d], f32 or f16 storage (norm.cu).
+lsc_status launch_layernorm(const void* x, void* y, int32_t dtype, int64_t rows, int64_t d, const float* gamma,
+                            const float* beta, float eps, cudaStream_t st);
+lsc_status launch_softmax(const void* x, void* y, int32_t dtype, int64_t rows, int64_t d, cudaStream_t st);
+
 lsc_status launch_quantize_nchw_to_s2d_i8(const float* x, int8_t* y, int64_t n, int64_t c, int64_t h,
                                           int64_t w, int64_t ph, int64_t pw, int64_t ph_end, int64_t pw_end,
                                           int64_t blk, int64_t cp, float scale, int rounding, cudaStream_t st);

@@ -295,12 +295,78 @@ float orc_act(float x, int act) {
       if (x > 20.0f) return x;
       if (x < -20.0f) return 0.0f;
       return x / (1.0f + expf(-x));
+    case ORC_ACT_GELU: {
+      // Gelu::tanh_gelu with its polynomial tanh_approx (core/operator/gelu.rs:77-103)
+      const float sqrt_2_over_pi = 0.7978845608f;
+      const float c = 0.044715f;
+      const float x_cube = x * x * x;
+      const float t = sqrt_2_over_pi * (x + c * x_cube);
+      float th;
+      if (t > 5.0f) {
+        th = 1.0f;
+      } else if (t < -5.0f) {
+        th = -1.0f;
+      } else {
+        const float t2 = t * t, t3 = t2 * t, t5 = t3 * t2, t7 = t5 * t2;
+        th = t - t3 / 3.0f + t5 / 5.0f - t7 / 7.0f;
+      }
+      return 0.5f * x * (1.0f + th);
+    }
     default: return x;
   }
 }
 
 void orc_act_inplace(float* x, int64_t n, int act) {
   for (int64_t i = 0; i < n; ++i) x[i] = orc_act(x[i], act);
+}
+
+// LayerNorm::normalize_simd (core/operator/layernorm.rs:153-205) per row: mean = sum / d,
+// variance = sum((x - mean)^2) / d, std = sqrt(variance + eps), y = (x - mean) / std, then
+// gamma * y and + beta.  Sums run in index order in f32 (the reference's horizontal_sum
+// order differs by lane; the comparison is against a stated tolerance).
+void orc_layernorm(const float* x, float* y, int64_t rows, int64_t d, const float* gamma,
+                   const float* beta, float eps) {
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* xr = x + r * d;
+    float* yr = y + r * d;
+    if (d == 0) continue;
+    float s = 0.0f;
+    for (int64_t i = 0; i < d; ++i) s += xr[i];
+    const float mean = s / static_cast<float>(d);
+    float sq = 0.0f;
+    for (int64_t i = 0; i < d; ++i) {
+      const float t = xr[i] - mean;
+      sq += t * t;
+    }
+    const float var = sq / static_cast<float>(d);
+    const float sd = sqrtf(var + eps);
+    for (int64_t i = 0; i < d; ++i) {
+      float v = (xr[i] - mean) / sd;
+      if (gamma) v = gamma[i] * v;
+      if (beta) v += beta[i];
+      yr[i] = v;
+    }
+  }
+}
+
+// Softmax::compute (core/operator/softmax.rs:106-146) per row: max by f32::max, sum of
+// exp(x - max) in index order, y = exp(x - max) * (1 / sum); a row whose sum is not positive
+// is left as it is.
+void orc_softmax(const float* x, float* y, int64_t rows, int64_t d) {
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* xr = x + r * d;
+    float* yr = y + r * d;
+    for (int64_t i = 0; i < d; ++i) yr[i] = xr[i];
+    if (d == 0) continue;
+    float mx = -INFINITY;
+    for (int64_t i = 0; i < d; ++i) mx = fmaxf(mx, xr[i]);
+    float s = 0.0f;
+    for (int64_t i = 0; i < d; ++i) s += expf(xr[i] - mx);
+    if (s > 0.0f) {
+      const float scale = 1.0f / s;
+      for (int64_t i = 0; i < d; ++i) yr[i] = expf(xr[i] - mx) * scale;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------

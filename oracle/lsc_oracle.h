@@ -37,6 +37,7 @@ extern "C" {
 #define ORC_ACT_RELU 1  /* core/platform/simd.rs:552-556 */
 #define ORC_ACT_RELU6 2 /* core/platform/simd.rs:558-562 */
 #define ORC_ACT_SILU 3  /* core/operator/silu.rs:47-61   */
+#define ORC_ACT_GELU 4  /* core/operator/gelu.rs:77-103  */
 
 /* quantized dtypes understood by quantize_value / find_scale_zp */
 #define ORC_QUINT8 0
@@ -89,6 +90,12 @@ void orc_bn_fold(const float* w, const float* bias, const float* gamma, const fl
                  float* w_out, float* b_out);
 float orc_act(float x, int act);
 void orc_act_inplace(float* x, int64_t n, int act);
+/* LayerNorm over the last axis of [rows, d]: (x - mean) / sqrt(var + eps), then * gamma[i],
+   + beta[i] when given (core/operator/layernorm.rs:153-205). */
+void orc_layernorm(const float* x, float* y, int64_t rows, int64_t d, const float* gamma,
+                   const float* beta, float eps);
+/* Softmax over the last axis of [rows, d] (core/operator/softmax.rs:106-146). */
+void orc_softmax(const float* x, float* y, int64_t rows, int64_t d);
 
 /* ---- quantization (core/quantization/helpers.rs, core/cpu/quantized_ops.rs) ---- */
 float orc_round(float x, int rounding);

@@ -18,7 +18,7 @@ LIB_PATH = os.path.join(HERE, "liblsc_oracle.so")
 
 ROUND_HALF_AWAY = 0
 ROUND_HALF_EVEN = 1
-ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SILU = 0, 1, 2, 3
+ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SILU, ACT_GELU = 0, 1, 2, 3, 4
 QUINT8, QINT8, QINT32 = 0, 1, 2
 
 
@@ -58,6 +58,8 @@ def _declare(l):
         "orc_batchnorm_inference": [P, P, I64, I64, I64, P, P, P, P, F32],
         "orc_bn_fold": [P, P, P, P, P, P, F32, I64, I64, P, P],
         "orc_act_inplace": [P, I64, C.c_int],
+        "orc_layernorm": [P, P, I64, I64, P, P, F32],
+        "orc_softmax": [P, P, I64, I64],
         "orc_quantize_tensor": [P, I64, F32, I32, C.c_int, P],
         "orc_dequantize_tensor": [P, I64, F32, I32, C.c_int, P],
         "orc_quantize_sym": [P, P, I64, F32, C.c_int],
@@ -182,6 +184,27 @@ def bn_fold(w, bias, gamma, beta, mean, var, eps=1e-5):
 def act(x, kind):
     y = _c(x, np.float32).copy()
     lib().orc_act_inplace(_p(y), y.size, kind)
+    return y
+
+
+def layernorm(x, gamma=None, beta=None, eps=1e-5):
+    """LayerNorm over the last axis (layernorm.rs:153-205)."""
+    x = _c(x, np.float32)
+    d = x.shape[-1]
+    y = np.empty_like(x)
+    g = None if gamma is None else _c(gamma, np.float32)
+    b = None if beta is None else _c(beta, np.float32)
+    lib().orc_layernorm(_p(x), _p(y), x.size // max(d, 1), d, _p(g) if g is not None else None,
+                        _p(b) if b is not None else None, eps)
+    return y
+
+
+def softmax(x):
+    """Softmax over the last axis (softmax.rs:106-146)."""
+    x = _c(x, np.float32)
+    d = x.shape[-1]
+    y = np.empty_like(x)
+    lib().orc_softmax(_p(x), _p(y), x.size // max(d, 1), d)
     return y
 
 

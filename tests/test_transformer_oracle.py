@@ -1,0 +1,72 @@
+"""Oracle restatements of the transformer-block operators pinned to the reference's own tests:
+GELU (core/operator/gelu.rs tests), LayerNorm (layernorm.rs:250-300), Softmax
+(softmax.rs:224-270).  Also records the reference GELU's polynomial-tanh behaviour, which the
+CUDA path reproduces for parity."""
+import numpy as np
+
+from oracle import oracle as orc
+
+
+def gelu(x):
+    return orc.act(np.asarray(x, np.float32), orc.ACT_GELU)
+
+
+def test_gelu_reference_kats():
+    # gelu.rs tests: GELU(0) ~ 0, 0 < GELU(1) < 1, GELU(-1) < 0, small inputs keep their sign
+    g = gelu([0.0, 1.0, -1.0, -0.1, 0.1])
+    assert abs(g[0]) < 1e-4
+    assert 0.0 < g[1] < 1.0
+    assert g[2] < 0.0
+    assert g[3] < 0.0 and g[4] > 0.0
+    # test_gelu_slice: [-1, 0, 1]
+    s = gelu([-1.0, 0.0, 1.0])
+    assert s[0] < 0.0 and abs(s[1]) < 1e-4 and s[2] > 0.0
+
+
+def test_gelu_polynomial_tanh_and_saturation():
+    """The reference's tanh_approx is x - x^3/3 + x^5/5 - x^7/7 for |t| <= 5 (gelu.rs:91-103),
+    which leaves tanh for |t| > ~1: GELU(3) comes out large and negative, while past the +-5
+    cut-off (|x| > ~3.5) the tanh saturates and GELU(x) is x or -0."""
+    x = np.array([3.0, 4.0, -4.0, 10.0, -10.0], np.float32)
+    g = gelu(x)
+    assert g[0] < -100.0
+    assert g[1] == np.float32(4.0) and g[3] == np.float32(10.0)
+    assert g[2] == 0.0 and g[4] == 0.0
+    # the f32 expression in the reference's order
+    t = np.float32(0.7978845608) * (np.float32(1.5) + np.float32(0.044715) * (np.float32(1.5) ** 3))
+    t2 = t * t
+    th = t - (t2 * t) / np.float32(3) + (t2 * t * t2) / np.float32(5) - (t2 * t * t2 * t2) / np.float32(7)
+    assert gelu([1.5])[0] == np.float32(0.5) * np.float32(1.5) * (np.float32(1) + th)
+
+
+def test_layernorm_reference_kats():
+    y = orc.layernorm(np.array([[1.0, 2.0, 3.0, 4.0]], np.float32), eps=1e-5)
+    # test_normalize: mean 2.5, normalised variance ~ 1
+    assert abs(float(np.var(y)) - 1.0) < 0.01
+    assert abs(float(np.mean(y))) < 1e-6
+    # affine weight / bias as in test_layernorm_affine
+    g = np.array([1, 2, 3, 4], np.float32)
+    b = np.array([0.1, 0.2, 0.3, 0.4], np.float32)
+    ya = orc.layernorm(np.array([[1.0, 2.0, 3.0, 4.0]], np.float32), g, b)
+    np.testing.assert_allclose(ya, g * y + b, rtol=1e-6)
+
+
+def test_softmax_reference_kats():
+    y = orc.softmax(np.array([[1.0, 2.0, 3.0]], np.float32))
+    assert abs(float(y.sum()) - 1.0) < 1e-4 and (y > 0).all() and np.argmax(y) == 2
+    s = np.exp(-2.0) + np.exp(-1.0) + 1.0
+    np.testing.assert_allclose(y[0], np.exp(np.array([-2.0, -1.0, 0.0])) / s, rtol=1e-6)
+    big = orc.softmax(np.array([[1000.0, 1001.0, 1002.0]], np.float32))
+    assert abs(float(big.sum()) - 1.0) < 1e-4
+
+
+def test_layernorm_and_softmax_match_float64():
+    rng = np.random.default_rng(0)
+    x = rng.normal(size=(64, 768)).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, 768).astype(np.float32)
+    b = rng.normal(scale=0.1, size=768).astype(np.float32)
+    xd = x.astype(np.float64)
+    ref = (xd - xd.mean(1, keepdims=True)) / np.sqrt(xd.var(1, keepdims=True) + 1e-5) * g + b
+    np.testing.assert_allclose(orc.layernorm(x, g, b), ref, atol=2e-5, rtol=1e-5)
+    e = np.exp(xd - xd.max(1, keepdims=True))
+    np.testing.assert_allclose(orc.softmax(x), e / e.sum(1, keepdims=True), atol=1e-7, rtol=1e-5)
