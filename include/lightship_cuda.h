@@ -323,6 +323,28 @@ lsc_status lsc_find_scale_zp_per_channel_f32_noalloc(const float* x, int64_t cha
                                                      int32_t symmetric, float* scales_out,
                                                      int32_t* zero_points_out, lsc_stream stream);
 
+/* ---- FP16 attention products (transformer block) ---------------------------------------
+ * Batched C[bb][m][n] = alpha * sum_k A[bb][m][k] * B[bb][n][k] on the tensor cores (f16
+ * operands, f32 accumulation), bb = b * heads + h.  Operand element (bb, row, k) is at
+ * a + b*as_batch + (h + a_head0)*as_head + row*as_row + k (f16 elements; k contiguous; strides
+ * multiples of 8; base 16-byte aligned; K a multiple of 8), likewise for b; C element
+ * (bb, m, n) is at c + b*cs_batch + h*cs_head + m*cs_row + n, c_dtype LSC_DTYPE_F16 or F32.
+ * Serves scores = Q K^T / sqrt(d) and O = P V of the reference's attention
+ * (core/operator/attention.rs) on the FP16 path of the BERT-shaped workload; the reference's
+ * CPU backend has no FP16 kernel of its own. */
+lsc_status lsc_gemm_f16_batched(const void* a, int64_t as_row, int64_t as_head, int64_t as_batch,
+                                int64_t a_head0, const void* b, int64_t bs_row, int64_t bs_head,
+                                int64_t bs_batch, int64_t b_head0, int64_t batch, int64_t heads,
+                                int64_t m, int64_t n, int64_t k, float alpha, void* c,
+                                int32_t c_dtype, int64_t cs_row, int64_t cs_head, int64_t cs_batch,
+                                lsc_stream stream);
+/* y[b][h][c][r] = x[b][h + head0][r][c] (f16; x strides in elements), the K-major layout of V
+ * for O = P V.  No counterpart in the reference. */
+lsc_status lsc_transpose_heads_f16(const void* x, void* y, int64_t x_batch_stride,
+                                   int64_t x_head_stride, int64_t x_row_stride, int64_t head0,
+                                   int64_t batch, int64_t heads, int64_t rows, int64_t cols,
+                                   lsc_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

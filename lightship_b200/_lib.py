@@ -28,6 +28,7 @@ ERROR_UNSUPPORTED_LAYOUT = 14
 ERROR_TIMEOUT = 15
 
 ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SILU, ACT_GELU = 0, 1, 2, 3, 4
+DTYPE_F32, DTYPE_F16 = 0, 1  # lsc_dtype
 ROUND_HALF_AWAY, ROUND_HALF_EVEN = 0, 1
 FP32_3XTF32, FP32_TF32 = 0, 1
 MEM_HOST, MEM_DEVICE = 0, 1
@@ -118,6 +119,9 @@ SIGNATURES = {
     "lsc_find_scale_zp_per_channel_workspace_size": (C.c_uint64, [I64]),
     "lsc_find_scale_zp_per_channel_f32": (ST, [P, I64, I64, I32, I32, P, C.c_uint64, P, P, P]),
     "lsc_find_scale_zp_per_channel_f32_noalloc": (ST, [P, I64, I64, I32, I32, P, P, P]),
+    "lsc_gemm_f16_batched": (ST, [P, I64, I64, I64, I64, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, F32, P, I32,
+                                  I64, I64, I64, P]),
+    "lsc_transpose_heads_f16": (ST, [P, P, I64, I64, I64, I64, I64, I64, I64, I64, P]),
 }
 
 _lib = None

@@ -220,6 +220,11 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_mnmajor(uint32_t saddr, uint
 __host__ __device__ constexpr uint32_t idesc_i8(uint32_t m, uint32_t n) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
+// kind::f16 with f16 A and B (format 0) and f32 accumulation (D format 1), both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t m, uint32_t n) {
+  return (1u << 4) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
 __host__ __device__ constexpr uint32_t idesc_tf32(uint32_t m, uint32_t n, uint32_t b_mn_major) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (b_mn_major << 16) | ((n >> 3) << 17) |
          ((m >> 4) << 24);
@@ -233,6 +238,13 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
   asm volatile(

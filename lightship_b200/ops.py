@@ -88,3 +88,34 @@ def check_device() -> int:
     w = C.c_uint32(0)
     check(lib().lsc_check_device(C.byref(w)))
     return w.value
+
+
+def gemm_f16_batched(a, b, out, batch, heads, m, n, k, alpha=1.0, a_strides=None, b_strides=None,
+                     out_strides=None, a_head0=0, b_head0=0):
+    """Batched FP16 tensor-core GEMM with f32 accumulation (see ``lsc_gemm_f16_batched``):
+    out[bb][m][n] = alpha * sum_k a[bb][m][k] * b[bb][n][k], bb = batch_index * heads + head.
+
+    a, b: CUDA f16 tensors; ``*_strides`` = (row, head, batch) element strides, defaulting to a
+    contiguous [batch, heads, rows, k] layout; out: CUDA f16 or f32 tensor with
+    ``out_strides`` (row, head, batch), default contiguous [batch, heads, m, n].
+    """
+    _need(a, torch.float16, "a")
+    _need(b, torch.float16, "b")
+    if out.dtype not in (torch.float16, torch.float32) or not out.is_cuda:
+        raise ValueError("out: expected a CUDA f16 or f32 tensor")
+    a_strides = a_strides or (k, m * k, heads * m * k)
+    b_strides = b_strides or (k, n * k, heads * n * k)
+    out_strides = out_strides or (n, m * n, heads * m * n)
+    dt = _lib.DTYPE_F16 if out.dtype == torch.float16 else _lib.DTYPE_F32
+    check(lib().lsc_gemm_f16_batched(_ptr(a), *a_strides, a_head0, _ptr(b), *b_strides, b_head0, batch, heads,
+                                     m, n, k, float(alpha), _ptr(out), dt, *out_strides, _stream(a.device)))
+    return out
+
+
+def transpose_heads_f16(x, y, batch, heads, rows, cols, x_strides, head0=0):
+    """y[b][h][c][r] = x[b][h + head0][r][c]; x_strides = (batch, head, row) element strides."""
+    _need(x, torch.float16, "x")
+    _need(y, torch.float16, "y")
+    check(lib().lsc_transpose_heads_f16(_ptr(x), _ptr(y), *x_strides, head0, batch, heads, rows, cols,
+                                        _stream(x.device)))
+    return y
