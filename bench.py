@@ -28,7 +28,9 @@ the data path (NCCL is used only for barriers and the max-over-ranks timing redu
 
 ``--impl reference`` times the reference's CPU path (the oracle port; the Rust reference
 cannot be built here) on the host cores, rank 0 only, and prints the same metric.
-``--workload gemm`` makes the 4096^3 INT8 GEMM (TOPS) the headline instead.
+``--workload gemm`` makes the 4096^3 INT8 GEMM (TOPS) the headline instead; ``--workload bert``
+the BERT-base encoder block (sequences/s, batch 32 x seq 384 split over the GPUs), which the
+default line also carries on rank 0 as ``bert_block``.
 """
 from __future__ import annotations
 
@@ -57,6 +59,9 @@ GEMM_M = GEMM_N = GEMM_K = 4096
 GEMM_OPS = 2 * GEMM_M * GEMM_N * GEMM_K
 GEMM_WORKLOAD = ("int8 per-channel GEMM M=N=K=4096, int32 bias, requant int8 (half-even); dequant f32 "
                  "variant alongside")
+BERT_BATCH, BERT_SEQ, BERT_SEED = 32, 384, 20260501
+BERT_WORKLOAD = ("BERT-base encoder block (pre-LN, hidden 768, 12 heads x 64, FFN 3072 GELU), seq 384, batch 32 "
+                 "split over the GPUs; INT8 per-channel projections, FP16 attention")
 RESNET_WORKLOAD = ("ResNet-18 INT8 (conv1 7x7/2, 4 BasicBlock stages 64/128/256/512, maxpool 3x3/2, "
                    "global avgpool, FC-1000), 224x224x3 input, batch 256 split over the GPUs")
 
@@ -166,6 +171,8 @@ def run_reference(args):
         return 0
     if args.workload == "gemm":
         return run_reference_gemm(args)
+    if args.workload == "bert":
+        return run_reference_bert(args)
     # calibrate once on two images, then size each step to about two minutes in total
     _, _, scales = cpu_resnet_sample(2)
     t1, _, _ = cpu_resnet_sample(1, scales)
@@ -227,7 +234,134 @@ def run_reference_gemm(args):
     return 0
 
 
+def cpu_bert_sample(seqs, scales=None, threads=0):
+    """The oracle's quantized encoder block on `seqs` sequences of 384 tokens; returns seconds
+    and the scales (calibrated from this sample when none are given)."""
+    from lightship_b200.bert import HIDDEN, build_params
+    from oracle import oracle as orc
+    p = build_params(BERT_SEED)
+    x = np.random.default_rng(DATA_SEED).standard_normal((seqs * BERT_SEQ, HIDDEN)).astype(np.float32)
+    if scales is None:
+        scales = {"q1": 1.0, "q2": 1.0, "q3": 1.0, "u": 1.0}
+        for q, src in (("q1", "ln1"), ("q2", "o"), ("q3", "ln2")):
+            scales[q] = orc.find_scale_zp(orc.encoder_block_int8(x, p, scales, seqs, BERT_SEQ, threads=threads)[src])[0]
+        q3 = orc.encoder_block_int8(x, p, scales, seqs, BERT_SEQ, threads=threads)["q3"]
+        uf = orc.fc_i8_f32_weights(q3, scales["q3"], p["w1"], p["b1"], orc.ACT_GELU, 1.0, threads=threads)[1]
+        scales["u"] = orc.find_scale_zp(uf)[0]
+    t0 = time.perf_counter()
+    orc.encoder_block_int8(x, p, scales, seqs, BERT_SEQ, threads=threads)
+    return time.perf_counter() - t0, scales
+
+
+def run_reference_bert(args):
+    _, scales = cpu_bert_sample(1)
+    t1, _ = cpu_bert_sample(1, scales)
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    seqs = int(max(1, min(BERT_BATCH, budget / max(t1, 1e-6))))
+    for _ in range(args.warmup):
+        cpu_bert_sample(seqs, scales)
+    times = [cpu_bert_sample(seqs, scales)[0] for _ in range(args.steps)]
+    t = sum(times) / len(times)
+    value = seqs / t
+    line = {"metric": METRIC, "value": value, "unit": "sequences/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8+f16", "data": "synthetic",
+            "config": {"workload": BERT_WORKLOAD, "sequences_per_step": seqs},
+            "cpu_baseline": {"value": value, "unit": "sequences/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{seqs} sequences of 384 tokens per step through the oracle's quantized "
+                                       "encoder block (INT8 projections, f32 attention with f16 rounding points)"},
+            "e2e": {"value": value, "unit": "sequences/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # --------------------------------------------------------------------------- GPU side
+def bert_measure(torch, dev, batch, steps, warmup, be):
+    """The encoder block for `batch` sequences of 384 on this device.
+
+    Returns a dict: the graph-replayed block time (L2 flushed before every step), the per-stage
+    breakdown of one eager pass (events around each launch, queued behind a device sleep),
+    the INT8 projection kernels' TOPS, and the end-to-end time with the f32 input copied from
+    pinned host memory and the f32 output copied back every step."""
+    from lightship_b200 import _lib
+    from lightship_b200.bert import HIDDEN, INT8_OPS_PER_TOKEN, BertBlockInt8, attention_flops
+    blk = BertBlockInt8(be, batch, BERT_SEQ, dev, seed=BERT_SEED)
+    x = np.random.default_rng(DATA_SEED).standard_normal((batch * BERT_SEQ, HIDDEN)).astype(np.float32)
+    x_host = torch.from_numpy(x).pin_memory()
+    blk.calibrate(x_host.to(dev))
+    stream = torch.cuda.current_stream(dev)
+    evs = {}
+
+    def wrap(fn, name_of):
+        def run(*a, **k):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            fn(*a, **k)
+            e.record(stream)
+            evs.setdefault(name_of(a), []).append((s, e))
+        return run
+
+    orig_run, orig_att = blk._run, blk._attention
+    blk._run = wrap(orig_run, lambda a: a[0])
+    blk._attention = wrap(orig_att, lambda a: "attention")
+    for _ in range(3):
+        torch.cuda.synchronize(dev)
+        torch.cuda._sleep(20_000_000)
+        blk.forward_device()
+    torch.cuda.synchronize(dev)
+    blk._run, blk._attention = orig_run, orig_att
+    stage = {k: float(np.mean([s.elapsed_time(e) for s, e in v])) for k, v in evs.items()}
+    tokens = batch * BERT_SEQ
+    gemm_ms = sum(stage[k] for k in ("qkv", "out", "ffn_up_i8", "ffn_down"))
+    gemm_tops = INT8_OPS_PER_TOKEN * tokens / (gemm_ms * 1e-3) / 1e12
+
+    graph = blk.capture()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(warmup):
+        flush.zero_()
+        graph.replay()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize(dev)
+    for s, e in ev:
+        flush.zero_()
+        s.record(stream)
+        graph.replay()
+        e.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = float(np.mean([s.elapsed_time(e) for s, e in ev]))
+
+    lib = _lib.lib()
+    out_host = torch.empty((tokens, HIDDEN), dtype=torch.float32).pin_memory()
+    nbytes = tokens * HIDDEN * 4
+    sptr = C.c_void_p(stream.cuda_stream)
+
+    def e2e_step():
+        _lib.check(lib.lsc_memcpy_h2d(C.c_void_p(blk.buf["x"].data_ptr()), C.c_void_p(x_host.data_ptr()), nbytes,
+                                      sptr))
+        graph.replay()
+        _lib.check(lib.lsc_memcpy_d2h(C.c_void_p(out_host.data_ptr()), C.c_void_p(blk.buf["out"].data_ptr()),
+                                      nbytes, sptr))
+
+    e2e_steps = max(3, min(steps, 20))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ee.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = es.elapsed_time(ee) / e2e_steps
+    e2e_ok = bool(torch.equal(out_host, blk.buf["out"].cpu()))
+    del graph
+    blk.graph = None
+    return {"ms": ms, "stage_ms": stage, "gemm_ms": gemm_ms, "gemm_tops": gemm_tops,
+            "attention_tflops": attention_flops(batch, BERT_SEQ) / (stage["attention"] * 1e-3) / 1e12,
+            "e2e_ms": e2e_ms, "bytes": nbytes, "e2e_ok": e2e_ok, "scales": dict(blk.scales),
+            "launches": blk.kernel_launches()}
+
+
 def gemm_measure(torch, dev, steps, warmup):
     """The 4096^3 INT8 chain on this device, timed per output variant.
 
@@ -344,6 +478,49 @@ def run_gpu(args):
                              for k, v in variants.items()},
                 "gpu_launches": 3 * args.steps, "clocks": clocks}
         if world > 1:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return 0
+
+    if args.workload == "bert":
+        from lightship_b200.backend import CudaBackend, GpuBackendConfig
+        if BERT_BATCH % world:
+            raise SystemExit(f"batch {BERT_BATCH} does not split over {world} GPUs")
+        per = BERT_BATCH // world
+        be = CudaBackend(GpuBackendConfig(device_id=local, arena_bytes=64 << 20))
+        sampler = ClockSampler(uuid)
+        sampler.start()
+        barrier()
+        r = bert_measure(torch, dev, per, args.steps, args.warmup, be)
+        barrier()
+        clocks = sampler.stop()
+        ms_max = max_over_ranks(r["ms"])
+        e2e_max = max_over_ranks(r["e2e_ms"])
+        line = {"metric": METRIC, "value": BERT_BATCH / (ms_max * 1e-3), "unit": "sequences/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8+f16", "data": "synthetic",
+                "config": {"workload": BERT_WORKLOAD, "global_batch": BERT_BATCH, "per_gpu_batch": per,
+                           "seq_len": BERT_SEQ, "parallelism": f"batch split x{world} (no collective)",
+                           "l2": "flushed (256 MiB write) before every timed step"},
+                "roofline": {"bound": "tensor", "kernel": "contraction_i8_kernel (QKV/out/FFN projections)",
+                             "achieved": r["gemm_tops"], "peak": int8_peak, "unit": "TOPS",
+                             "frac": r["gemm_tops"] / int8_peak, "traffic": None, "peak_source": peak_source,
+                             "projection_share_of_step": r["gemm_ms"] / r["ms"]},
+                "stage_ms": r["stage_ms"], "attention_tflops": r["attention_tflops"],
+                "e2e": {"value": BERT_BATCH / (e2e_max * 1e-3), "unit": "sequences/s",
+                        "h2d_bytes_per_step": r["bytes"] * world, "d2h_bytes_per_step": r["bytes"] * world,
+                        "api": "lsc_memcpy_h2d + block graph + lsc_memcpy_d2h", "matches_device_run": r["e2e_ok"]},
+                "gpu_launches": r["launches"] * args.steps, "clocks": clocks}
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            seqs = 16
+            dt, _ = cpu_bert_sample(seqs, r["scales"])
+            line["cpu_baseline"] = {"value": seqs / dt, "unit": "sequences/s", "cores": os.cpu_count(),
+                                    "kind": "port", "sample": f"{seqs} sequences of 384 tokens through the "
+                                                              f"oracle's quantized encoder block, {dt:.2f} s"}
+        be.close()
+        if world > 1:
+            dist.barrier()
             dist.destroy_process_group()
         if rank == 0:
             print(json.dumps(line), flush=True)
@@ -472,6 +649,13 @@ def run_gpu(args):
                                   "traffic": load_traffic("contraction_i8_gemm_4096.md"),
                                   "variants": {k: {"TOPS": v[0], "ms_per_launch": v[1],
                                                    "roofline_frac": v[0] / int8_peak} for k, v in variants.items()}}
+    if rank == 0 and not args.no_bert:
+        r = bert_measure(torch, dev, BERT_BATCH, max(20, min(args.steps, 100)), 5, be)
+        line["bert_block"] = {"value": BERT_BATCH / (r["ms"] * 1e-3), "unit": "sequences/s", "ms_per_block": r["ms"],
+                              "workload": BERT_WORKLOAD, "projection_tops": r["gemm_tops"],
+                              "projection_roofline_frac": r["gemm_tops"] / int8_peak,
+                              "attention_tflops": r["attention_tflops"], "stage_ms": r["stage_ms"],
+                              "e2e_sequences_per_s": BERT_BATCH / (r["e2e_ms"] * 1e-3)}
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             imgs = 24
@@ -496,11 +680,12 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["lightship", "reference"], default="lightship")
-    ap.add_argument("--workload", choices=["resnet18", "gemm"], default="resnet18")
+    ap.add_argument("--workload", choices=["resnet18", "gemm", "bert"], default="resnet18")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH,
                     help="global ResNet batch (default 256, the benchmark's; smaller only for profiling)")
     ap.add_argument("--no-gemm", action="store_true", help="skip the 4096^3 GEMM sub-measurement")
+    ap.add_argument("--no-bert", action="store_true", help="skip the encoder-block sub-measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -675,7 +675,9 @@ lsc_status execute_activation(const lsc_op* op, const lsc_tensor* in, int n_in, 
 // last axis's length, epsilon from bn_epsilon (0 -> the reference's 1e-5).  Softmax
 // (operator/softmax.rs:37-169): the last axis (SoftmaxAxis::Last, the reference's default).
 // Both keep the input's storage type (f32 or f16) and shape.
-lsc_status compile_layernorm(lsc_op* op, const lsc_tensor* in, int n_in, int n_out) {
+// An int8 output (QInt8, one scale, zero point 0) makes the kernel quantize the normalised
+// row as a following Quantize operator would (helpers.rs:138-156); its scale is fixed here.
+lsc_status compile_layernorm(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_tensor* out, int n_out) {
   if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "LayerNorm: missing input or output");
   const lsc_tensor& x = in[0];
   if (x.dtype != LSC_DTYPE_F32 && x.dtype != LSC_DTYPE_F16)
@@ -683,6 +685,18 @@ lsc_status compile_layernorm(lsc_op* op, const lsc_tensor* in, int n_in, int n_o
   if (x.ndim < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "LayerNorm requires at least 1D input");
   op->kind = OpKind::kLayerNorm;
   op->qdtype = x.dtype;
+  op->q_channels = 0;
+  if (is_int8(out[0].dtype)) {
+    const lsc_quant& q = out[0].quant;
+    if (q.count != 1 || !q.scale || !(q.scale[0] > 0.0f))
+      return set_error(LSC_ERROR_INVALID_ARGUMENT, "LayerNorm: int8 output '%s' needs one scale > 0", tname(out[0]));
+    if (q.zero_point && q.zero_point[0] != 0)
+      return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "LayerNorm: int8 output must be symmetric (zero point 0)");
+    op->q_channels = 1;  // marks the quantized output
+    op->q_scale0 = q.scale[0];
+  } else if (out[0].dtype != x.dtype) {
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "LayerNorm: output dtype must match the input or be int8");
+  }
   const int64_t d = x.shape[x.ndim - 1];
   op->n = d;
   op->s_out = bn_eps(op->desc);
@@ -727,14 +741,20 @@ lsc_status execute_rownorm(const lsc_op* op, const lsc_tensor* in, int n_in, lsc
   const int64_t total = numel(x);
   if (total < 0) return set_error(LSC_ERROR_SHAPE_MISMATCH, "bad shape");
   const int64_t esz = dtype_size(x.dtype);
-  if (out[0].dtype != x.dtype) return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "output dtype must match the input");
+  const bool quantized = ln && op->q_channels == 1;
+  if (quantized ? !is_int8(out[0].dtype) : out[0].dtype != x.dtype)
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "output dtype %d does not match the compiled operator",
+                     out[0].dtype);
   const void* xd = nullptr;
   void* yd = nullptr;
   lsc_status st;
-  if ((st = s.input(x, total * esz, &xd)) || (st = s.output(out[0], total * esz, &yd))) return st;
+  if ((st = s.input(x, total * esz, &xd)) || (st = s.output(out[0], total * (quantized ? 1 : esz), &yd))) return st;
   out[0].ndim = x.ndim;
   for (int i = 0; i < x.ndim; ++i) out[0].shape[i] = x.shape[i];
   const int64_t rows = d > 0 ? total / d : 0;
+  if (quantized)
+    return launch_layernorm(xd, nullptr, x.dtype, rows, d, op->scale, op->bias_f32, op->s_out, s.st,
+                            static_cast<int8_t*>(yd), op->q_scale0, op->rounding);
   if (ln) return launch_layernorm(xd, yd, x.dtype, rows, d, op->scale, op->bias_f32, op->s_out, s.st);
   return launch_softmax(xd, yd, x.dtype, rows, d, s.st);
 }

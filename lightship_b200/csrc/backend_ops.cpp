@@ -161,7 +161,7 @@ lsc_status compile_qgemm(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_t
   }
   for (int i = 0; i < n_out; ++i) {
     const int32_t dt = out[i].dtype;
-    if (!(is_int8(dt) || dt == LSC_DTYPE_F32 || dt == LSC_DTYPE_I32 || dt == LSC_DTYPE_QINT32))
+    if (!(is_int8(dt) || dt == LSC_DTYPE_F32 || dt == LSC_DTYPE_F16 || dt == LSC_DTYPE_I32 || dt == LSC_DTYPE_QINT32))
       return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "output '%s': dtype %d", tname(out[i]), dt);
     if (is_int8(dt)) {
       float so = op->desc.output_scale;
@@ -208,21 +208,41 @@ lsc_status execute_qgemm(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_t
   int8_t* o_i8 = nullptr;
   float* o_f32 = nullptr;
   int32_t* o_i32 = nullptr;
+  GemmExtras ex;
+  float s_out = op->s_out;
   for (int i = 0; i < n_out; ++i) {
     lsc_tensor& t = out[i];
     const int64_t es = dtype_size(t.dtype);
     void* d = nullptr;
     lsc_status st = s.output(t, m * n * es, &d);
     if (st) return st;
-    if (is_int8(t.dtype)) o_i8 = static_cast<int8_t*>(d);
-    else if (t.dtype == LSC_DTYPE_F32) o_f32 = static_cast<float*>(d);
-    else o_i32 = static_cast<int32_t*>(d);
+    if (is_int8(t.dtype)) {
+      o_i8 = static_cast<int8_t*>(d);
+      // a calibrated output scale carried by the output tensor overrides the compiled one
+      if (t.quant.count > 0 && t.quant.scale && t.quant.scale[0] > 0.0f) s_out = t.quant.scale[0];
+    } else if (t.dtype == LSC_DTYPE_F32) {
+      o_f32 = static_cast<float*>(d);
+    } else if (t.dtype == LSC_DTYPE_F16) {
+      ex.out_f16 = d;
+    } else {
+      o_i32 = static_cast<int32_t*>(d);
+    }
     set_shape(t, {m, n});
+  }
+  // optional f32 residual (execute-time input 1), [M, N], added before the activation
+  if (n_in >= 2 && in[1].data) {
+    const lsc_tensor& r = in[1];
+    if (r.dtype != LSC_DTYPE_F32) return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "GEMM residual must be f32");
+    if (numel(r) != m * n) return set_error(LSC_ERROR_SHAPE_MISMATCH, "GEMM residual '%s' must be [M, N]", tname(r));
+    const void* rd = nullptr;
+    lsc_status st = s.input(r, m * n * 4, &rd);
+    if (st) return st;
+    ex.res_f32 = static_cast<const float*>(rd);
   }
   if (m == 0) return LSC_SUCCESS;
   return launch_gemm_i8(static_cast<const int8_t*>(ad), static_cast<const int8_t*>(op->w), m, n, kp,
-                        op->bias_i32, op->scale, op->s_out, op->act, op->rounding, o_i8, o_f32,
-                        o_i32, n, s.st);
+                        op->bias_i32, op->scale, s_out, op->act, op->rounding, o_i8, o_f32,
+                        o_i32, n, s.st, &ex);
 }
 
 // ---------------------------------------------------------------- quantize / dequantize
@@ -335,7 +355,7 @@ lsc_status compile_op(lsc_backend* be, lsc_op* op, const lsc_tensor* in, int n_i
     case LSC_OP_RELU6: return compile_activation(op, in, n_in, n_out, LSC_ACT_RELU6);
     case LSC_OP_SILU: return compile_activation(op, in, n_in, n_out, LSC_ACT_SILU);
     case LSC_OP_GELU: return compile_activation(op, in, n_in, n_out, LSC_ACT_GELU);
-    case LSC_OP_LAYERNORM: return compile_layernorm(op, in, n_in, n_out);
+    case LSC_OP_LAYERNORM: return compile_layernorm(op, in, n_in, out, n_out);
     case LSC_OP_SOFTMAX: return compile_softmax(op, in, n_in, n_out);
     case LSC_OP_QUANTIZE: {
       if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Quantize needs 1 input and 1 output");

@@ -140,7 +140,7 @@ lsc_status compile_pool(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, b
 lsc_status execute_pool(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out,
                         Staging& s);
 lsc_status compile_activation(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, int act);
-lsc_status compile_layernorm(lsc_op* op, const lsc_tensor* in, int n_in, int n_out);
+lsc_status compile_layernorm(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_tensor* out, int n_out);
 lsc_status compile_softmax(lsc_op* op, const lsc_tensor* in, int n_in, int n_out);
 lsc_status execute_rownorm(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out,
                            Staging& s);

@@ -25,6 +25,8 @@
 
 #include <mutex>
 
+#include <cuda_fp16.h>
+
 #include "epilogue.cuh"
 #include "lsc_internal.h"
 #include "sm100.cuh"
@@ -42,6 +44,8 @@ struct I8Params {
   int8_t* out_i8;
   float* out_f32;
   int32_t* out_i32;
+  __half* out_f16;        // optional f16 copy of the f32 output (after the activation)
+  const float* res_f32;   // optional f32 residual [M, ldo] added before the activation
   int64_t ldo;
   int32_t vec_ok;  // 16-byte vector stores are legal for full column chunks
   uint32_t* err;
@@ -142,7 +146,7 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
         if (col0 + j < p.n) p.out_i32[base + j] = acc[j];
     }
   }
-  if (!p.out_f32 && !p.out_i8) return;
+  if (!p.out_f32 && !p.out_i8 && !p.out_f16) return;
   float y[W];
 #pragma unroll
   for (int j = 0; j < W; j += 4) {
@@ -170,8 +174,25 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
           y[j] = __fadd_rn(y[j], __fmul_rn(__int2float_rn(p.residual[base + j]), p.res_scale));
     }
   }
+  if (p.res_f32) {
+    if (vec) {
+      const float4* rp = reinterpret_cast<const float4*>(p.res_f32 + base);
+#pragma unroll
+      for (int v = 0; v < W / 4; ++v) {
+        const float4 r4 = __ldg(rp + v);
+        y[4 * v + 0] = __fadd_rn(y[4 * v + 0], r4.x);
+        y[4 * v + 1] = __fadd_rn(y[4 * v + 1], r4.y);
+        y[4 * v + 2] = __fadd_rn(y[4 * v + 2], r4.z);
+        y[4 * v + 3] = __fadd_rn(y[4 * v + 3], r4.w);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < W; ++j)
+        if (col0 + j < p.n) y[j] = __fadd_rn(y[j], p.res_f32[base + j]);
+    }
+  }
   // A ReLU feeding only the int8 output is applied inside the requantization's clamp.
-  const bool relu_folded = ACT == LSC_ACT_RELU && !p.out_f32 && p.inv_s_out > 0.0f;
+  const bool relu_folded = ACT == LSC_ACT_RELU && !p.out_f32 && !p.out_f16 && p.inv_s_out > 0.0f;
   if (!relu_folded) {
 #pragma unroll
     for (int j = 0; j < W; ++j) y[j] = apply_act<ACT>(y[j]);
@@ -185,6 +206,25 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
 #pragma unroll
       for (int j = 0; j < W; ++j)
         if (col0 + j < p.n) p.out_f32[base + j] = y[j];
+    }
+  }
+  if (p.out_f16) {
+    __half* o = p.out_f16 + base;
+    if (vec) {
+#pragma unroll
+      for (int v = 0; v < W / 8; ++v) {
+        uint32_t h[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const __half2 hh = __floats2half2_rn(y[8 * v + 2 * t], y[8 * v + 2 * t + 1]);
+          h[t] = *reinterpret_cast<const uint32_t*>(&hh);
+        }
+        reinterpret_cast<uint4*>(o)[v] = make_uint4(h[0], h[1], h[2], h[3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < W; ++j)
+        if (col0 + j < p.n) o[j] = __float2half_rn(y[j]);
     }
   }
   if (p.out_i8) {
@@ -796,9 +836,10 @@ int pair_tile_n(int64_t m, int64_t n) {
 }
 
 lsc_status check_common(int64_t m, int64_t n, int act, int rounding, const float* scale,
-                        int8_t* out_i8, float* out_f32, int32_t* out_i32, const char* who) {
+                        int8_t* out_i8, float* out_f32, int32_t* out_i32, const char* who,
+                        const void* out_f16 = nullptr) {
   if (m < 0 || n < 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: negative size", who);
-  if (!out_i8 && !out_f32 && !out_i32)
+  if (!out_i8 && !out_f32 && !out_i32 && !out_f16)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: no output given", who);
   if (m > 0 && n > 0 && !scale) return set_error(LSC_ERROR_INVALID_ARGUMENT, "%s: null scale", who);
   if (act < LSC_ACT_NONE || act > LSC_ACT_GELU)
@@ -834,8 +875,9 @@ void fill_outputs(I8Params& p, const int32_t* bias, const float* scale, float s_
 lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k,
                           const int32_t* bias, const float* scale, float s_out, int act,
                           int rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
-                          int64_t ldo, cudaStream_t stream) {
-  lsc_status st = check_common(m, n, act, rounding, scale, out_i8, out_f32, out_i32, "gemm_i8");
+                          int64_t ldo, cudaStream_t stream, const GemmExtras* extras) {
+  lsc_status st = check_common(m, n, act, rounding, scale, out_i8, out_f32, out_i32, "gemm_i8",
+                               extras ? extras->out_f16 : nullptr);
   if (st) return st;
   if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_i8: size too large");
@@ -872,6 +914,11 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
   p.n = static_cast<int32_t>(n);
   p.k = static_cast<int32_t>(k);
   fill_outputs(p, bias, scale, s_out, rounding, out_i8, out_f32, out_i32, ldo, ds->err_word);
+  if (extras) {
+    p.out_f16 = static_cast<__half*>(extras->out_f16);
+    p.res_f32 = extras->res_f32;
+    if ((reinterpret_cast<uintptr_t>(p.out_f16) | reinterpret_cast<uintptr_t>(p.res_f32)) & 15) p.vec_ok = 0;
+  }
   if (pair) return launch_pair(ta, tw, p, act, ds->sm_count, stream);
   return launch_bn<0>(bn, ta, tw, p, act, ds->sm_count, stream);
 }

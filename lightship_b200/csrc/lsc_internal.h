@@ -70,10 +70,16 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
 
 // INT8 GEMM + requant/dequant epilogue (contraction_i8.cu).  ldo = row stride of the outputs in
 // elements.  Validates its arguments.
+// Optional extras of the GEMM chain: an f16 copy of the (activated) f32 result and an f32
+// residual [M, ldo] added before the activation.
+struct GemmExtras {
+  void* out_f16 = nullptr;
+  const float* res_f32 = nullptr;
+};
 lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k,
                           const int32_t* bias, const float* scale, float s_out, int act,
                           int rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
-                          int64_t ldo, cudaStream_t stream);
+                          int64_t ldo, cudaStream_t stream, const GemmExtras* extras = nullptr);
 
 // FP32 contractions as split-TF32 (contraction_tf32.cu).  GEMM: A [M,K] and B [N,K] K-major
 // (hi and lo parts; lo unused when split == false), K a multiple of 4, output row-major with
@@ -106,8 +112,12 @@ lsc_status launch_quantize_nchw_to_nhwc_i8(const float* x, int8_t* y, int64_t n,
                                            int64_t hw, int64_t cp, float scale, int rounding,
                                            cudaStream_t st);
 // Row-wise LayerNorm / Softmax over the last axis of [rows, d], f32 or f16 storage (norm.cu).
+// LayerNorm writes int8 to q (R(y / q_scale), saturated) instead of y when q is non-null.
 lsc_status launch_layernorm(const void* x, void* y, int32_t dtype, int64_t rows, int64_t d, const float* gamma,
-                            const float* beta, float eps, cudaStream_t st);
+                            const float* beta, float eps, cudaStream_t st, int8_t* q = nullptr,
+                            float q_scale = 0.0f, int rounding = LSC_ROUND_HALF_AWAY);
+// RN(1 / s) when s and 1/s are normal floats, else 0 (pool.cu).
+float reciprocal_or_zero(float s);
 lsc_status launch_softmax(const void* x, void* y, int32_t dtype, int64_t rows, int64_t d, cudaStream_t st);
 
 lsc_status launch_quantize_nchw_to_s2d_i8(const float* x, int8_t* y, int64_t n, int64_t c, int64_t h,

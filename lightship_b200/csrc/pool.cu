@@ -190,13 +190,6 @@ __global__ void avgpool_i8_kernel(const int8_t* __restrict__ x, int64_t n, int64
   }
 }
 
-// RN(1 / s) when s and its reciprocal are normal floats (the reciprocal requantization's
-// precondition), else 0, which makes every element take the division.
-float reciprocal_or_zero(float s) {
-  const float inv = 1.0f / s;
-  return (std::isnormal(s) && std::isnormal(inv)) ? inv : 0.0f;
-}
-
 int grid_p(int64_t n, int sm_count) {
   int64_t g = (n + 255) / 256;
   const int64_t cap = static_cast<int64_t>(sm_count) * 8;
@@ -205,6 +198,13 @@ int grid_p(int64_t n, int sm_count) {
 }
 
 }  // namespace
+
+// RN(1 / s) when s and its reciprocal are normal floats (the reciprocal requantization's
+// precondition), else 0, which makes every element take the division.
+float reciprocal_or_zero(float s) {
+  const float inv = 1.0f / s;
+  return (std::isnormal(s) && std::isnormal(inv)) ? inv : 0.0f;
+}
 
 lsc_status launch_quantize_nchw_to_nhwc_i8(const float* x, int8_t* y, int64_t n, int64_t c,
                                            int64_t hw, int64_t cp, float scale, int rounding,

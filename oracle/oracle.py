@@ -413,3 +413,70 @@ def avgpool_i8_nhwc(x, s_in, s_out=1.0, rounding=ROUND_HALF_AWAY):
     yf = np.empty((n, c), np.float32)
     lib().orc_avgpool_i8_nhwc(_p(x), n, h * w, c, s_in, s_out, rounding, _p(yq), _p(yf))
     return yq, yf
+
+
+# ---------------------------------------------------------------- transformer encoder block
+def fc_i8_f32_weights(a_q, s_a, w, b, act=ACT_NONE, s_out=1.0, rounding=ROUND_HALF_AWAY, threads=0):
+    """FullyConnected on int8 activations (scale s_a) with f32 weights [N, K] quantized per
+    output channel and an f32 bias quantized to int32 in accumulator units
+    (quantized_ops.rs:13-48 with helpers.rs:101-160): returns (int8, f32) outputs of the chain."""
+    wq, sw = quantize_weights_per_channel(w)
+    scale = (np.float32(s_a) * sw).astype(np.float32)
+    bq = np.array([quantize_value(float(b[o]), float(scale[o]), 0, QINT32) for o in range(w.shape[0])], np.int32)
+    oi8, of32, _ = gemm_i8_chain(a_q, wq, bq, scale, act, s_out, rounding, threads, want=("i8", "f32"))
+    return oi8, of32
+
+
+def attention_scores_f16(qkv, batch, seq, heads, head_dim, threads=0):
+    """Q K^T / sqrt(head_dim) per head from a [batch*seq, 3*heads*head_dim] f16 projection
+    (Q, K, V head-major), products accumulated in f32 (the reference GEMM) and stored as f16."""
+    x = np.asarray(qkv, np.float16).astype(np.float32).reshape(batch, seq, 3, heads, head_dim)
+    out = np.empty((batch, heads, seq, seq), np.float16)
+    alpha = np.float32(1.0 / np.sqrt(head_dim))
+    for bi in range(batch):
+        for h in range(heads):
+            q = np.ascontiguousarray(x[bi, :, 0, h, :])
+            kt = np.ascontiguousarray(x[bi, :, 1, h, :].T)
+            out[bi, h] = (matmul(q, kt, threads) * alpha).astype(np.float16)
+    return out
+
+
+def attention_context(p, qkv, batch, seq, heads, head_dim, threads=0):
+    """P V per head: f16 probabilities [batch, heads, seq, seq] times the f16 V heads,
+    accumulated in f32, written token-major [batch*seq, heads*head_dim] f32."""
+    x = np.asarray(qkv, np.float16).astype(np.float32).reshape(batch, seq, 3, heads, head_dim)
+    pf = np.asarray(p, np.float16).astype(np.float32)
+    out = np.empty((batch, seq, heads, head_dim), np.float32)
+    for bi in range(batch):
+        for h in range(heads):
+            out[bi, :, h, :] = matmul(np.ascontiguousarray(pf[bi, h]), np.ascontiguousarray(x[bi, :, 2, h, :]),
+                                      threads)
+    return out.reshape(batch * seq, heads * head_dim)
+
+
+def encoder_block_int8(x, params, scales, batch, seq, heads=12, head_dim=64, rounding=ROUND_HALF_AWAY,
+                       threads=0):
+    """A pre-LayerNorm encoder block with INT8 projections and f16 attention, composed of the
+    reference operators: LayerNorm (layernorm.rs:153-205), per-tensor quantize
+    (helpers.rs:138-156), the INT8 chain, Softmax (softmax.rs:106-146), GELU (gelu.rs:77-103).
+    ``scales`` holds the per-tensor activation scales q1 (LN1 out), q2 (attention context),
+    q3 (LN2 out) and u (GELU out).  Returns every intermediate by name."""
+    p = params
+    r = {}
+    r["ln1"] = layernorm(x, p["ln1_g"], p["ln1_b"], 1e-5)
+    r["q1"] = quantize_tensor(r["ln1"], scales["q1"], 0)
+    r["qkv"] = fc_i8_f32_weights(r["q1"], scales["q1"], p["wqkv"], p["bqkv"], rounding=rounding,
+                                 threads=threads)[1].astype(np.float16)
+    r["scores"] = attention_scores_f16(r["qkv"], batch, seq, heads, head_dim, threads)
+    r["p"] = softmax(r["scores"].astype(np.float32)).astype(np.float16)
+    r["o"] = attention_context(r["p"], r["qkv"], batch, seq, heads, head_dim, threads)
+    r["q2"] = quantize_tensor(r["o"], scales["q2"], 0)
+    r["h"] = fc_i8_f32_weights(r["q2"], scales["q2"], p["wo"], p["bo"], rounding=rounding,
+                               threads=threads)[1] + np.asarray(x, np.float32)
+    r["ln2"] = layernorm(r["h"], p["ln2_g"], p["ln2_b"], 1e-5)
+    r["q3"] = quantize_tensor(r["ln2"], scales["q3"], 0)
+    r["u"] = fc_i8_f32_weights(r["q3"], scales["q3"], p["w1"], p["b1"], ACT_GELU, scales["u"], rounding,
+                               threads)[0]
+    r["out"] = fc_i8_f32_weights(r["u"], scales["u"], p["w2"], p["b2"], rounding=rounding,
+                                 threads=threads)[1] + r["h"]
+    return r

@@ -47,7 +47,10 @@ def test_gemm_i8_gelu_epilogue(cuda, m, n, k):
 
 def test_gelu_operator_f32(be):
     from lightship_b200.backend import DataType, OperatorDef, OperatorType, Tensor
+    rng = np.random.default_rng(17)
+    tiny = np.float32(2.0) ** rng.integers(-149, -100, 20000).astype(np.float32)
     x = np.concatenate([np.linspace(-12, 12, 40001, dtype=np.float32),
+                        rng.uniform(-4, 4, 1 << 21).astype(np.float32), tiny, -tiny,
                         np.array([0.0, -0.0, np.inf, -np.inf, np.nan], np.float32)])
     xt = Tensor("x", [x.size], DataType.F32, x)
     yt = Tensor("y", [x.size], DataType.F32, np.zeros_like(x))
@@ -80,9 +83,10 @@ def _rownorm(be, kind, x, dtype, gamma=None, beta=None, eps=0.0):
     return xs, yd.cpu().numpy()
 
 
-@pytest.mark.parametrize("rows,d", [(384 * 4, 768), (33, 1000), (7, 4096), (5, 1)])
+@pytest.mark.parametrize("rows,d", [(384 * 4, 768), (33, 1000), (7, 4096), (5, 1), (9, 100), (3, 6)])
 def test_layernorm_f32(be, rows, d):
-    """f32: |Δ| <= 2e-5 + 2e-5 |y| against the oracle (different summation order)."""
+    """f32: |Δ| <= 2e-5 + 2e-5 |y| against the oracle (different summation order).  Rows of
+    up to 1024 (d % 4 == 0) take the warp-per-row kernel, the rest the CTA-per-row one."""
     rng = np.random.default_rng(rows + d)
     x = (rng.normal(size=(rows, d)) * 3 + 1).astype(np.float32)
     g = rng.uniform(0.5, 1.5, d).astype(np.float32)
@@ -101,10 +105,10 @@ def test_layernorm_f16_and_default_eps(be):
     np.testing.assert_allclose(y.astype(np.float32), want.astype(np.float32), atol=2e-3, rtol=1e-3)
 
 
-@pytest.mark.parametrize("rows,d", [(32 * 12 * 384 // 8, 384), (50, 1000), (3, 1)])
+@pytest.mark.parametrize("rows,d", [(32 * 12 * 384 // 8, 384), (50, 1000), (3, 1), (17, 12), (4, 1028)])
 def test_softmax_f32(be, rows, d):
-    """f32: |Δ| <= 1e-7 + 1e-5 |y| against the oracle (device exp is the correctly rounded
-    one, the oracle's glibc expf; tree-ordered sum)."""
+    """f32: |Δ| <= 1e-7 + 1e-5 |y| against the oracle (device exp is CUDA's expf, within 2 ulp;
+    the oracle's is glibc's; tree-ordered sum)."""
     rng = np.random.default_rng(rows + d)
     x = (rng.normal(size=(rows, d)) * 4).astype(np.float32)
     _, y = _rownorm(be, "sm", x, np.float32)
@@ -122,12 +126,97 @@ def test_softmax_f16_attention_rows(be):
     np.testing.assert_allclose(y.astype(np.float32), want.astype(np.float32), atol=2e-4, rtol=1e-3)
 
 
-def test_softmax_large_values_and_in_place(be):
+@pytest.mark.parametrize("pad", [0, 1])
+def test_softmax_large_values_and_in_place(be, pad):
+    """Rows of 3 (CTA kernel) and of 4 (warp kernel), updated in place; -inf entries give 0."""
     import torch
     from lightship_b200.backend import DataType, OperatorDef, OperatorType, Tensor
     x = np.array([[1000.0, 1001.0, 1002.0], [-1e30, 0.0, 1e30]], np.float32)
+    if pad:
+        x = np.concatenate([x, np.full((2, 1), -np.inf, np.float32)], axis=1)
     xd = torch.from_numpy(x).cuda()
     t = Tensor("x", list(x.shape), DataType.F32, xd)
     op = be.compile_operator(OperatorDef("sm", OperatorType.Softmax), None, [t], [t])
     be.execute(op, [t], [t])
     np.testing.assert_allclose(xd.cpu().numpy(), orc.softmax(x), atol=1e-7, rtol=1e-5)
+
+
+def _assert_quantized_close(q, ref, scale, slack):
+    """q equals quantize_tensor(ref, scale) except where ref / scale lies within `slack` of a
+    rounding boundary (a tolerance-level difference in ref may move it across), and there by one."""
+    want = orc.quantize_tensor(ref, scale, 0).astype(np.int32)
+    diff = q.astype(np.int32) - want
+    t = np.abs(ref.astype(np.float64) / scale)
+    near = np.abs(t - np.floor(t) - 0.5) <= slack
+    assert np.abs(diff).max() <= 1
+    assert (diff[~near] == 0).all(), int((diff[~near] != 0).sum())
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float16])
+@pytest.mark.parametrize("rounding", [0, 1])
+def test_layernorm_int8_output(be, dtype, rounding):
+    """LayerNorm writing int8 (the following Quantize folded in): against the oracle's
+    quantize_tensor of its LayerNorm, equal except within the LayerNorm tolerance of a rounding
+    boundary; and equal to the device's own f32 LayerNorm quantized by the Quantize operator."""
+    import torch
+    from lightship_b200.backend import DataType, OperatorDef, OperatorType, Quantization, Rounding, Tensor
+    rng = np.random.default_rng(11 + rounding)
+    rows, d, s_q = 2048, 768, 0.04
+    x = rng.normal(size=(rows, d)).astype(dtype)
+    g = rng.uniform(0.8, 1.2, d).astype(np.float32)
+    b = rng.normal(scale=0.02, size=d).astype(np.float32)
+    dt = DataType.F32 if dtype == np.float32 else DataType.F16
+    xt = Tensor("x", [rows, d], dt, torch.from_numpy(x).cuda())
+    qd = torch.empty((rows, d), dtype=torch.int8, device="cuda")
+    qt = Tensor("q", [rows, d], DataType.QInt8, qd, quantization=Quantization([s_q]))
+    ins = [xt, Tensor("g", [d], DataType.F32, g), Tensor("b", [d], DataType.F32, b)]
+    op = be.compile_operator(OperatorDef("lnq", OperatorType.LayerNorm, rounding=Rounding(rounding)), None, ins, [qt])
+    be.execute(op, [xt], [qt])
+    # the same LayerNorm to f32 (same kernel arithmetic), then the Quantize operator
+    yd = torch.empty((rows, d), dtype=torch.float32 if dtype == np.float32 else torch.float16, device="cuda")
+    yt = Tensor("y", [rows, d], dt, yd)
+    op2 = be.compile_operator(OperatorDef("ln", OperatorType.LayerNorm), None, ins, [yt])
+    be.execute(op2, [xt], [yt])
+    torch.cuda.synchronize()
+    if dtype == np.float32:
+        q2 = torch.empty((rows, d), dtype=torch.int8, device="cuda")
+        q2t = Tensor("q2", [rows, d], DataType.QInt8, q2, quantization=Quantization([s_q]))
+        opq = be.compile_operator(OperatorDef("q", OperatorType.Quantize, rounding=Rounding(rounding)), None,
+                                  [yt], [q2t])
+        be.execute(opq, [yt], [q2t])
+        torch.cuda.synchronize()
+        assert torch.equal(q2, qd)
+    ref = orc.layernorm(x.astype(np.float32), g, b, 1e-5)
+    _assert_quantized_close(qd.cpu().numpy(), ref, s_q, 2e-3)  # LayerNorm |dy| <= 2e-5 ~ 5e-4 steps
+    assert (qd.cpu().numpy() != 0).mean() > 0.9
+
+
+@pytest.mark.parametrize("m,n,k,act", [(384, 2304, 768, 0), (300, 200, 96, 4), (1024, 768, 3072, 0), (129, 40, 64, 1)])
+def test_fully_connected_f16_output_and_f32_residual(be, cuda, m, n, k, act):
+    """The INT8 FullyConnected writing f16 (the QKV projection feeding FP16 attention) and
+    adding an f32 residual before the activation (output projection, FFN down): vector
+    stores on full chunks, scalar stores on ragged N; CTA pairs at the wide shapes."""
+    import torch
+    from lightship_b200.backend import Activation, DataType, OperatorDef, OperatorType, Quantization, Tensor
+    rng = np.random.default_rng(m * 7 + n)
+    s_a = 0.04
+    a = rng.integers(-127, 128, size=(m, k), dtype=np.int8)
+    w = rng.normal(0, 0.02, size=(n, k)).astype(np.float32)
+    bias = rng.normal(0, 0.02, size=n).astype(np.float32)
+    res = rng.standard_normal((m, n)).astype(np.float32)
+    xa = Tensor("a", [m, k], DataType.QInt8, torch.from_numpy(a).to(cuda), quantization=Quantization([s_a]))
+    y16 = torch.empty((m, n), dtype=torch.float16, device=cuda)
+    y32 = torch.empty((m, n), dtype=torch.float32, device=cuda)
+    outs = [Tensor("y16", [m, n], DataType.F16, y16), Tensor("y32", [m, n], DataType.F32, y32)]
+    op = be.compile_operator(OperatorDef("fc", OperatorType.FullyConnected, activation=Activation(act)), None,
+                             [xa, Tensor("w", [n, k], DataType.F32, w), Tensor("b", [n], DataType.F32, bias)], outs)
+    rt = Tensor("r", [m, n], DataType.F32, torch.from_numpy(res).to(cuda))
+    be.execute(op, [xa, rt], outs)
+    want = orc.fc_i8_f32_weights(a, s_a, w, bias)[1] + res
+    want = orc.act(want, act)
+    np.testing.assert_array_equal(y32.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    np.testing.assert_array_equal(y16.cpu().numpy().view(np.uint16), want.astype(np.float16).view(np.uint16))
+    # without the residual the same operator reproduces the plain chain
+    be.execute(op, [xa], outs)
+    plain = orc.act(orc.fc_i8_f32_weights(a, s_a, w, bias)[1], act)
+    np.testing.assert_array_equal(y32.cpu().numpy().view(np.uint32), plain.view(np.uint32))

@@ -70,3 +70,46 @@ def test_layernorm_and_softmax_match_float64():
     np.testing.assert_allclose(orc.layernorm(x, g, b), ref, atol=2e-5, rtol=1e-5)
     e = np.exp(xd - xd.max(1, keepdims=True))
     np.testing.assert_allclose(orc.softmax(x), e / e.sum(1, keepdims=True), atol=1e-7, rtol=1e-5)
+
+
+def _ln64(v, g, b):
+    m = v.mean(-1, keepdims=True)
+    return (v - m) / np.sqrt(((v - m) ** 2).mean(-1, keepdims=True) + 1e-5) * g + b
+
+
+def test_attention_helpers_match_float64():
+    """Q/K/V head slicing of the [tokens, 3*heads*dim] projection, Q K^T / 8, and P V."""
+    rng = np.random.default_rng(0)
+    b, s, h, d = 2, 32, 3, 64
+    qkv = rng.standard_normal((b * s, 3 * h * d)).astype(np.float16)
+    sc = orc.attention_scores_f16(qkv, b, s, h, d)
+    q = qkv.astype(np.float64).reshape(b, s, 3, h, d)
+    ref = np.einsum("bihd,bjhd->bhij", q[:, :, 0], q[:, :, 1]) / 8.0
+    np.testing.assert_allclose(sc.astype(np.float64), ref, rtol=2e-3, atol=2e-3)
+    p = orc.softmax(sc.astype(np.float32)).astype(np.float16)
+    o = orc.attention_context(p, qkv, b, s, h, d)
+    ref_o = np.einsum("bhij,bjhd->bihd", p.astype(np.float64), q[:, :, 2]).reshape(b * s, h * d)
+    np.testing.assert_allclose(o, ref_o, rtol=1e-5, atol=1e-5)
+
+
+def test_encoder_block_oracle_tracks_float_model():
+    """The quantized block's attention half against a float64 restatement: the residual
+    stream after the output projection agrees to the INT8 quantization error."""
+    from lightship_b200.bert import build_params
+    b, s = 1, 64
+    p = build_params(3)
+    x = np.random.default_rng(4).standard_normal((b * s, 768)).astype(np.float32)
+    ln1 = orc.layernorm(x, p["ln1_g"], p["ln1_b"], 1e-5)
+    scales = {"q1": orc.find_scale_zp(ln1)[0], "q2": 1.0, "q3": 1.0, "u": 1.0}
+    scales["q2"] = orc.find_scale_zp(orc.encoder_block_int8(x, p, scales, b, s)["o"])[0]
+    r = orc.encoder_block_int8(x, p, scales, b, s)
+    a = _ln64(x.astype(np.float64), p["ln1_g"], p["ln1_b"])
+    qkv = (a @ p["wqkv"].T.astype(np.float64) + p["bqkv"]).reshape(b, s, 3, 12, 64)
+    sc = np.einsum("bihd,bjhd->bhij", qkv[:, :, 0], qkv[:, :, 1]) / 8.0
+    e = np.exp(sc - sc.max(-1, keepdims=True))
+    o = np.einsum("bhij,bjhd->bihd", e / e.sum(-1, keepdims=True), qkv[:, :, 2]).reshape(b * s, 768)
+    h = o @ p["wo"].T.astype(np.float64) + p["bo"] + x
+    assert np.linalg.norm(r["h"] - h) <= 0.05 * np.linalg.norm(h - x)
+    # the int8 stages are the oracle's own quantize of its f32 stages
+    assert np.array_equal(r["q1"], orc.quantize_tensor(r["ln1"], scales["q1"], 0))
+    assert r["u"].dtype == np.int8 and r["out"].shape == (b * s, 768)
