@@ -48,6 +48,10 @@ struct I8Params {
   const float* res_f32;   // optional f32 residual [M, ldo] added before the activation
   int64_t ldo;
   int32_t vec_ok;  // 16-byte vector stores are legal for full column chunks
+  // 32-byte (256-bit) accesses are legal for full chunks of: bit 0 out_f32, bit 1 out_f16,
+  // bit 2 res_f32 (pointer 32-byte aligned, row pitch a multiple of 32 bytes); each one
+  // sector per L2 request instead of half of one
+  int32_t wide;
   uint32_t* err;
   // optional int8 residual added before the activation (same layout as the outputs):
   // y = (f32)acc * scale + (f32)r * res_scale
@@ -115,13 +119,40 @@ struct PairCfg {
 };
 
 
+// The int8 words of a 16-column chunk held back so that it and the adjacent chunk of the same
+// row leave as one 32-byte store (a full sector per L2 request).
+template <int W>
+struct I8Pend {
+  uint32_t w[W / 4];
+  bool held = false;
+};
+
+// Pulls this thread's residual segment for the coming tile into L2 (issued before the
+// accumulator is ready, so the loads in the epilogue hit L2): `cols` columns from col0.
+__device__ __forceinline__ void prefetch_residual(const I8Params& p, int row, int col0, int cols) {
+  if (row >= p.m) return;
+  if (p.res_f32) {
+    const float* rp = p.res_f32 + static_cast<int64_t>(row) * p.ldo;
+    for (int i = 0; i < cols; i += 32)
+      if (col0 + i < p.n) asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + col0 + i));
+  }
+  if (p.residual) {
+    const int8_t* rp = p.residual + static_cast<int64_t>(row) * p.ldo;
+    for (int i = 0; i < cols; i += 128)
+      if (col0 + i < p.n) asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + col0 + i));
+  }
+}
+
 // Epilogue for W consecutive columns of one output row held by this thread; cs / cb are the
 // chunk's per-column scales and biases staged in shared memory (zero past the last column).
 // Each output is stored as soon as it is final (i32, then f32, then int8) so the
-// accumulator, f32 and int8 arrays are never live together.
+// accumulator, f32 and int8 arrays are never live together.  pair_first: this thread's next
+// call is the adjacent chunk (col0 + W) of the same row, so its int8 words may be held in
+// `pend` and stored with that chunk's.
 template <int ACT, int W>
 __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t (&r)[W],
-                                               const float* cs, const int32_t* cb, int row, int col0) {
+                                               const float* cs, const int32_t* cb, int row, int col0,
+                                               I8Pend<W>& pend, bool pair_first) {
   static_assert(W % 16 == 0, "chunks are whole 16-byte int8 vectors");
   if (row >= p.m) return;
   const bool vec = (col0 + W <= p.n) && p.vec_ok;
@@ -175,7 +206,15 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
     }
   }
   if (p.res_f32) {
-    if (vec) {
+    if (vec && (p.wide & 4)) {
+#pragma unroll
+      for (int v = 0; v < W / 8; ++v) {
+        uint32_t rv[8];
+        ld_global_nc_v8(p.res_f32 + base + 8 * v, rv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[8 * v + j] = __fadd_rn(y[8 * v + j], __uint_as_float(rv[j]));
+      }
+    } else if (vec) {
       const float4* rp = reinterpret_cast<const float4*>(p.res_f32 + base);
 #pragma unroll
       for (int v = 0; v < W / 4; ++v) {
@@ -193,12 +232,23 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
   }
   // A ReLU feeding only the int8 output is applied inside the requantization's clamp.
   const bool relu_folded = ACT == LSC_ACT_RELU && !p.out_f32 && !p.out_f16 && p.inv_s_out > 0.0f;
-  if (!relu_folded) {
+  if constexpr (ACT == LSC_ACT_GELU) {
+#pragma unroll
+    for (int j = 0; j < W; j += 2) act_gelu2(y[j], y[j + 1]);
+  } else if (!relu_folded) {
 #pragma unroll
     for (int j = 0; j < W; ++j) y[j] = apply_act<ACT>(y[j]);
   }
   if (p.out_f32) {
-    if (vec) {
+    if (vec && (p.wide & 1)) {
+#pragma unroll
+      for (int v = 0; v < W / 8; ++v) {
+        uint32_t ov[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ov[j] = __float_as_uint(y[8 * v + j]);
+        st_global_v8(p.out_f32 + base + 8 * v, ov);
+      }
+    } else if (vec) {
       float4* dst = reinterpret_cast<float4*>(p.out_f32 + base);
 #pragma unroll
       for (int j = 0; j < W / 4; ++j) dst[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
@@ -210,7 +260,18 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
   }
   if (p.out_f16) {
     __half* o = p.out_f16 + base;
-    if (vec) {
+    if (vec && (p.wide & 2)) {
+#pragma unroll
+      for (int v = 0; v < W / 16; ++v) {
+        uint32_t h[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const __half2 hh = __floats2half2_rn(y[16 * v + 2 * t], y[16 * v + 2 * t + 1]);
+          h[t] = *reinterpret_cast<const uint32_t*>(&hh);
+        }
+        st_global_v8(o + 16 * v, h);
+      }
+    } else if (vec) {
 #pragma unroll
       for (int v = 0; v < W / 8; ++v) {
         uint32_t h[4];
@@ -230,7 +291,20 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
   if (p.out_i8) {
     uint32_t pk[W / 4];
     requant_pack<W>(y, p.s_out, p.inv_s_out, relu_folded, p.rounding, pk);
-    if (vec) {
+    if (W == 16 && vec && pair_first && (p.wide & 8) && col0 + 2 * W <= p.n) {
+#pragma unroll
+      for (int j = 0; j < W / 4; ++j) pend.w[j] = pk[j];
+      pend.held = true;
+    } else if (W == 16 && pend.held) {
+      uint32_t v[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[j] = pend.w[j];
+        v[4 + j] = pk[j];
+      }
+      st_global_v8(p.out_i8 + base - W, v);
+      pend.held = false;
+    } else if (vec) {
       uint4* dst = reinterpret_cast<uint4*>(p.out_i8 + base);
 #pragma unroll
       for (int v = 0; v < W / 16; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
@@ -459,10 +533,12 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       }
       const int buf = local & 1;
       const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
+      const int row = mb * C::BM + row_in_tile;
+      prefetch_residual(p, row, nb * C::BN + part * C::COLS_PER_EPI_WARP, C::COLS_PER_EPI_WARP);
       if (!mbar_wait(&tfull[buf], buf_phase, abort_flag, p.err)) break;
       tc_fence_after();
-      const int row = mb * C::BM + row_in_tile;
       constexpr int CHUNKS = C::COLS_PER_EPI_WARP / C::EPI_W;
+      I8Pend<C::EPI_W> pend;
 #pragma unroll 1
       for (int c = 0; c < CHUNKS; ++c) {
         const int tcol = part * C::COLS_PER_EPI_WARP + c * C::EPI_W;
@@ -477,7 +553,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
           if (lane == 0) mbar_arrive(&tempty[buf]);
         }
         epilogue_chunk<ACT, C::EPI_W>(p, r, w_scale + c * C::EPI_W, w_bias + c * C::EPI_W, row,
-                                      nb * C::BN + tcol);
+                                      nb * C::BN + tcol, pend, CHUNKS % 2 == 0 && c % 2 == 0);
       }
     }
   }
@@ -674,10 +750,12 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
       }
       const int buf = local & 1;
       const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
+      const int row = mb * 256 + static_cast<int>(rank) * ROWS + row_in_tile;
+      prefetch_residual(p, row, nb * PN + part * COLS, COLS);
       if (!mbar_wait(&tfull[buf], buf_phase, abort_flag, p.err)) break;
       tc_fence_after();
-      const int row = mb * 256 + static_cast<int>(rank) * ROWS + row_in_tile;
       constexpr int CHUNKS = COLS / P::EPI_W;
+      I8Pend<P::EPI_W> pend;
 #pragma unroll 1
       for (int c = 0; c < CHUNKS; ++c) {
         const int tcol = part * COLS + c * P::EPI_W;
@@ -691,7 +769,8 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(tempty_even + buf * 8);
         }
-        epilogue_chunk<ACT, P::EPI_W>(p, r, w_scale + c * P::EPI_W, w_bias + c * P::EPI_W, row, nb * PN + tcol);
+        epilogue_chunk<ACT, P::EPI_W>(p, r, w_scale + c * P::EPI_W, w_bias + c * P::EPI_W, row, nb * PN + tcol,
+                                      pend, CHUNKS % 2 == 0 && c % 2 == 0);
       }
     }
   }
@@ -867,6 +946,8 @@ void fill_outputs(I8Params& p, const int32_t* bias, const float* scale, float s_
                                reinterpret_cast<uintptr_t>(scale) |
                                reinterpret_cast<uintptr_t>(bias);
   p.vec_ok = ((align_bits & 15) == 0 && (ldo % 16) == 0) ? 1 : 0;
+  p.wide = (p.vec_ok && (reinterpret_cast<uintptr_t>(out_f32) & 31) == 0 && ldo % 8 == 0) ? 1 : 0;
+  if (p.vec_ok && (reinterpret_cast<uintptr_t>(out_i8) & 31) == 0 && ldo % 32 == 0) p.wide |= 8;
   p.err = err;
 }
 
@@ -918,6 +999,12 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
     p.out_f16 = static_cast<__half*>(extras->out_f16);
     p.res_f32 = extras->res_f32;
     if ((reinterpret_cast<uintptr_t>(p.out_f16) | reinterpret_cast<uintptr_t>(p.res_f32)) & 15) p.vec_ok = 0;
+    if (!p.vec_ok) {
+      p.wide = 0;
+    } else {
+      if (p.out_f16 && (reinterpret_cast<uintptr_t>(p.out_f16) & 31) == 0 && ldo % 16 == 0) p.wide |= 2;
+      if (p.res_f32 && (reinterpret_cast<uintptr_t>(p.res_f32) & 31) == 0 && ldo % 8 == 0) p.wide |= 4;
+    }
   }
   if (pair) return launch_pair(ta, tw, p, act, ds->sm_count, stream);
   return launch_bn<0>(bn, ta, tw, p, act, ds->sm_count, stream);
@@ -1000,6 +1087,7 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
   p.residual = residual;
   p.res_scale = res_scale;
   if (reinterpret_cast<uintptr_t>(residual) & 15) p.vec_ok = 0;
+  if (!p.vec_ok) p.wide = 0;
   switch (acb) {
     case 128: return launch_bn<128>(bn, ta, tw, p, act, ds->sm_count, stream);
     case 64: return launch_bn<64>(bn, ta, tw, p, act, ds->sm_count, stream);

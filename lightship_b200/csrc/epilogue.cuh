@@ -131,6 +131,46 @@ __device__ __forceinline__ uint64_t f2sub(uint64_t a, uint64_t b) {
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// act_gelu on two values with two-lane arithmetic: the same operations in the same order, so
+// bit-identical to the scalar form.  The series is evaluated for every argument and replaced
+// by +-1 beyond |t| > 5 afterwards (an overflowed series there is discarded).
+// x + 0.044715 * x^3 is computed with scalar intrinsics: ptxas contracts a mul.rn.f32x2 whose
+// only use is an add.rn.f32x2 into a single fma.rn.f32x2 (one rounding where the reference
+// rounds twice), and the scalar .rn forms are never contracted.
+__device__ __forceinline__ void act_gelu2(float& a, float& b) {
+  const uint64_t x = f2pack(a, b);
+  const uint64_t x_cube = f2mul(f2mul(x, x), x);
+  float ca, cb;
+  f2unpack(x_cube, ca, cb);
+  const uint64_t inner = f2pack(__fadd_rn(a, __fmul_rn(0.044715f, ca)), __fadd_rn(b, __fmul_rn(0.044715f, cb)));
+  const uint64_t t = f2mul(f2pack(0.7978845608f, 0.7978845608f), inner);
+  const uint64_t t2 = f2mul(t, t);
+  const uint64_t t3 = f2mul(t2, t);
+  const uint64_t t5 = f2mul(t3, t2);
+  const uint64_t t7 = f2mul(t5, t2);
+  // x / c as div_by_const: q = x*z, r = fma(q, -c, x), fma(r, z, q)
+  auto div2 = [](uint64_t v, float c, float z) {
+    const uint64_t z2 = f2pack(z, z);
+    const uint64_t q = f2mul(v, z2);
+    return f2fma(f2fma(q, f2pack(-c, -c), v), z2, q);
+  };
+  uint64_t r = f2sub(t, div2(t3, 3.0f, 1.0f / 3.0f));
+  r = f2add(r, div2(t5, 5.0f, 1.0f / 5.0f));
+  r = f2sub(r, div2(t7, 7.0f, 1.0f / 7.0f));
+  float ta, tb, ra, rb;
+  f2unpack(t, ta, tb);
+  f2unpack(r, ra, rb);
+  ra = ta > 5.0f ? 1.0f : (ta < -5.0f ? -1.0f : ra);
+  rb = tb > 5.0f ? 1.0f : (tb < -5.0f ? -1.0f : rb);
+  const uint64_t y = f2mul(f2mul(f2pack(0.5f, 0.5f), x), f2add(f2pack(1.0f, 1.0f), f2pack(ra, rb)));
+  f2unpack(y, a, b);
+}
 
 // requant_i8 for W values, packed four to a word (value j in byte j%4 of pk[j/4]), without
 // the per-element IEEE division; same results.
