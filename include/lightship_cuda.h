@@ -345,6 +345,21 @@ lsc_status lsc_transpose_heads_f16(const void* x, void* y, int64_t x_batch_strid
                                    int64_t batch, int64_t heads, int64_t rows, int64_t cols,
                                    lsc_stream stream);
 
+/* Fused multi-head attention of an encoder block: for each batch b, head h and query q,
+ *   out[b, q, h, :] = sum_k P[q, k] V[b, k, h, :],  P = f16(softmax_k(f16(alpha * Q[b,q,h,:] . K[b,k,h,:])))
+ * with f32 accumulation -- what lsc_gemm_f16_batched (scores), the Softmax operator and
+ * lsc_gemm_f16_batched (P V) compute in sequence, without the [batch, heads, seq, seq] scores
+ * in memory.  qkv is the f16 QKV projection [batch, seq, 3, heads, 64] (Q, K, V head-major),
+ * 16-byte aligned.  Outputs
+ * [batch, seq, heads, 64]: out_f32 (32-byte aligned) and/or out_i8, the latter quantized
+ * per tensor with s_out (quantize_value's arithmetic, `rounding` as lsc_rounding).  seq a
+ * multiple of 128 up to 384, head dim 64.  Replaces the attention the reference declares
+ * (core/ir/operator.rs:54-58, core/operator/attention.rs), whose CPU backend has no kernel;
+ * the softmax is operator/softmax.rs:106-146.  A row whose scores hold an infinity or NaN
+ * yields NaN outputs. */
+lsc_status lsc_attention_f16(const void* qkv, int64_t batch, int64_t seq, int64_t heads, float alpha,
+                             float* out_f32, int8_t* out_i8, float s_out, int32_t rounding, lsc_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

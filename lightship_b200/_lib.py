@@ -122,6 +122,7 @@ SIGNATURES = {
     "lsc_gemm_f16_batched": (ST, [P, I64, I64, I64, I64, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, F32, P, I32,
                                   I64, I64, I64, P]),
     "lsc_transpose_heads_f16": (ST, [P, P, I64, I64, I64, I64, I64, I64, I64, I64, P]),
+    "lsc_attention_f16": (ST, [P, I64, I64, I64, F32, P, P, F32, I32, P]),
 }
 
 _lib = None

@@ -7,16 +7,16 @@ hidden 768, 12 heads x 64, FFN 3072.  The four projections are INT8 FullyConnect
 (per-channel weights quantized at compile from f32 N(0, 0.02); activations quantized per
 tensor with scales calibrated on the first batch), their epilogues adding the bias, the GELU
 (FFN up, requantized straight to int8 for FFN down), the f32 residual (output projection and
-FFN down) or writing f16 (the fused QKV projection, read in place by the attention GEMMs).
-Attention runs on the FP16 tensor-core GEMM (scores and P V) with an f16 Softmax between
-them.  Every operator is this backend's: Backend operators for LayerNorm, Quantize, the INT8
-projections and Softmax, the C ABI's FP16 GEMM and head transpose for attention.  The forward
-pass is one CUDA graph of 11 kernel launches; LayerNorm writes the int8 input of the
-projection after it directly.
+FFN down) or writing f16 (the fused QKV projection, read in place by the attention).  The
+attention is one fused kernel (scores, f16 softmax and P V without the scores leaving the
+chip) writing its output already quantized for the output projection, and LayerNorm writes
+the int8 input of the projection after it, so the forward pass is one CUDA graph of 7 kernel
+launches: LayerNorm, QKV, attention, output projection, LayerNorm, FFN up, FFN down.
 
 Reference operators: LayerNorm (core/operator/layernorm.rs:153-205), GELU (gelu.rs:77-103),
 Softmax (softmax.rs:106-146), the INT8 chain (core/cpu/quantized_ops.rs:13-48,
-quantization/helpers.rs:101-160); the block shape follows the survey's configuration 5.
+quantization/helpers.rs:101-160); the block shape is the BERT-base encoder-block benchmark
+configuration (seq 384, batch 32).
 """
 from __future__ import annotations
 
@@ -71,8 +71,6 @@ class BertBlockInt8:
             "ln1": torch.empty(t, HIDDEN, dtype=torch.float32, **e),
             "q1": torch.empty(t, HIDDEN, dtype=torch.int8, **e),
             "qkv": torch.empty(batch, seq, 3 * HEADS, HEAD_DIM, dtype=torch.float16, **e),
-            "scores": torch.empty(batch, HEADS, seq, seq, dtype=torch.float16, **e),
-            "vt": torch.empty(batch, HEADS, HEAD_DIM, seq, dtype=torch.float16, **e),
             "o": torch.empty(t, HIDDEN, dtype=torch.float32, **e),
             "q2": torch.empty(t, HIDDEN, dtype=torch.int8, **e),
             "h": torch.empty(t, HIDDEN, dtype=torch.float32, **e),
@@ -109,14 +107,6 @@ class BertBlockInt8:
     def _calibrated(self, q, src, fixed):
         return float(fixed[q]) if fixed else self._scale_of(self.buf[src])
 
-    def _calibrate_quantize(self, q, src, fixed):
-        """Fixes the scale of int8 activation `q` and compiles the Quantize operator that
-        writes it from f32 buffer `src` (the operator carries the scale from compile)."""
-        self.scales[q] = self._calibrated(q, src, fixed)
-        self.ops[q] = self.be.compile_operator(
-            OperatorDef(q, OperatorType.Quantize, rounding=self.rounding), None, [self._f32(src)],
-            [self._i8(q, self.scales[q])])
-
     def _run(self, name, ins, outs):
         self.be.execute(self.ops[name], ins, outs, stream=self._stream())
 
@@ -128,21 +118,10 @@ class BertBlockInt8:
             outs)
 
     # ------------------------------------------------------------------ stages
-    def _quantize(self, name, src, dst):
-        self._run(name, [self._f32(src)], [self._i8(dst, self.scales[dst])])
-
-    def _attention(self):
-        b, s = self.batch, self.seq
-        row, head, bat = 3 * HEADS * HEAD_DIM, HEAD_DIM, s * 3 * HEADS * HEAD_DIM
-        qkv = self.buf["qkv"]
-        ops.gemm_f16_batched(qkv, qkv, self.buf["scores"], b, HEADS, s, s, HEAD_DIM, alpha=1.0 / 8.0,
-                             a_strides=(row, head, bat), b_strides=(row, head, bat), a_head0=0, b_head0=HEADS)
-        sc = self.buf["scores"]
-        st = Tensor("scores", list(sc.shape), DataType.F16, sc)
-        self._run("softmax", [st], [st])
-        ops.transpose_heads_f16(qkv, self.buf["vt"], b, HEADS, s, HEAD_DIM, (bat, head, row), head0=2 * HEADS)
-        ops.gemm_f16_batched(sc, self.buf["vt"], self.buf["o"], b, HEADS, s, HEAD_DIM, s,
-                             out_strides=(HEADS * HEAD_DIM, HEAD_DIM, s * HEADS * HEAD_DIM))
+    def _attention(self, out_f32=None, out_i8=None):
+        """softmax(Q K^T / 8) V per head, fused (one kernel), from the f16 QKV projection."""
+        ops.attention_f16(self.buf["qkv"], self.batch, self.seq, HEADS, alpha=1.0 / 8.0, out_f32=out_f32,
+                          out_i8=out_i8, s_out=self.scales.get("q2", 1.0), rounding=int(self.rounding))
 
     def _qkv_out(self):
         qkv = self.buf["qkv"].view(self.batch * self.seq, 3 * HIDDEN)
@@ -158,17 +137,14 @@ class BertBlockInt8:
         torch = self.torch
         p = self.params
         self.buf["x"].copy_(x)
-        sc = self.buf["scores"]
-        st = Tensor("scores", list(sc.shape), DataType.F16, sc)
-        self.ops["softmax"] = self.be.compile_operator(OperatorDef("softmax", OperatorType.Softmax), None, [st], [st])
         # LN1 (f32) -> scale of q1 -> LN1 to int8 -> QKV -> attention -> scale of q2 -> out proj (+x) ...
         self._ln_calibrate("ln1", "x", "q1", p["ln1_g"], p["ln1_b"], scales)
         self._run("ln1", [self._f32("x")], [self._i8("q1", self.scales["q1"])])
         self._fc("qkv", "q1", self.scales["q1"], p["wqkv"], p["bqkv"], [self._qkv_out()])
         self._run("qkv", [self._i8("q1", self.scales["q1"])], [self._qkv_out()])
-        self._attention()
-        self._calibrate_quantize("q2", "o", scales)
-        self._quantize("q2", "o", "q2")
+        self._attention(out_f32=self.buf["o"])
+        self.scales["q2"] = self._calibrated("q2", "o", scales)
+        self._attention(out_i8=self.buf["q2"])
         self._fc("out", "q2", self.scales["q2"], p["wo"], p["bo"], [self._f32("h")])
         self._run("out", [self._i8("q2", self.scales["q2"]), self._f32("x")], [self._f32("h")])
         self._ln_calibrate("ln2", "h", "q3", p["ln2_g"], p["ln2_b"], scales)
@@ -197,12 +173,11 @@ class BertBlockInt8:
             [self._i8(q, self.scales[q])])
 
     def forward_device(self):
-        """One block forward on the device-resident input buffer ``buf['x']`` (11 launches)."""
+        """One block forward on the device-resident input buffer ``buf['x']`` (7 launches)."""
         sc = self.scales
         self._run("ln1", [self._f32("x")], [self._i8("q1", sc["q1"])])
         self._run("qkv", [self._i8("q1", sc["q1"])], [self._qkv_out()])
-        self._attention()
-        self._quantize("q2", "o", "q2")
+        self._attention(out_i8=self.buf["q2"])
         self._run("out", [self._i8("q2", sc["q2"]), self._f32("x")], [self._f32("h")])
         self._run("ln2", [self._f32("h")], [self._i8("q3", sc["q3"])])
         self._run("ffn_up_i8", [self._i8("q3", sc["q3"])], [self._i8("u", sc["u"])])
@@ -227,5 +202,5 @@ class BertBlockInt8:
 
     @staticmethod
     def kernel_launches():
-        return 11
+        return 7
 

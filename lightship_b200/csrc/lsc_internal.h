@@ -118,6 +118,12 @@ lsc_status launch_layernorm(const void* x, void* y, int32_t dtype, int64_t rows,
                             float q_scale = 0.0f, int rounding = LSC_ROUND_HALF_AWAY);
 // RN(1 / s) when s and 1/s are normal floats, else 0 (pool.cu).
 float reciprocal_or_zero(float s);
+// y[b][h][c][r] = x[b][h + h0][r][c], f16 (contraction_f16.cu).
+lsc_status launch_transpose_heads_f16(const void* x, void* y, int64_t xb, int64_t xh, int64_t xr, int64_t h0,
+                                      int64_t batch, int64_t heads, int64_t rows, int64_t cols, cudaStream_t stream);
+// Fused attention over a [batch, seq, 3, heads, 64] f16 QKV projection (attention_f16.cu).
+lsc_status launch_attention_f16(const void* qkv, int64_t batch, int64_t seq, int64_t heads, float alpha,
+                                float* out_f32, int8_t* out_i8, float s_out, int rounding, cudaStream_t stream);
 lsc_status launch_softmax(const void* x, void* y, int32_t dtype, int64_t rows, int64_t d, cudaStream_t st);
 
 lsc_status launch_quantize_nchw_to_s2d_i8(const float* x, int8_t* y, int64_t n, int64_t c, int64_t h,

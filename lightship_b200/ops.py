@@ -119,3 +119,20 @@ def transpose_heads_f16(x, y, batch, heads, rows, cols, x_strides, head0=0):
     check(lib().lsc_transpose_heads_f16(_ptr(x), _ptr(y), *x_strides, head0, batch, heads, rows, cols,
                                         _stream(x.device)))
     return y
+
+
+def attention_f16(qkv, batch, seq, heads, alpha=0.125, out_f32=None, out_i8=None, s_out=1.0, rounding=0):
+    """Fused attention (see ``lsc_attention_f16``) over the f16 QKV projection ``qkv``
+    ([batch, seq, 3, heads, 64] elements, contiguous); outputs [batch * seq, heads * 64] f32
+    and/or int8 (quantized with ``s_out``)."""
+    _need(qkv, torch.float16, "qkv")
+    if out_f32 is None and out_i8 is None:
+        raise ValueError("attention_f16: no output")
+    _need(out_f32, torch.float32, "out_f32")
+    _need(out_i8, torch.int8, "out_i8")
+    need = batch * seq * heads * 64
+    for name, t in (("qkv", qkv), ("out_f32", out_f32), ("out_i8", out_i8)):
+        if t is not None and t.numel() < (3 * need if name == "qkv" else need):
+            raise ValueError(f"attention_f16: {name} too small")
+    check(lib().lsc_attention_f16(_ptr(qkv), batch, seq, heads, float(alpha), _ptr(out_f32), _ptr(out_i8),
+                                  float(s_out), int(rounding), _stream(qkv.device)))

@@ -2,9 +2,10 @@
 
 Stage by stage, each device stage is fed the device's own previous intermediate in the oracle,
 so every stage is checked on identical inputs: quantize and the INT8 projections (f16 QKV, f32
-residual adds, GELU requantized to int8) bit-exact; LayerNorm, the attention GEMMs and Softmax
-(different f32 summation order, f16 rounding of the result) within the stated tolerances.  The
-whole block from the input alone is then compared with a tolerance on its output.
+residual adds, GELU requantized to int8) bit-exact; LayerNorm and the fused attention
+(different f32 summation order, the device exp, f16 rounding points as the oracle's) within
+the stated tolerances.  The whole block from the input alone is then compared with a
+tolerance on its output.
 """
 import numpy as np
 import pytest
@@ -48,13 +49,14 @@ def test_encoder_block_stages(batch, seq):
     dq = d["qkv"].reshape(batch * seq, -1)
     assert np.array_equal(dq.view(np.uint16), qkv.view(np.uint16))
 
-    # softmax(Q K^T / 8): f32 sums in another order, rounded to f16 twice (scores, probabilities)
+    # fused attention, softmax(Q K^T / 8) V: f32 sums in another order, the device exp, scores
+    # and probabilities rounded to f16 at the same points; o is the f32 output of the
+    # calibration pass, q2 the int8 output of the forward pass (same kernel arithmetic)
     scores = orc.attention_scores_f16(dq, batch, seq, HEADS, HEAD_DIM)
     prob = orc.softmax(scores.astype(np.float32)).astype(np.float16)
-    np.testing.assert_allclose(d["scores"].astype(np.float32), prob.astype(np.float32), rtol=2e-2, atol=2e-4)
-
-    o = orc.attention_context(d["scores"], dq, batch, seq, HEADS, HEAD_DIM)
-    np.testing.assert_allclose(d["o"], o, rtol=1e-3, atol=1e-4)
+    o = orc.attention_context(prob, dq, batch, seq, HEADS, HEAD_DIM)
+    np.testing.assert_allclose(d["o"], o, rtol=1e-2, atol=2e-3)
+    assert np.median(np.abs(d["o"] - o)) < 1e-4
     assert np.array_equal(d["q2"], orc.quantize_tensor(d["o"], sc["q2"], 0))
 
     h = orc.fc_i8_f32_weights(d["q2"], sc["q2"], p["wo"], p["bo"])[1] + x
