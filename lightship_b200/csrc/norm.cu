@@ -206,6 +206,17 @@ __global__ void __launch_bounds__(kRowWarps * 32) softmax_rows_kernel(const T* x
 
 // LayerNorm over rows of d <= 128*J elements, output T, or int8 when q != nullptr
 // (q = R(y / s_out), saturated; the Quantize operator's arithmetic).
+// a / b with y = RN(1 / b) computed once per row: q = RN(a y), r = a - q b (exact by FMA),
+// RN(q + r y) -- Markstein's division by way of a correctly rounded reciprocal (P. Markstein,
+// IBM J. Res. Dev. 34(1), 1990), which returns RN(a / b) while q stays in the normal range.
+// Zero, tiny, huge and non-finite quotients take the IEEE division.
+__device__ __forceinline__ float div_by_row(float a, float b, float y) {
+  const float q = __fmul_rn(a, y);
+  const float aq = fabsf(q);
+  if (!(aq > 7.5e-37f && aq < 1.3e36f)) return __fdiv_rn(a, b);
+  return __fmaf_rn(__fmaf_rn(-q, b, a), y, q);
+}
+
 template <typename T, int J, int RND>
 __global__ void __launch_bounds__(kRowWarps * 32) layernorm_rows_kernel(const T* x, T* y, int8_t* q, int64_t rows,
                                                                         int d, const float* __restrict__ gamma,
@@ -241,6 +252,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) layernorm_rows_kernel(const T*
     }
     const float var = __fdiv_rn(warp_sum(sq), fd);
     const float sd = __fsqrt_rn(__fadd_rn(var, eps));
+    const float inv_sd = __frcp_rn(sd);
 #pragma unroll
     for (int j = 0; j < J; ++j) {
       const int i = 128 * j + 4 * lane;
@@ -248,7 +260,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) layernorm_rows_kernel(const T*
       float o[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        float t = __fdiv_rn(__fsub_rn(v[j][e], mean), sd);
+        float t = div_by_row(__fsub_rn(v[j][e], mean), sd, inv_sd);
         if (gamma) t = __fmul_rn(__ldg(gamma + i + e), t);
         if (beta) t = __fadd_rn(t, __ldg(beta + i + e));
         o[e] = t;
