@@ -119,40 +119,24 @@ struct PairCfg {
 };
 
 
-// The int8 words of a 16-column chunk held back so that it and the adjacent chunk of the same
-// row leave as one 32-byte store (a full sector per L2 request).
-template <int W>
-struct I8Pend {
-  uint32_t w[W / 4];
-  bool held = false;
-};
-
-// Pulls this thread's residual segment for the coming tile into L2 (issued before the
+// Pulls this thread's f32 residual segment for the coming tile into L2 (issued before the
 // accumulator is ready, so the loads in the epilogue hit L2): `cols` columns from col0.
 __device__ __forceinline__ void prefetch_residual(const I8Params& p, int row, int col0, int cols) {
-  if (row >= p.m) return;
-  if (p.res_f32) {
-    const float* rp = p.res_f32 + static_cast<int64_t>(row) * p.ldo;
-    for (int i = 0; i < cols; i += 32)
-      if (col0 + i < p.n) asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + col0 + i));
-  }
-  if (p.residual) {
-    const int8_t* rp = p.residual + static_cast<int64_t>(row) * p.ldo;
-    for (int i = 0; i < cols; i += 128)
-      if (col0 + i < p.n) asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + col0 + i));
-  }
+  if (row >= p.m || !p.res_f32) return;
+  const float* rp = p.res_f32 + static_cast<int64_t>(row) * p.ldo;
+  for (int i = 0; i < cols; i += 32)
+    if (col0 + i < p.n) asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + col0 + i));
 }
 
 // Epilogue for W consecutive columns of one output row held by this thread; cs / cb are the
 // chunk's per-column scales and biases staged in shared memory (zero past the last column).
 // Each output is stored as soon as it is final (i32, then f32, then int8) so the
-// accumulator, f32 and int8 arrays are never live together.  pair_first: this thread's next
-// call is the adjacent chunk (col0 + W) of the same row, so its int8 words may be held in
-// `pend` and stored with that chunk's.
-template <int ACT, int W>
+// accumulator, f32 and int8 arrays are never live together.  EXT compiles in the f16 output
+// and the f32 residual (the transformer projections); without them the CNN's kernels keep
+// their registers and instructions for the int8 path.
+template <int ACT, int W, bool EXT>
 __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t (&r)[W],
-                                               const float* cs, const int32_t* cb, int row, int col0,
-                                               I8Pend<W>& pend, bool pair_first) {
+                                               const float* cs, const int32_t* cb, int row, int col0) {
   static_assert(W % 16 == 0, "chunks are whole 16-byte int8 vectors");
   if (row >= p.m) return;
   const bool vec = (col0 + W <= p.n) && p.vec_ok;
@@ -177,7 +161,7 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
         if (col0 + j < p.n) p.out_i32[base + j] = acc[j];
     }
   }
-  if (!p.out_f32 && !p.out_i8 && !p.out_f16) return;
+  if (!p.out_f32 && !p.out_i8 && !(EXT && p.out_f16)) return;
   float y[W];
 #pragma unroll
   for (int j = 0; j < W; j += 4) {
@@ -205,7 +189,7 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
           y[j] = __fadd_rn(y[j], __fmul_rn(__int2float_rn(p.residual[base + j]), p.res_scale));
     }
   }
-  if (p.res_f32) {
+  if (EXT && p.res_f32) {
     if (vec && (p.wide & 4)) {
 #pragma unroll
       for (int v = 0; v < W / 8; ++v) {
@@ -231,7 +215,7 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
     }
   }
   // A ReLU feeding only the int8 output is applied inside the requantization's clamp.
-  const bool relu_folded = ACT == LSC_ACT_RELU && !p.out_f32 && !p.out_f16 && p.inv_s_out > 0.0f;
+  const bool relu_folded = ACT == LSC_ACT_RELU && !p.out_f32 && !(EXT && p.out_f16) && p.inv_s_out > 0.0f;
   if constexpr (ACT == LSC_ACT_GELU) {
 #pragma unroll
     for (int j = 0; j < W; j += 2) act_gelu2(y[j], y[j + 1]);
@@ -258,7 +242,7 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
         if (col0 + j < p.n) p.out_f32[base + j] = y[j];
     }
   }
-  if (p.out_f16) {
+  if (EXT && p.out_f16) {
     __half* o = p.out_f16 + base;
     if (vec && (p.wide & 2)) {
 #pragma unroll
@@ -291,20 +275,7 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
   if (p.out_i8) {
     uint32_t pk[W / 4];
     requant_pack<W>(y, p.s_out, p.inv_s_out, relu_folded, p.rounding, pk);
-    if (W == 16 && vec && pair_first && (p.wide & 8) && col0 + 2 * W <= p.n) {
-#pragma unroll
-      for (int j = 0; j < W / 4; ++j) pend.w[j] = pk[j];
-      pend.held = true;
-    } else if (W == 16 && pend.held) {
-      uint32_t v[8];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[j] = pend.w[j];
-        v[4 + j] = pk[j];
-      }
-      st_global_v8(p.out_i8 + base - W, v);
-      pend.held = false;
-    } else if (vec) {
+    if (vec) {
       uint4* dst = reinterpret_cast<uint4*>(p.out_i8 + base);
 #pragma unroll
       for (int v = 0; v < W / 16; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
@@ -333,7 +304,7 @@ __device__ __forceinline__ uint64_t a_desc(uint32_t a0, int kk) {
   }
 }
 
-template <int BN, int ACT, int ACB>
+template <int BN, int ACT, int ACB, bool EXT>
 __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
     contraction_i8_kernel(const __grid_constant__ CUtensorMap tmA,
                           const __grid_constant__ CUtensorMap tmW, const I8Params p) {
@@ -534,11 +505,10 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       const int buf = local & 1;
       const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
       const int row = mb * C::BM + row_in_tile;
-      prefetch_residual(p, row, nb * C::BN + part * C::COLS_PER_EPI_WARP, C::COLS_PER_EPI_WARP);
+      if constexpr (EXT) prefetch_residual(p, row, nb * C::BN + part * C::COLS_PER_EPI_WARP, C::COLS_PER_EPI_WARP);
       if (!mbar_wait(&tfull[buf], buf_phase, abort_flag, p.err)) break;
       tc_fence_after();
       constexpr int CHUNKS = C::COLS_PER_EPI_WARP / C::EPI_W;
-      I8Pend<C::EPI_W> pend;
 #pragma unroll 1
       for (int c = 0; c < CHUNKS; ++c) {
         const int tcol = part * C::COLS_PER_EPI_WARP + c * C::EPI_W;
@@ -552,8 +522,8 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[buf]);
         }
-        epilogue_chunk<ACT, C::EPI_W>(p, r, w_scale + c * C::EPI_W, w_bias + c * C::EPI_W, row,
-                                      nb * C::BN + tcol, pend, CHUNKS % 2 == 0 && c % 2 == 0);
+        epilogue_chunk<ACT, C::EPI_W, EXT>(p, r, w_scale + c * C::EPI_W, w_bias + c * C::EPI_W, row,
+                                           nb * C::BN + tcol);
       }
     }
   }
@@ -581,7 +551,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
 //   epilogue (warps 2-17, both CTAs): as the single-CTA kernel on the CTA's own rows; the
 //     last TMEM read of a tile arrives on the even CTA's `tempty` (2 x 16 arrivals).
 // All waits are bounded; both CTAs meet at a cluster barrier before TMEM is released.
-template <int PN, int ACT>
+template <int PN, int ACT, bool EXT>
 __global__ void __launch_bounds__(PairCfg::THREADS, 1)
     contraction_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                                const __grid_constant__ CUtensorMap tmW, const I8Params p) {
@@ -751,11 +721,10 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
       const int buf = local & 1;
       const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
       const int row = mb * 256 + static_cast<int>(rank) * ROWS + row_in_tile;
-      prefetch_residual(p, row, nb * PN + part * COLS, COLS);
+      if constexpr (EXT) prefetch_residual(p, row, nb * PN + part * COLS, COLS);
       if (!mbar_wait(&tfull[buf], buf_phase, abort_flag, p.err)) break;
       tc_fence_after();
       constexpr int CHUNKS = COLS / P::EPI_W;
-      I8Pend<P::EPI_W> pend;
 #pragma unroll 1
       for (int c = 0; c < CHUNKS; ++c) {
         const int tcol = part * COLS + c * P::EPI_W;
@@ -769,8 +738,8 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(tempty_even + buf * 8);
         }
-        epilogue_chunk<ACT, P::EPI_W>(p, r, w_scale + c * P::EPI_W, w_bias + c * P::EPI_W, row, nb * PN + tcol,
-                                      pend, CHUNKS % 2 == 0 && c % 2 == 0);
+        epilogue_chunk<ACT, P::EPI_W, EXT>(p, r, w_scale + c * P::EPI_W, w_bias + c * P::EPI_W, row,
+                                           nb * PN + tcol);
       }
     }
   }
@@ -784,14 +753,14 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
   }
 }
 
-template <int BN, int ACT, int ACB>
+template <int BN, int ACT, int ACB, bool EXT>
 lsc_status launch_cfg(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p,
                       int sm_count, cudaStream_t stream) {
   using C = I8Cfg<BN>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(contraction_i8_kernel<BN, ACT, ACB>,
+    attr_err = cudaFuncSetAttribute(contraction_i8_kernel<BN, ACT, ACB, EXT>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
   });
   if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(contraction_i8)");
@@ -807,33 +776,33 @@ lsc_status launch_cfg(const CUtensorMap& ta, const CUtensorMap& tw, const I8Para
   q.w_resident = (n_tiles == 1 && m_tiles >= 2 * grid && C::res_smem_bytes(kblocks) <= kSmemLimit) ? 1 : 0;
   q.a_stages = q.w_resident ? C::RES_STAGES : C::STAGES;
   const int smem = q.w_resident ? C::res_smem_bytes(kblocks) : C::SMEM_BYTES;
-  contraction_i8_kernel<BN, ACT, ACB><<<grid, C::THREADS, smem, stream>>>(ta, tw, q);
+  contraction_i8_kernel<BN, ACT, ACB, EXT><<<grid, C::THREADS, smem, stream>>>(ta, tw, q);
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }
 
-template <int BN, int ACB>
+template <int BN, int ACB, bool EXT>
 lsc_status launch_act(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p, int act,
                       int sm_count, cudaStream_t stream) {
   switch (act) {
-    case LSC_ACT_RELU: return launch_cfg<BN, LSC_ACT_RELU, ACB>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_RELU6: return launch_cfg<BN, LSC_ACT_RELU6, ACB>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_SILU: return launch_cfg<BN, LSC_ACT_SILU, ACB>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_GELU: return launch_cfg<BN, LSC_ACT_GELU, ACB>(ta, tw, p, sm_count, stream);
-    default: return launch_cfg<BN, LSC_ACT_NONE, ACB>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_RELU: return launch_cfg<BN, LSC_ACT_RELU, ACB, EXT>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_RELU6: return launch_cfg<BN, LSC_ACT_RELU6, ACB, EXT>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_SILU: return launch_cfg<BN, LSC_ACT_SILU, ACB, EXT>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_GELU: return launch_cfg<BN, LSC_ACT_GELU, ACB, EXT>(ta, tw, p, sm_count, stream);
+    default: return launch_cfg<BN, LSC_ACT_NONE, ACB, EXT>(ta, tw, p, sm_count, stream);
   }
 }
 
 // Launch of the CTA-pair kernel: clusters of 2, one pair per two SMs up to the number of
 // pairs the device can hold at once (persistent over 256 x 256 tiles).
-template <int PN, int ACT>
+template <int PN, int ACT, bool EXT>
 lsc_status launch_pair_act(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p, int sm_count,
                            cudaStream_t stream) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   static int max_pairs = 0;
   std::call_once(once, [sm_count] {
-    attr_err = cudaFuncSetAttribute(contraction_i8_pair_kernel<PN, ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_err = cudaFuncSetAttribute(contraction_i8_pair_kernel<PN, ACT, EXT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     PairCfg::SMEM_BYTES);
     if (attr_err != cudaSuccess) return;
     cudaLaunchConfig_t cfg = {};
@@ -847,7 +816,7 @@ lsc_status launch_pair_act(const CUtensorMap& ta, const CUtensorMap& tw, const I
     cfg.dynamicSmemBytes = PairCfg::SMEM_BYTES;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    attr_err = cudaOccupancyMaxActiveClusters(&max_pairs, contraction_i8_pair_kernel<PN, ACT>, &cfg);
+    attr_err = cudaOccupancyMaxActiveClusters(&max_pairs, contraction_i8_pair_kernel<PN, ACT, EXT>, &cfg);
   });
   if (attr_err != cudaSuccess) return cuda_error(attr_err, "contraction_i8_pair setup");
   if (max_pairs < 1) return set_error(LSC_ERROR_EXECUTION_FAILED, "gemm_i8: no CTA pair fits on the device");
@@ -865,28 +834,29 @@ lsc_status launch_pair_act(const CUtensorMap& ta, const CUtensorMap& tw, const I
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  LSC_CUDA_TRY(cudaLaunchKernelEx(&cfg, contraction_i8_pair_kernel<PN, ACT>, ta, tw, p));
+  LSC_CUDA_TRY(cudaLaunchKernelEx(&cfg, contraction_i8_pair_kernel<PN, ACT, EXT>, ta, tw, p));
   return LSC_SUCCESS;
 }
 
+template <bool EXT>
 lsc_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p, int act, int sm_count,
                        cudaStream_t stream) {
   switch (act) {
-    case LSC_ACT_RELU: return launch_pair_act<256, LSC_ACT_RELU>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_RELU6: return launch_pair_act<256, LSC_ACT_RELU6>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_SILU: return launch_pair_act<256, LSC_ACT_SILU>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_GELU: return launch_pair_act<256, LSC_ACT_GELU>(ta, tw, p, sm_count, stream);
-    default: return launch_pair_act<256, LSC_ACT_NONE>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_RELU: return launch_pair_act<256, LSC_ACT_RELU, EXT>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_RELU6: return launch_pair_act<256, LSC_ACT_RELU6, EXT>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_SILU: return launch_pair_act<256, LSC_ACT_SILU, EXT>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_GELU: return launch_pair_act<256, LSC_ACT_GELU, EXT>(ta, tw, p, sm_count, stream);
+    default: return launch_pair_act<256, LSC_ACT_NONE, EXT>(ta, tw, p, sm_count, stream);
   }
 }
 
-template <int ACB>
+template <int ACB, bool EXT = false>
 lsc_status launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p,
                      int act, int sm_count, cudaStream_t stream) {
   switch (bn) {
-    case 64: return launch_act<64, ACB>(ta, tw, p, act, sm_count, stream);
-    case 128: return launch_act<128, ACB>(ta, tw, p, act, sm_count, stream);
-    default: return launch_act<256, ACB>(ta, tw, p, act, sm_count, stream);
+    case 64: return launch_act<64, ACB, EXT>(ta, tw, p, act, sm_count, stream);
+    case 128: return launch_act<128, ACB, EXT>(ta, tw, p, act, sm_count, stream);
+    default: return launch_act<256, ACB, EXT>(ta, tw, p, act, sm_count, stream);
   }
 }
 
@@ -947,7 +917,6 @@ void fill_outputs(I8Params& p, const int32_t* bias, const float* scale, float s_
                                reinterpret_cast<uintptr_t>(bias);
   p.vec_ok = ((align_bits & 15) == 0 && (ldo % 16) == 0) ? 1 : 0;
   p.wide = (p.vec_ok && (reinterpret_cast<uintptr_t>(out_f32) & 31) == 0 && ldo % 8 == 0) ? 1 : 0;
-  if (p.vec_ok && (reinterpret_cast<uintptr_t>(out_i8) & 31) == 0 && ldo % 32 == 0) p.wide |= 8;
   p.err = err;
 }
 
@@ -1006,7 +975,11 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
       if (p.res_f32 && (reinterpret_cast<uintptr_t>(p.res_f32) & 31) == 0 && ldo % 8 == 0) p.wide |= 4;
     }
   }
-  if (pair) return launch_pair(ta, tw, p, act, ds->sm_count, stream);
+  if (p.out_f16 || p.res_f32) {
+    if (pair) return launch_pair<true>(ta, tw, p, act, ds->sm_count, stream);
+    return launch_bn<0, true>(bn, ta, tw, p, act, ds->sm_count, stream);
+  }
+  if (pair) return launch_pair<false>(ta, tw, p, act, ds->sm_count, stream);
   return launch_bn<0>(bn, ta, tw, p, act, ds->sm_count, stream);
 }
 
