@@ -635,6 +635,7 @@ def run_gpu(args):
                      "achieved": conv_tops, "peak": int8_peak, "unit": "TOPS", "frac": conv_tops / int8_peak,
                      "traffic": load_traffic("contraction_i8_conv_layer1_b256.md"), "peak_source": peak_source,
                      "conv_share_of_step": conv_ms / ms if ms > 0 else None},
+        "conv_us": {k: round(1e3 * float(np.mean([s.elapsed_time(e) for s, e in v])), 2) for k, v in evs.items()},
         "e2e": {"value": e2e_value, "unit": "img/s", "h2d_bytes_per_step": in_bytes * world,
                 "d2h_bytes_per_step": out_bytes * world, "api": "lsc_memcpy_h2d + network + lsc_memcpy_d2h",
                 "matches_device_run": e2e_ok},

@@ -216,7 +216,10 @@ void lsc_backend_destroy(lsc_backend* backend);                             /* D
 int32_t lsc_backend_is_available(const lsc_backend* backend);               /* is_available */
 lsc_status lsc_backend_capabilities(const lsc_backend* backend, lsc_caps* caps); /* capabilities */
 /* compile_operator(def, fusion, inputs, outputs): weights/static inputs that carry data are
- * prepacked on the device now (BN fold, per-channel INT8 quantization, layout change). */
+ * prepacked on the device now (BN fold, per-channel INT8 quantization, layout change).
+ * Conv2d with groups > 1 takes the reference's grouped filter [Cout, Cin/groups, KH, KW]
+ * (convolution.rs:105-122) and runs it as the dense convolution whose filter is zero outside
+ * each output channel's group: exact, at groups x the MACs. */
 lsc_status lsc_compile_operator(lsc_backend* backend, const lsc_op_desc* def,
                                 const lsc_tensor* inputs, int32_t n_inputs,
                                 const lsc_tensor* outputs, int32_t n_outputs, lsc_op** out);

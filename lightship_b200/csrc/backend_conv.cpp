@@ -98,6 +98,22 @@ lsc_status conv_weights_f32(lsc_op* op, const lsc_tensor* in, int n_in, std::vec
   return LSC_SUCCESS;
 }
 
+// A grouped filter [co, ci_g, kh, kw] (Conv2d::forward with groups, convolution.rs:105-122:
+// output channel o belongs to group o / (co / groups) and reads input channels
+// [group * ci_g, (group + 1) * ci_g)) as the dense [co, groups * ci_g, kh, kw] filter that is
+// zero outside each output channel's group.  The dense convolution then computes the grouped
+// one: the zero taps add exact zeros, and the per-output-channel maxima that the weight
+// quantization and BN fold read are unchanged.  Costs groups x the MACs of a grouped kernel.
+std::vector<float> expand_groups(const std::vector<float>& w, int64_t co, int64_t ci_g, int64_t taps,
+                                 int64_t groups) {
+  const int64_t ci = ci_g * groups, per_g = ci_g * taps, opg = co / groups;
+  std::vector<float> out(static_cast<size_t>(co * ci * taps), 0.0f);
+  for (int64_t o = 0; o < co; ++o)
+    memcpy(&out[static_cast<size_t>(o * ci * taps + (o / opg) * per_g)], &w[static_cast<size_t>(o * per_g)],
+           static_cast<size_t>(per_g) * sizeof(float));
+  return out;
+}
+
 // OIHW [co, ci, kh, kw] -> [co, kh, kw, cp] (zero channels ci..cp-1).
 template <typename T>
 std::vector<T> oihw_to_ohwi(const T* w, int64_t co, int64_t ci, int64_t kh, int64_t kw, int64_t cp) {
@@ -186,8 +202,7 @@ lsc_status compile_conv(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_te
   if (n_in < 2 || n_out < 1)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "Conv2d requires 2 inputs (input, filter) and 1 output");
   const lsc_op_desc& d = op->desc;
-  if (d.groups > 1)
-    return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "Conv2d with groups=%d is not supported by the CUDA backend", d.groups);
+  if (d.groups < 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Conv2d: groups must be positive (got %d)", d.groups);
   if (d.fusion != LSC_FUSION_NONE && d.fusion != LSC_FUSION_CONV_RELU && d.fusion != LSC_FUSION_CONV_RELU6 &&
       d.fusion != LSC_FUSION_CONV_BATCHNORM)
     return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "Conv2d fusion %d is not supported", d.fusion);
@@ -203,7 +218,12 @@ lsc_status compile_conv(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_te
   op->dh = d.dilation_h > 0 ? d.dilation_h : 1;
   op->dw = d.dilation_w > 0 ? d.dilation_w : 1;
   op->act = fusion_act(d);
-  const int64_t co = wt.shape[0], ci = wt.shape[1];
+  const int64_t groups = d.groups > 1 ? d.groups : 1;
+  const int64_t co = wt.shape[0];
+  if (co % groups != 0)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "Conv2d: %lld output channels do not split into %lld groups",
+                     (long long)co, (long long)groups);
+  const int64_t ci = wt.shape[1] * groups;  // the filter holds Cin/groups channels per output channel
   op->n = co;
   op->c_in = ci;
   op->kh = wt.shape[2];
@@ -219,6 +239,7 @@ lsc_status compile_conv(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_te
   } else {
     return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "Conv2d filter '%s' must be f32 (quantized at compile for INT8)", tname(wt));
   }
+  if (groups > 1) w = expand_groups(w, co, wt.shape[1], op->kh * op->kw, groups);
   const int64_t taps = op->kh * op->kw;
   void* p = nullptr;
   lsc_status st;

@@ -210,14 +210,50 @@ def test_conv_f32_geometry(be, n, ci, co, h, wd, k, s, p, d):
     assert _rel_err(y.numpy().reshape(ref.shape), ref, mag) <= TOL_3XTF32
 
 
-def test_conv_groups_unsupported(be):
+def test_conv_groups_kat(be):
+    """convolution.rs:411-447: groups=2, input channels filled 1, 2, 3, 4, a 1x1 ones filter of
+    shape [4, 2, 1, 1]: output channels 0-1 sum channels 0-1 (3), channels 2-3 sum 2-3 (7)."""
+    B = _B()
+    r = K.CONV_GROUPS
+    x = np.stack([np.full((2, 2), v, np.float32) for v in r["channel_values"]])[None]
+    y = B.Tensor("y", [1], B.DataType.F32, np.zeros(16, np.float32))
+    _run(be, B.OperatorDef("conv", B.OperatorType.Conv2d, groups=r["groups"]),
+         [B.Tensor("x", list(x.shape), B.DataType.F32, x),
+          B.Tensor("w", list(r["w_shape"]), B.DataType.F32, np.ones(r["w_shape"], np.float32))], [y])
+    assert y.shape == list(r["y_shape"])
+    out = y.numpy().reshape(r["y_shape"])
+    assert np.all(out[0, :2] == 3.0) and np.all(out[0, 2:] == 7.0)
+
+
+@pytest.mark.parametrize("n,ci,co,h,k,s,p,g", [(2, 8, 12, 13, 3, 1, 1, 2), (1, 32, 32, 14, 3, 2, 1, 32),
+                                               (2, 12, 6, 9, 5, 1, 2, 3)])
+def test_conv_f32_groups(be, n, ci, co, h, k, s, p, g):
+    B = _B()
+    rng = np.random.default_rng(n * 1000 + ci * 10 + g)
+    x = rng.normal(size=(n, ci, h, h)).astype(np.float32)
+    w = rng.normal(0, 0.2, size=(co, ci // g, k, k)).astype(np.float32)
+    bias = rng.normal(size=co).astype(np.float32)
+    xt = B.Tensor("x", list(x.shape), B.DataType.F32, x)
+    oh = (h + 2 * p - k) // s + 1
+    y = B.Tensor("y", [1], B.DataType.F32, np.zeros(n * co * oh * oh, np.float32))
+    _run(be, B.OperatorDef("conv", B.OperatorType.Conv2d, stride=(s, s), padding=(p, p), groups=g),
+         [xt, B.Tensor("w", list(w.shape), B.DataType.F32, w), B.Tensor("b", [co], B.DataType.F32, bias)], [y],
+         runtime_inputs=[xt])
+    ref = orc.conv2d_nchw(x, w, bias, (s, s), (p, p), groups=g)
+    mag = orc.conv2d_nchw(np.abs(x), np.abs(w), None, (s, s), (p, p), groups=g).astype(np.float64) \
+        + np.abs(bias)[None, :, None, None]
+    assert y.shape == list(ref.shape)
+    assert _rel_err(y.numpy().reshape(ref.shape), ref, mag) <= TOL_3XTF32
+
+
+def test_conv_groups_must_divide_output_channels(be):
     B = _B()
     x = B.Tensor("x", [1, 4, 2, 2], B.DataType.F32, np.ones((1, 4, 2, 2), np.float32))
-    w = B.Tensor("w", [4, 2, 1, 1], B.DataType.F32, np.ones((4, 2, 1, 1), np.float32))
+    w = B.Tensor("w", [3, 2, 1, 1], B.DataType.F32, np.ones((3, 2, 1, 1), np.float32))
     with pytest.raises(B.LightShipError) as e:
         be.compile_operator(B.OperatorDef("conv", B.OperatorType.Conv2d, groups=2), None, [x, w],
                             [B.Tensor("y", [1], B.DataType.F32)])
-    assert e.value.code == 11
+    assert e.value.code == 2  # LSC_ERROR_INVALID_ARGUMENT
 
 
 # ------------------------------------------------------------------------------ BatchNorm / activations
@@ -314,4 +350,35 @@ def test_conv_int8_compiled_from_f32_weights(be, fold_bn):
     assert q.shape == [n, h, wd, co]
     np.testing.assert_array_equal(acc.numpy().reshape(want[2].shape), want[2])
     np.testing.assert_array_equal(y.numpy().reshape(want[1].shape).view(np.uint32), want[1].view(np.uint32))
+    np.testing.assert_array_equal(q.numpy().reshape(want[0].shape), want[0])
+
+
+@pytest.mark.parametrize("ci,co,groups,stride", [(64, 64, 2, 1), (32, 64, 4, 2), (48, 48, 48, 1)])
+def test_conv_int8_groups(be, ci, co, groups, stride):
+    """Grouped INT8 Conv2d (the last case depthwise): the backend quantizes the grouped f32
+    filter per output channel and runs it densely with zeros outside each group; the oracle runs
+    its grouped int8 convolution on the same quantized weights.  Bit-exact."""
+    B = _B()
+    rng = np.random.default_rng(ci + co + groups)
+    n, h = 2, 11
+    cig = ci // groups
+    x = rng.integers(-127, 128, size=(n, h, h, ci), dtype=np.int8)
+    w = rng.normal(0, np.sqrt(2 / (9 * cig)), size=(co, cig, 3, 3)).astype(np.float32)
+    bias = rng.normal(0, 0.1, co).astype(np.float32)
+    s_a, s_out = 0.02, 0.05
+    wq, sw = orc.quantize_weights_per_channel(np.ascontiguousarray(w.transpose(0, 2, 3, 1)))
+    scale = (np.float32(s_a) * sw).astype(np.float32)
+    bq = np.array([orc.quantize_value(float(bias[o]), float(scale[o]), 0, orc.QINT32) for o in range(co)], np.int32)
+    want = orc.conv2d_i8_nhwc_chain(x, wq, bq, scale, (stride, stride), (1, 1), (1, 1), groups, orc.ACT_RELU,
+                                    s_out, orc.ROUND_HALF_AWAY)
+    xt = B.Tensor("x", list(x.shape), B.DataType.QInt8, x, layout=B.StorageLayout.NHWC,
+                  quantization=B.Quantization([s_a]))
+    q = B.Tensor("q", [1], B.DataType.QInt8, np.zeros(want[0].size, np.int8))
+    acc = B.Tensor("acc", [1], B.DataType.I32, np.zeros(want[0].size, np.int32))
+    opdef = B.OperatorDef("conv", B.OperatorType.Conv2d, stride=(stride, stride), padding=(1, 1), groups=groups,
+                          activation=B.Activation.ReLU, output_scale=s_out)
+    _run(be, opdef, [xt, B.Tensor("w", list(w.shape), B.DataType.F32, w), B.Tensor("b", [co], B.DataType.F32, bias)],
+         [q, acc], fusion=B.FusionInfo.conv_relu(), runtime_inputs=[xt])
+    assert q.shape == list(want[0].shape)
+    np.testing.assert_array_equal(acc.numpy().reshape(want[2].shape), want[2])
     np.testing.assert_array_equal(q.numpy().reshape(want[0].shape), want[0])
