@@ -408,6 +408,13 @@ def gemm_measure(torch, dev, steps, warmup):
     return res, s_out
 
 
+def auto_branches(per_gpu_batch):
+    """Concurrent image groups for a per-GPU ResNet batch.  Measured on B200 (graph step time,
+    batch 32 / 64 / 128 / 256): two groups 322 / 450 / 676 / 1132 us against one chain's
+    299 / 411 / 666 / 1151 us, four groups at batch 32 362 us; one chain is kept."""
+    return 1
+
+
 def shard_bounds(batch, world, rank):
     """The contiguous slice [lo, hi) of the global batch that rank owns (batch % world == 0)."""
     if batch % world:
@@ -570,7 +577,8 @@ def run_gpu(args):
     conv_ms = sum(np.mean([s.elapsed_time(e) for s, e in v]) for v in evs.values())
     conv_tops = sum(conv_ops.values()) * per / (conv_ms * 1e-3) / 1e12
 
-    graph = model.capture(x_dev)
+    branches = args.branches if args.branches > 0 else auto_branches(per)
+    graph = model.capture(x_dev, branches=branches, concurrent_downsample=bool(args.ds_side))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for _ in range(args.warmup):
         flush.zero_()
@@ -619,9 +627,48 @@ def run_gpu(args):
         e2e_step()
     ee.record(stream)
     torch.cuda.synchronize(dev)
-    e2e_ms = max_over_ranks(es.elapsed_time(ee) / e2e_steps)
-    e2e_value = batch / (e2e_ms * 1e-3)
+    e2e_seq_ms = max_over_ranks(es.elapsed_time(ee) / e2e_steps)
     e2e_ok = bool(torch.equal(logits_host, model.logits.cpu()))
+
+    # the same, pipelined as a server runs it: step i+1's input upload (copy stream) overlaps
+    # step i's network (compute stream); two input buffers, one graph captured on each; the
+    # logits download follows each graph on the compute stream
+    x_dev2 = torch.empty_like(x_dev)
+    graph2 = model.capture(x_dev2, branches=branches, concurrent_downsample=bool(args.ds_side))
+    copy_stream = torch.cuda.Stream(dev)
+    cptr = C.c_void_p(copy_stream.cuda_stream)
+    bufs, graphs = (x_dev, x_dev2), (graph, graph2)
+    loaded = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+    for ev_ in freed:
+        ev_.record(stream)
+
+    def e2e_pipelined(n_steps):
+        for i in range(n_steps):
+            b = i & 1
+            copy_stream.wait_event(freed[b])
+            _lib.check(lib.lsc_memcpy_h2d(C.c_void_p(bufs[b].data_ptr()), C.c_void_p(x_host.data_ptr()), in_bytes,
+                                          cptr))
+            loaded[b].record(copy_stream)
+            stream.wait_event(loaded[b])
+            graphs[b].replay()
+            _lib.check(lib.lsc_memcpy_d2h(C.c_void_p(logits_host.data_ptr()), C.c_void_p(model.logits.data_ptr()),
+                                          out_bytes, sptr))
+            freed[b].record(stream)
+
+    e2e_pipelined(4)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ps, pe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ps.record(stream)
+    copy_stream.wait_event(ps)
+    e2e_pipelined(e2e_steps)
+    pe.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(ps.elapsed_time(pe) / e2e_steps)
+    e2e_value = batch / (e2e_ms * 1e-3)
+    e2e_ok = e2e_ok and bool(torch.equal(logits_host, model.logits.cpu()))
+    del graph2
 
     line = {
         "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
@@ -629,6 +676,7 @@ def run_gpu(args):
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": RESNET_WORKLOAD, "global_batch": batch, "per_gpu_batch": per,
                    "image": IMAGE, "parallelism": f"batch split x{world} (no collective)",
+                   "graph_branches": branches, "downsample_side_stream": bool(args.ds_side),
                    "l2": "flushed (256 MiB write) before every timed step", "seed": NET_SEED},
         "network_tops": img_ops * batch / (ms_max * 1e-3) / 1e12,
         "roofline": {"bound": "tensor", "kernel": "contraction_i8_kernel (INT8 implicit-GEMM conv)",
@@ -638,7 +686,9 @@ def run_gpu(args):
         "conv_us": {k: round(1e3 * float(np.mean([s.elapsed_time(e) for s, e in v])), 2) for k, v in evs.items()},
         "e2e": {"value": e2e_value, "unit": "img/s", "h2d_bytes_per_step": in_bytes * world,
                 "d2h_bytes_per_step": out_bytes * world, "api": "lsc_memcpy_h2d + network + lsc_memcpy_d2h",
-                "matches_device_run": e2e_ok},
+                "pipelined": "step i+1's upload (copy stream) overlaps step i's network; every step's "
+                             "upload and logits download are inside the timed region",
+                "sequential_value": batch / (e2e_seq_ms * 1e-3), "matches_device_run": e2e_ok},
         "gpu_launches": model.kernel_launches() * args.steps,
         "clocks": clocks,
     }
@@ -683,6 +733,10 @@ def main():
     ap.add_argument("--impl", choices=["lightship", "reference"], default="lightship")
     ap.add_argument("--workload", choices=["resnet18", "gemm", "bert"], default="resnet18")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--branches", type=int, default=0,
+                    help="image groups run concurrently inside the ResNet graph (0 = chosen by the per-GPU batch)")
+    ap.add_argument("--ds-side", type=int, default=1,
+                    help="1 = run each stage's downsample conv on a side stream beside its first conv")
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH,
                     help="global ResNet batch (default 256, the benchmark's; smaller only for profiling)")
     ap.add_argument("--no-gemm", action="store_true", help="skip the 4096^3 GEMM sub-measurement")

@@ -359,6 +359,8 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the next kernel on the stream may now be scheduled onto SMs this grid leaves
+  griddep_launch_dependents();
 
   const int m_tiles = (p.m + C::BM - 1) / C::BM;
   const int n_tiles = (p.n + C::BN - 1) / C::BN;
@@ -371,10 +373,12 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       int issued = 0;
       bool ok = true;
       if (wres) {
-        // the whole weight tile (one N tile: nb = 0) once, on its own barrier
+        // the whole weight tile (one N tile: nb = 0) once, on its own barrier; the weights are
+        // constant, so they are requested before the wait for the previous kernel
         mbar_arrive_expect_tx(wfull, static_cast<uint32_t>(kblocks * C::B_BYTES));
         for (int kb = 0; kb < kblocks; ++kb) tma_load_2d(&tmW, wfull, sW + kb * C::B_BYTES, kb * C::BK, 0);
       }
+      griddep_wait();  // A is the previous kernel's output
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int mb = tile % m_tiles, nb = tile / m_tiles;
         // filter-origin coordinates of the tile's first output pixel (convolution only)
@@ -490,6 +494,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
     int32_t* w_bias = reinterpret_cast<int32_t*>(w_scale + C::COLS_PER_EPI_WARP);
     int staged_nb = -1;
     int local = 0;
+    griddep_wait();  // outputs and the residual belong to earlier kernels until they finish
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int mb = tile % m_tiles, nb = tile / m_tiles;
       if (nb != staged_nb) {
@@ -612,6 +617,7 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t full_even = mapa_shared(smem_u32(full), 0);
   const uint32_t tempty_even = mapa_shared(smem_u32(tempty), 0);
+  griddep_launch_dependents();
 
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int m_tiles = (p.m + 255) / 256;
@@ -625,6 +631,7 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
       uint32_t stage = 0, phase = 0;
       int issued = 0;
       bool ok = true;
+      griddep_wait();  // A is the previous kernel's output
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
         const int mb = tile % m_tiles, nb = tile / m_tiles;
         for (int kb = 0; kb < kblocks; ++kb) {
@@ -706,6 +713,7 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
     int32_t* w_bias = reinterpret_cast<int32_t*>(w_scale + COLS);
     int staged_nb = -1;
     int local = 0;
+    griddep_wait();  // outputs and the residual belong to earlier kernels until they finish
     for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
       const int mb = tile % m_tiles, nb = tile / m_tiles;
       if (nb != staged_nb) {
@@ -755,7 +763,7 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
 
 template <int BN, int ACT, int ACB, bool EXT>
 lsc_status launch_cfg(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p,
-                      int sm_count, cudaStream_t stream) {
+                      const DeviceState& ds, cudaStream_t stream) {
   using C = I8Cfg<BN>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
@@ -767,7 +775,7 @@ lsc_status launch_cfg(const CUtensorMap& ta, const CUtensorMap& tw, const I8Para
   const int m_tiles = (p.m + C::BM - 1) / C::BM;
   const int n_tiles = (p.n + C::BN - 1) / C::BN;
   const int tiles = m_tiles * n_tiles;
-  const int grid = tiles < sm_count ? tiles : sm_count;
+  const int grid = tiles < ds.sm_count ? tiles : ds.sm_count;
   // Keep the weights resident when there is a single N tile, they fit beside a RES_STAGES A
   // ring, and each CTA runs several M tiles (so the one-time load is amortised): the W tile
   // then crosses L2 once per CTA instead of once per M tile.
@@ -776,32 +784,32 @@ lsc_status launch_cfg(const CUtensorMap& ta, const CUtensorMap& tw, const I8Para
   q.w_resident = (n_tiles == 1 && m_tiles >= 2 * grid && C::res_smem_bytes(kblocks) <= kSmemLimit) ? 1 : 0;
   q.a_stages = q.w_resident ? C::RES_STAGES : C::STAGES;
   const int smem = q.w_resident ? C::res_smem_bytes(kblocks) : C::SMEM_BYTES;
-  contraction_i8_kernel<BN, ACT, ACB, EXT><<<grid, C::THREADS, smem, stream>>>(ta, tw, q);
-  LSC_CUDA_TRY(cudaGetLastError());
+  LSC_CUDA_TRY(launch_dependent(ds.overlap_launches, contraction_i8_kernel<BN, ACT, ACB, EXT>, dim3(grid), dim3(C::THREADS),
+                                smem, stream, ta, tw, q));
   return LSC_SUCCESS;
 }
 
 template <int BN, int ACB, bool EXT>
 lsc_status launch_act(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p, int act,
-                      int sm_count, cudaStream_t stream) {
+                      const DeviceState& ds, cudaStream_t stream) {
   switch (act) {
-    case LSC_ACT_RELU: return launch_cfg<BN, LSC_ACT_RELU, ACB, EXT>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_RELU6: return launch_cfg<BN, LSC_ACT_RELU6, ACB, EXT>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_SILU: return launch_cfg<BN, LSC_ACT_SILU, ACB, EXT>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_GELU: return launch_cfg<BN, LSC_ACT_GELU, ACB, EXT>(ta, tw, p, sm_count, stream);
-    default: return launch_cfg<BN, LSC_ACT_NONE, ACB, EXT>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_RELU: return launch_cfg<BN, LSC_ACT_RELU, ACB, EXT>(ta, tw, p, ds, stream);
+    case LSC_ACT_RELU6: return launch_cfg<BN, LSC_ACT_RELU6, ACB, EXT>(ta, tw, p, ds, stream);
+    case LSC_ACT_SILU: return launch_cfg<BN, LSC_ACT_SILU, ACB, EXT>(ta, tw, p, ds, stream);
+    case LSC_ACT_GELU: return launch_cfg<BN, LSC_ACT_GELU, ACB, EXT>(ta, tw, p, ds, stream);
+    default: return launch_cfg<BN, LSC_ACT_NONE, ACB, EXT>(ta, tw, p, ds, stream);
   }
 }
 
 // Launch of the CTA-pair kernel: clusters of 2, one pair per two SMs up to the number of
 // pairs the device can hold at once (persistent over 256 x 256 tiles).
 template <int PN, int ACT, bool EXT>
-lsc_status launch_pair_act(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p, int sm_count,
+lsc_status launch_pair_act(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p, const DeviceState& ds,
                            cudaStream_t stream) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   static int max_pairs = 0;
-  std::call_once(once, [sm_count] {
+  std::call_once(once, [&ds] {
     attr_err = cudaFuncSetAttribute(contraction_i8_pair_kernel<PN, ACT, EXT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     PairCfg::SMEM_BYTES);
     if (attr_err != cudaSuccess) return;
@@ -811,7 +819,7 @@ lsc_status launch_pair_act(const CUtensorMap& ta, const CUtensorMap& tw, const I
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(static_cast<unsigned>(sm_count & ~1));
+    cfg.gridDim = dim3(static_cast<unsigned>(ds.sm_count & ~1));
     cfg.blockDim = dim3(PairCfg::THREADS);
     cfg.dynamicSmemBytes = PairCfg::SMEM_BYTES;
     cfg.attrs = attr;
@@ -823,40 +831,42 @@ lsc_status launch_pair_act(const CUtensorMap& ta, const CUtensorMap& tw, const I
   const int tiles = ((p.m + 255) / 256) * ((p.n + PN - 1) / PN);
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see launch_dependent
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
   cfg.blockDim = dim3(PairCfg::THREADS);
   cfg.dynamicSmemBytes = PairCfg::SMEM_BYTES;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = ds.overlap_launches ? 2 : 1;
   LSC_CUDA_TRY(cudaLaunchKernelEx(&cfg, contraction_i8_pair_kernel<PN, ACT, EXT>, ta, tw, p));
   return LSC_SUCCESS;
 }
 
 template <bool EXT>
-lsc_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p, int act, int sm_count,
+lsc_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p, int act, const DeviceState& ds,
                        cudaStream_t stream) {
   switch (act) {
-    case LSC_ACT_RELU: return launch_pair_act<256, LSC_ACT_RELU, EXT>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_RELU6: return launch_pair_act<256, LSC_ACT_RELU6, EXT>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_SILU: return launch_pair_act<256, LSC_ACT_SILU, EXT>(ta, tw, p, sm_count, stream);
-    case LSC_ACT_GELU: return launch_pair_act<256, LSC_ACT_GELU, EXT>(ta, tw, p, sm_count, stream);
-    default: return launch_pair_act<256, LSC_ACT_NONE, EXT>(ta, tw, p, sm_count, stream);
+    case LSC_ACT_RELU: return launch_pair_act<256, LSC_ACT_RELU, EXT>(ta, tw, p, ds, stream);
+    case LSC_ACT_RELU6: return launch_pair_act<256, LSC_ACT_RELU6, EXT>(ta, tw, p, ds, stream);
+    case LSC_ACT_SILU: return launch_pair_act<256, LSC_ACT_SILU, EXT>(ta, tw, p, ds, stream);
+    case LSC_ACT_GELU: return launch_pair_act<256, LSC_ACT_GELU, EXT>(ta, tw, p, ds, stream);
+    default: return launch_pair_act<256, LSC_ACT_NONE, EXT>(ta, tw, p, ds, stream);
   }
 }
 
 template <int ACB, bool EXT = false>
 lsc_status launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const I8Params& p,
-                     int act, int sm_count, cudaStream_t stream) {
+                     int act, const DeviceState& ds, cudaStream_t stream) {
   switch (bn) {
-    case 64: return launch_act<64, ACB, EXT>(ta, tw, p, act, sm_count, stream);
-    case 128: return launch_act<128, ACB, EXT>(ta, tw, p, act, sm_count, stream);
-    default: return launch_act<256, ACB, EXT>(ta, tw, p, act, sm_count, stream);
+    case 64: return launch_act<64, ACB, EXT>(ta, tw, p, act, ds, stream);
+    case 128: return launch_act<128, ACB, EXT>(ta, tw, p, act, ds, stream);
+    default: return launch_act<256, ACB, EXT>(ta, tw, p, act, ds, stream);
   }
 }
 
@@ -976,11 +986,11 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
     }
   }
   if (p.out_f16 || p.res_f32) {
-    if (pair) return launch_pair<true>(ta, tw, p, act, ds->sm_count, stream);
-    return launch_bn<0, true>(bn, ta, tw, p, act, ds->sm_count, stream);
+    if (pair) return launch_pair<true>(ta, tw, p, act, *ds, stream);
+    return launch_bn<0, true>(bn, ta, tw, p, act, *ds, stream);
   }
-  if (pair) return launch_pair<false>(ta, tw, p, act, ds->sm_count, stream);
-  return launch_bn<0>(bn, ta, tw, p, act, ds->sm_count, stream);
+  if (pair) return launch_pair<false>(ta, tw, p, act, *ds, stream);
+  return launch_bn<0>(bn, ta, tw, p, act, *ds, stream);
 }
 
 lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& g,
@@ -1062,10 +1072,10 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
   if (reinterpret_cast<uintptr_t>(residual) & 15) p.vec_ok = 0;
   if (!p.vec_ok) p.wide = 0;
   switch (acb) {
-    case 128: return launch_bn<128>(bn, ta, tw, p, act, ds->sm_count, stream);
-    case 64: return launch_bn<64>(bn, ta, tw, p, act, ds->sm_count, stream);
-    case 32: return launch_bn<32>(bn, ta, tw, p, act, ds->sm_count, stream);
-    default: return launch_bn<16>(bn, ta, tw, p, act, ds->sm_count, stream);
+    case 128: return launch_bn<128>(bn, ta, tw, p, act, *ds, stream);
+    case 64: return launch_bn<64>(bn, ta, tw, p, act, *ds, stream);
+    case 32: return launch_bn<32>(bn, ta, tw, p, act, *ds, stream);
+    default: return launch_bn<16>(bn, ta, tw, p, act, *ds, stream);
   }
 }
 

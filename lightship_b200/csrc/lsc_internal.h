@@ -27,7 +27,39 @@ struct DeviceState {
   size_t smem_optin = 0;
   size_t total_memory = 0;
   uint32_t* err_word = nullptr;  // device address of the sticky error word
+  bool overlap_launches = true;  // dependent launches (LSC_OVERLAP_LAUNCHES=0 turns them off)
 };
+
+// Launches `kernel` with programmatic stream serialization when `overlap` is set: its CTAs may
+// be scheduled, and run their prologue, while the previous kernel on the stream is finishing.
+// Every kernel launched this way calls griddep_wait() before it reads what an earlier kernel
+// wrote or writes what an earlier kernel may still read.  Graph capture keeps the relation.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_dependent(bool overlap, void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                                    size_t smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = overlap ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+#ifdef __CUDACC__
+// Device side of a dependent launch.  griddep_wait(): blocks the calling thread until the
+// kernels this grid depends on have completed and their memory is visible (returns at once
+// when the launch had no such dependency).  griddep_launch_dependents(): this CTA allows the
+// next dependent kernel to be scheduled; it starts once every CTA has said so or exited.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+#endif
 
 // State of the calling thread's current device; nullptr (with the error set) on failure.
 DeviceState* current_device_state();
@@ -132,6 +164,9 @@ lsc_status launch_quantize_nchw_to_s2d_i8(const float* x, int8_t* y, int64_t n, 
 lsc_status launch_maxpool_i8(const int8_t* x, int8_t* y, int64_t n, int64_t h, int64_t w, int64_t c,
                              int64_t oh, int64_t ow, int kh, int kw, int sh, int sw, int ph, int pw,
                              cudaStream_t st);
+lsc_status launch_maxpool_f32(const float* x, float* y, int64_t n, int64_t c, int64_t h, int64_t w, int64_t oh,
+                              int64_t ow, int kh, int kw, int sh, int sw, int ph, int pw, cudaStream_t st);
+lsc_status launch_avgpool_f32(const float* x, float* y, int64_t n, int64_t c, int64_t hw, cudaStream_t st);
 lsc_status launch_avgpool_i8(const int8_t* x, int64_t n, int64_t hw, int64_t c, float s_in, float s_out,
                              int rounding, int8_t* y_i8, float* y_f32, cudaStream_t st);
 

@@ -39,6 +39,8 @@ __device__ __forceinline__ int8_t quantize_i8(float v, float s) {
 template <int RND>
 __global__ void quantize_nchw_to_nhwc_kernel(const float* __restrict__ x, int8_t* __restrict__ y,
                                              int c, int hw, int cp, float scale, float inv_s) {
+  griddep_wait();  // launched as a dependent kernel: inputs and outputs are settled from here on
+  griddep_launch_dependents();
   const int groups = cp >> 4;
   const int img = blockIdx.y;
   const float* xi = x + static_cast<size_t>(img) * c * hw;
@@ -68,6 +70,8 @@ template <int RND>
 __global__ void quantize_nchw_to_s2d_kernel(const float* __restrict__ x, int8_t* __restrict__ y,
                                             int c, int h, int w, int ph, int pw, int blk, int hs,
                                             int ws, int cp, float scale, float inv_s) {
+  griddep_wait();  // launched as a dependent kernel: inputs and outputs are settled from here on
+  griddep_launch_dependents();
   const int groups = cp >> 4;
   const int ys = blockIdx.y, img = blockIdx.z;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -106,6 +110,8 @@ template <int RND>
 __global__ void quantize_nchw_to_s2d_c3b2_kernel(const float* __restrict__ x, int8_t* __restrict__ y,
                                                  int h, int w, int ph, int pw, int hs, int ws,
                                                  float scale, float inv_s) {
+  griddep_wait();  // launched as a dependent kernel: inputs and outputs are settled from here on
+  griddep_launch_dependents();
   const int ys = blockIdx.y, img = blockIdx.z;
   const int xs = blockIdx.x * blockDim.x + threadIdx.x;
   if (xs >= ws) return;
@@ -142,6 +148,8 @@ __device__ __forceinline__ uint32_t vmax_s8x4(uint32_t a, uint32_t b) { return _
 template <int KH, int KW>
 __global__ void maxpool_i8_kernel(const int8_t* __restrict__ x, int8_t* __restrict__ y, int h, int w,
                                   int c, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw) {
+  griddep_wait();  // launched as a dependent kernel: inputs and outputs are settled from here on
+  griddep_launch_dependents();
   const int groups = c >> 4;
   const int oy = blockIdx.y, img = blockIdx.z;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -174,6 +182,8 @@ template <int RND>
 __global__ void avgpool_i8_kernel(const int8_t* __restrict__ x, int64_t n, int64_t hw, int64_t c,
                                   float s_in, float s_out, int8_t* __restrict__ y_i8,
                                   float* __restrict__ y_f32) {
+  griddep_wait();  // launched as a dependent kernel: inputs and outputs are settled from here on
+  griddep_launch_dependents();
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
   const int64_t slabs = (c + 31) / 32;
   for (int64_t wi = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
@@ -197,7 +207,81 @@ int grid_p(int64_t n, int sm_count) {
   return static_cast<int>(g < 1 ? 1 : g);
 }
 
+// MaxPool2d on f32 NCHW (Pool2d::max_pool2d, operator/pooling.rs): the max over the window's
+// in-bounds taps (padding taps take no part), one thread per output element.
+__global__ void maxpool_f32_nchw_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t planes,
+                                        int h, int w, int oh, int ow, int kh, int kw, int sh, int sw, int ph,
+                                        int pw) {
+  griddep_wait();  // launched as a dependent kernel: inputs and outputs are settled from here on
+  griddep_launch_dependents();
+  const int64_t total = planes * oh * ow;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int ox = static_cast<int>(i % ow);
+    const int oy = static_cast<int>((i / ow) % oh);
+    const int64_t plane = i / (static_cast<int64_t>(ow) * oh);
+    const float* xp = x + plane * h * w;
+    float m = -INFINITY;
+    for (int r = 0; r < kh; ++r) {
+      const int iy = oy * sh - ph + r;
+      if (iy < 0 || iy >= h) continue;
+      for (int c = 0; c < kw; ++c) {
+        const int ix = ox * sw - pw + c;
+        if (ix < 0 || ix >= w) continue;
+        m = fmaxf(m, __ldg(xp + static_cast<int64_t>(iy) * w + ix));
+      }
+    }
+    y[i] = m;
+  }
+}
+
+// GlobalAvgPool2d on f32 NCHW (operator/pooling.rs:457-490): (sum of the plane) / (H*W), one
+// warp per (n, c) plane; the sum is tree-ordered (the reference sums in sequence).
+__global__ void avgpool_f32_nchw_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t planes,
+                                        int64_t hw) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t p = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); p < planes;
+       p += warps) {
+    const float* xp = x + p * hw;
+    float acc = 0.0f;
+    for (int64_t i = lane; i < hw; i += 32) acc = __fadd_rn(acc, __ldg(xp + i));
+    for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+    if (lane == 0) y[p] = __fdiv_rn(acc, static_cast<float>(hw));
+  }
+}
+
 }  // namespace
+
+lsc_status launch_maxpool_f32(const float* x, float* y, int64_t n, int64_t c, int64_t h, int64_t w, int64_t oh,
+                              int64_t ow, int kh, int kw, int sh, int sw, int ph, int pw, cudaStream_t st) {
+  const int64_t total = n * c * oh * ow;
+  if (total == 0) return LSC_SUCCESS;
+  if (h > INT32_MAX || w > INT32_MAX) return set_error(LSC_ERROR_INVALID_ARGUMENT, "maxpool: image too large");
+  DeviceState* ds = current_device_state();
+  if (!ds) return LSC_ERROR_DEVICE_ERROR;
+  int64_t g = (total + 255) / 256;
+  if (g > static_cast<int64_t>(ds->sm_count) * 8) g = static_cast<int64_t>(ds->sm_count) * 8;
+  LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, maxpool_f32_nchw_kernel, dim3(static_cast<unsigned>(g)),
+                                dim3(256), 0, st, x, y, n * c, static_cast<int>(h), static_cast<int>(w),
+                                static_cast<int>(oh), static_cast<int>(ow), kh, kw, sh, sw, ph, pw));
+  return LSC_SUCCESS;
+}
+
+lsc_status launch_avgpool_f32(const float* x, float* y, int64_t n, int64_t c, int64_t hw, cudaStream_t st) {
+  const int64_t planes = n * c;
+  if (planes == 0) return LSC_SUCCESS;
+  if (hw <= 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "global avgpool: empty spatial extent");
+  DeviceState* ds = current_device_state();
+  if (!ds) return LSC_ERROR_DEVICE_ERROR;
+  int64_t g = (planes + 7) / 8;
+  if (g > static_cast<int64_t>(ds->sm_count) * 8) g = static_cast<int64_t>(ds->sm_count) * 8;
+  LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, avgpool_f32_nchw_kernel, dim3(static_cast<unsigned>(g)),
+                                dim3(256), 0, st, x, y, planes, hw));
+  return LSC_SUCCESS;
+}
 
 // RN(1 / s) when s and its reciprocal are normal floats (the reciprocal requantization's
 // precondition), else 0, which makes every element take the division.
@@ -224,11 +308,11 @@ lsc_status launch_quantize_nchw_to_nhwc_i8(const float* x, int8_t* y, int64_t n,
   if (bx > cap) bx = cap;
   const dim3 grid(static_cast<unsigned>(bx < 1 ? 1 : bx), static_cast<unsigned>(n));
   if (rounding == LSC_ROUND_HALF_EVEN)
-    quantize_nchw_to_nhwc_kernel<LSC_ROUND_HALF_EVEN><<<grid, 256, 0, st>>>(x, y, static_cast<int>(c), static_cast<int>(hw),
-                                                                           static_cast<int>(cp), scale, inv_s);
+    LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, quantize_nchw_to_nhwc_kernel<LSC_ROUND_HALF_EVEN>, grid, dim3(256), 0, st,
+                                  x, y, static_cast<int>(c), static_cast<int>(hw), static_cast<int>(cp), scale, inv_s));
   else
-    quantize_nchw_to_nhwc_kernel<LSC_ROUND_HALF_AWAY><<<grid, 256, 0, st>>>(x, y, static_cast<int>(c), static_cast<int>(hw),
-                                                                           static_cast<int>(cp), scale, inv_s);
+    LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, quantize_nchw_to_nhwc_kernel<LSC_ROUND_HALF_AWAY>, grid, dim3(256), 0, st,
+                                  x, y, static_cast<int>(c), static_cast<int>(hw), static_cast<int>(cp), scale, inv_s));
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }
@@ -249,30 +333,34 @@ lsc_status launch_quantize_nchw_to_s2d_i8(const float* x, int8_t* y, int64_t n, 
   if (n == 0 || hs == 0 || per_row == 0) return LSC_SUCCESS;
   if (n > 65535 || hs > 65535 || c * h * w > INT32_MAX || ws * cp > INT32_MAX || blk > 64)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "space-to-depth: batch or image too large");
+  DeviceState* ds = current_device_state();
+  if (!ds) return LSC_ERROR_DEVICE_ERROR;
   const dim3 grid(static_cast<unsigned>((per_row + 127) / 128), static_cast<unsigned>(hs), static_cast<unsigned>(n));
   const int ic = static_cast<int>(c), ih = static_cast<int>(h), iw = static_cast<int>(w);
   const float inv_s = reciprocal_or_zero(scale);
   if (c == 3 && blk == 2 && cp == 16) {
     const dim3 g2(static_cast<unsigned>((ws + 127) / 128), static_cast<unsigned>(hs), static_cast<unsigned>(n));
     if (rounding == LSC_ROUND_HALF_EVEN)
-      quantize_nchw_to_s2d_c3b2_kernel<LSC_ROUND_HALF_EVEN><<<g2, 128, 0, st>>>(
-          x, y, ih, iw, static_cast<int>(ph), static_cast<int>(pw), static_cast<int>(hs), static_cast<int>(ws), scale,
-          inv_s);
+      LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, quantize_nchw_to_s2d_c3b2_kernel<LSC_ROUND_HALF_EVEN>, g2,
+                                    dim3(128), 0, st, x, y, ih, iw, static_cast<int>(ph), static_cast<int>(pw),
+                                    static_cast<int>(hs), static_cast<int>(ws), scale, inv_s));
     else
-      quantize_nchw_to_s2d_c3b2_kernel<LSC_ROUND_HALF_AWAY><<<g2, 128, 0, st>>>(
-          x, y, ih, iw, static_cast<int>(ph), static_cast<int>(pw), static_cast<int>(hs), static_cast<int>(ws), scale,
-          inv_s);
+      LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, quantize_nchw_to_s2d_c3b2_kernel<LSC_ROUND_HALF_AWAY>, g2,
+                                    dim3(128), 0, st, x, y, ih, iw, static_cast<int>(ph), static_cast<int>(pw),
+                                    static_cast<int>(hs), static_cast<int>(ws), scale, inv_s));
     LSC_CUDA_TRY(cudaGetLastError());
     return LSC_SUCCESS;
   }
   if (rounding == LSC_ROUND_HALF_EVEN)
-    quantize_nchw_to_s2d_kernel<LSC_ROUND_HALF_EVEN><<<grid, 128, 0, st>>>(
-        x, y, ic, ih, iw, static_cast<int>(ph), static_cast<int>(pw), static_cast<int>(blk), static_cast<int>(hs),
-        static_cast<int>(ws), static_cast<int>(cp), scale, inv_s);
+    LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, quantize_nchw_to_s2d_kernel<LSC_ROUND_HALF_EVEN>, grid, dim3(128),
+                                  0, st, x, y, ic, ih, iw, static_cast<int>(ph), static_cast<int>(pw),
+                                  static_cast<int>(blk), static_cast<int>(hs), static_cast<int>(ws),
+                                  static_cast<int>(cp), scale, inv_s));
   else
-    quantize_nchw_to_s2d_kernel<LSC_ROUND_HALF_AWAY><<<grid, 128, 0, st>>>(
-        x, y, ic, ih, iw, static_cast<int>(ph), static_cast<int>(pw), static_cast<int>(blk), static_cast<int>(hs),
-        static_cast<int>(ws), static_cast<int>(cp), scale, inv_s);
+    LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, quantize_nchw_to_s2d_kernel<LSC_ROUND_HALF_AWAY>, grid, dim3(128),
+                                  0, st, x, y, ic, ih, iw, static_cast<int>(ph), static_cast<int>(pw),
+                                  static_cast<int>(blk), static_cast<int>(hs), static_cast<int>(ws),
+                                  static_cast<int>(cp), scale, inv_s));
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }
@@ -287,15 +375,20 @@ lsc_status launch_maxpool_i8(const int8_t* x, int8_t* y, int64_t n, int64_t h, i
   if (n == 0 || oh == 0 || per_row == 0) return LSC_SUCCESS;
   if (n > 65535 || oh > 65535 || h * w * c > INT32_MAX || oh * ow * c > INT32_MAX)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "maxpool: batch or image too large");
+  DeviceState* ds = current_device_state();
+  if (!ds) return LSC_ERROR_DEVICE_ERROR;
   const dim3 grid(static_cast<unsigned>((per_row + 127) / 128), static_cast<unsigned>(oh), static_cast<unsigned>(n));
   const int ih = static_cast<int>(h), iw = static_cast<int>(w), ic = static_cast<int>(c);
   const int ioh = static_cast<int>(oh), iow = static_cast<int>(ow);
   if (kh == 3 && kw == 3)
-    maxpool_i8_kernel<3, 3><<<grid, 128, 0, st>>>(x, y, ih, iw, ic, ioh, iow, kh, kw, sh, sw, ph, pw);
+    LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, maxpool_i8_kernel<3, 3>, grid, dim3(128), 0, st, x, y, ih, iw, ic,
+                                  ioh, iow, kh, kw, sh, sw, ph, pw));
   else if (kh == 2 && kw == 2)
-    maxpool_i8_kernel<2, 2><<<grid, 128, 0, st>>>(x, y, ih, iw, ic, ioh, iow, kh, kw, sh, sw, ph, pw);
+    LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, maxpool_i8_kernel<2, 2>, grid, dim3(128), 0, st, x, y, ih, iw, ic,
+                                  ioh, iow, kh, kw, sh, sw, ph, pw));
   else
-    maxpool_i8_kernel<0, 0><<<grid, 128, 0, st>>>(x, y, ih, iw, ic, ioh, iow, kh, kw, sh, sw, ph, pw);
+    LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, maxpool_i8_kernel<0, 0>, grid, dim3(128), 0, st, x, y, ih, iw, ic,
+                                  ioh, iow, kh, kw, sh, sw, ph, pw));
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }
@@ -309,9 +402,11 @@ lsc_status launch_avgpool_i8(const int8_t* x, int64_t n, int64_t hw, int64_t c, 
   const int64_t warps = n * ((c + 31) / 32);
   const int grid = grid_p(warps * 32, ds->sm_count);
   if (rounding == LSC_ROUND_HALF_EVEN)
-    avgpool_i8_kernel<LSC_ROUND_HALF_EVEN><<<grid, 256, 0, st>>>(x, n, hw, c, s_in, s_out, y_i8, y_f32);
+    LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, avgpool_i8_kernel<LSC_ROUND_HALF_EVEN>, dim3(grid), dim3(256), 0,
+                                  st, x, n, hw, c, s_in, s_out, y_i8, y_f32));
   else
-    avgpool_i8_kernel<LSC_ROUND_HALF_AWAY><<<grid, 256, 0, st>>>(x, n, hw, c, s_in, s_out, y_i8, y_f32);
+    LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, avgpool_i8_kernel<LSC_ROUND_HALF_AWAY>, dim3(grid), dim3(256), 0,
+                                  st, x, n, hw, c, s_in, s_out, y_i8, y_f32));
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }

@@ -1,6 +1,7 @@
 // runtime.cu -- error reporting, per-device state, tensor-map encoding and the
 // stateless kernel-level C entry points.
 #include <stdarg.h>
+#include <stdlib.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -65,6 +66,8 @@ DeviceState* device_state(int device) {
     s.cc_minor = prop.minor;
     s.smem_optin = prop.sharedMemPerBlockOptin;
     s.total_memory = prop.totalGlobalMem;
+    const char* ov = getenv("LSC_OVERLAP_LAUNCHES");
+    s.overlap_launches = !(ov && ov[0] == '0');
     void* addr = nullptr;
     e = cudaGetSymbolAddress(&addr, g_device_error_word);
     s.err_word = static_cast<uint32_t*>(addr);

@@ -143,8 +143,14 @@ class ResNet18Int8:
         self.f32_scratch = torch.empty(max(int(np.prod(s)) for s in self.shapes.values()),
                                        dtype=torch.float32, device=device)
         self.ws = torch.zeros(4, dtype=torch.int32, device=device)
+        self._sl = slice(None)  # images of the batch the run methods act on
+        self._ds_stream = None  # side stream for the downsample convs while a graph is captured
 
     # ------------------------------------------------------------------ helpers
+    def _buf(self, name):
+        """The activation buffer `name`, restricted to the images the current pass runs."""
+        return self.buf[name][self._sl]
+
     def _stream(self):
         return self.torch.cuda.current_stream(self.device).cuda_stream
 
@@ -176,14 +182,14 @@ class ResNet18Int8:
         return self.be.compile_operator(opdef, FusionInfo.conv_batch_norm(), ins, [out])
 
     def _run_conv(self, spec, in_name, in_scale, out_scale, residual=None, f32_out=None):
-        ins = [self._t("x", self.buf[in_name], DataType.QInt8, in_scale)]
+        ins = [self._t("x", self._buf(in_name), DataType.QInt8, in_scale)]
         if residual is not None:
             rname, rscale = residual
-            ins.append(self._t("r", self.buf[rname], DataType.QInt8, rscale))
+            ins.append(self._t("r", self._buf(rname), DataType.QInt8, rscale))
         if f32_out is not None:
             outs = [self._t("y", f32_out, DataType.F32)]
         else:
-            outs = [self._t("y", self.buf[spec.name], DataType.QInt8, out_scale)]
+            outs = [self._t("y", self._buf(spec.name), DataType.QInt8, out_scale)]
         self.be.execute(self.ops[spec.name], ins, outs, stream=self._stream())
 
     # ------------------------------------------------------------------ calibration
@@ -251,35 +257,48 @@ class ResNet18Int8:
         self.ops["maxpool"] = self.be.compile_operator(opdef, None, [xin], [self._t("y", self.buf["pool"], DataType.QInt8)])
 
     def _run_pool(self):
-        self.be.execute(self.ops["maxpool"], [self._t("x", self.buf["conv1"], DataType.QInt8)],
-                        [self._t("y", self.buf["pool"], DataType.QInt8)], stream=self._stream())
+        self.be.execute(self.ops["maxpool"], [self._t("x", self._buf("conv1"), DataType.QInt8)],
+                        [self._t("y", self._buf("pool"), DataType.QInt8)], stream=self._stream())
 
     def _run_gap(self):
-        self.be.execute(self.ops["gap"], [self._t("x", self.buf[self.last], DataType.QInt8, self.scales[self.last])],
-                        [self._t("y", self.buf["pooled"], DataType.QInt8, self.scales["pooled"])],
+        self.be.execute(self.ops["gap"], [self._t("x", self._buf(self.last), DataType.QInt8, self.scales[self.last])],
+                        [self._t("y", self._buf("pooled"), DataType.QInt8, self.scales["pooled"])],
                         stream=self._stream())
 
     def _run_fc(self):
-        pin = Tensor("p", [self.batch, 512], DataType.QInt8, self.buf["pooled"],
-                     quantization=Quantization([self.scales["pooled"]]))
-        self.be.execute(self.ops["fc"], [pin], [Tensor("logits", list(self.logits.shape), DataType.F32, self.logits)],
+        pooled, logits = self._buf("pooled"), self.logits[self._sl]
+        pin = Tensor("p", list(pooled.shape), DataType.QInt8, pooled, quantization=Quantization([self.scales["pooled"]]))
+        self.be.execute(self.ops["fc"], [pin], [Tensor("logits", list(logits.shape), DataType.F32, logits)],
                         stream=self._stream())
 
     # ------------------------------------------------------------------ inference
     def forward(self, x_f32):
         """Runs the calibrated network on an f32 NCHW device batch; returns the logits buffer."""
+        x_f32 = x_f32[self._sl]
         xt = Tensor("x", list(x_f32.shape), DataType.F32, x_f32, layout=StorageLayout.NCHW)
-        qin = Tensor("xq", list(self.buf["x_q"].shape), DataType.QInt8, self.buf["x_q"],
+        x_q = self._buf("x_q")
+        qin = Tensor("xq", list(x_q.shape), DataType.QInt8, x_q,
                      layout=StorageLayout.NHWC, quantization=Quantization([self.scales["input"]]))
         self.be.execute(self.ops["quant_in"], [xt], [qin], stream=self._stream())
         sc = self.scales
         self._run_conv(self.stem, "x_q", sc["input"], sc["conv1"])
         self._run_pool()
         prev = "pool"
+        torch = self.torch
         for c1, c2, ds in self.blocks:
+            side = self._ds_stream if ds is not None else None
+            if side is not None:
+                # the downsample reads the block input as conv1 does: run it beside conv1
+                cur = torch.cuda.current_stream(self.device)
+                side.wait_stream(cur)
+                with torch.cuda.stream(side):
+                    self._run_conv(ds, prev, sc[prev], sc[ds.name])
             self._run_conv(c1, prev, sc[prev], sc[c1.name])
             if ds is not None:
-                self._run_conv(ds, prev, sc[prev], sc[ds.name])
+                if side is not None:
+                    cur.wait_stream(side)
+                else:
+                    self._run_conv(ds, prev, sc[prev], sc[ds.name])
                 res = (ds.name, sc[ds.name])
             else:
                 res = (prev, sc[prev])
@@ -293,13 +312,46 @@ class ResNet18Int8:
         """Kernels per forward: input quantize + 20 convs + maxpool + avgpool + FC."""
         return 1 + len(self.convs) + 1 + 1 + 1
 
-    def capture(self, x_static):
-        """Records ``forward(x_static)`` as a CUDA graph (call after ``calibrate``)."""
+    def capture(self, x_static, branches: int = 1, concurrent_downsample: bool = False):
+        """Records ``forward(x_static)`` as a CUDA graph (call after ``calibrate``).
+
+        With ``branches`` > 1 the batch is cut into that many equal groups of images, each run
+        through the whole network on its own stream inside the graph (forked from and joined
+        back to the capturing stream).  Every image's computation is independent of the others
+        once the activation scales are fixed, so the logits are the same; the groups' kernels
+        overlap, which fills the SMs that one small batch's kernels leave idle.  With
+        ``concurrent_downsample`` each stage's 1x1 downsample conv runs on a side stream beside
+        the block's first conv (both read the block input; the second conv joins them)."""
         torch = self.torch
-        self.forward(x_static)  # warm: every kernel variant initialised before capture
-        torch.cuda.synchronize(self.device)
+        if branches < 1 or self.batch % branches:
+            raise ValueError(f"batch {self.batch} does not split into {branches} branches")
+        per = self.batch // branches
+        slices = [slice(k * per, (k + 1) * per) for k in range(branches)]
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self.forward(x_static)
+        ds_streams = [torch.cuda.Stream(self.device) if concurrent_downsample else None for _ in slices]
+        try:
+            # warm: every kernel variant (tile widths follow the group size) initialised first
+            for sl in slices:
+                self._sl = sl
+                self.forward(x_static)
+            self._sl = slice(None)
+            torch.cuda.synchronize(self.device)
+            if branches == 1:
+                with torch.cuda.graph(g):
+                    self._ds_stream = ds_streams[0]
+                    self.forward(x_static)
+            else:
+                side = [torch.cuda.Stream(self.device) for _ in slices]
+                with torch.cuda.graph(g):
+                    main = torch.cuda.current_stream(self.device)
+                    for sl, st, dst in zip(slices, side, ds_streams):
+                        st.wait_stream(main)
+                        with torch.cuda.stream(st):
+                            self._sl, self._ds_stream = sl, dst
+                            self.forward(x_static)
+                    for st in side:
+                        main.wait_stream(st)
+        finally:
+            self._sl, self._ds_stream = slice(None), None
         self.graph = g
         return g

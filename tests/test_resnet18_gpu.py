@@ -91,7 +91,11 @@ def test_resnet18_int8_bit_exact(be, cuda, rounding):
     assert not np.array_equal(logits[0], logits[1])
 
 
-def test_resnet18_graph_replay_matches_eager(be, cuda):
+@pytest.mark.parametrize("branches,ds_side", [(1, False), (2, False), (4, True), (1, True)])
+def test_resnet18_graph_replay_matches_eager(be, cuda, branches, ds_side):
+    """The captured graph (one chain, or the batch cut into concurrent image groups, with or
+    without the downsample convs on a side stream) gives the eager forward pass's logits bit
+    for bit, on an input other than the captured one."""
     import torch
     from lightship_b200.resnet18 import ResNet18Int8
     batch = 4
@@ -101,7 +105,7 @@ def test_resnet18_graph_replay_matches_eager(be, cuda):
     model.calibrate(x)
     eager = model.forward(x).clone()
     static = x.clone()
-    g = model.capture(static)
+    g = model.capture(static, branches=branches, concurrent_downsample=ds_side)
     x2 = torch.from_numpy(rng.normal(size=(batch, 3, 224, 224)).astype(np.float32)).to(cuda)
     static.copy_(x2)
     g.replay()
