@@ -88,11 +88,14 @@ typedef enum lsc_op_type {
   LSC_OP_QUANTIZE = 7,   /* quantize_tensor (quantization/helpers.rs:11-50) */
   LSC_OP_DEQUANTIZE = 8, /* dequantize_tensor (quantization/helpers.rs:53-94) */
   LSC_OP_QGEMM = 9,      /* quantized_gemm_int8 + requant/dequant (cpu/quantized_ops.rs:13-48) */
-  LSC_OP_MAXPOOL2D = 10, /* MaxPool2d on int8 NHWC (operator/pooling.rs:383-455) */
-  LSC_OP_GLOBAL_AVGPOOL2D = 11, /* GlobalAvgPool2d on int8 NHWC (operator/pooling.rs:457-530) */
+  LSC_OP_MAXPOOL2D = 10, /* MaxPool2d on int8 NHWC or f32 NCHW (operator/pooling.rs:383-455) */
+  LSC_OP_GLOBAL_AVGPOOL2D = 11, /* GlobalAvgPool2d on int8 NHWC ([N, C] out) or f32 NCHW
+                                   ([N, C, 1, 1] out, operator/pooling.rs:457-530) */
   LSC_OP_GELU = 12,      /* Gelu::compute, tanh form (operator/gelu.rs:77-103) */
   LSC_OP_LAYERNORM = 13, /* LayerNorm over the last axis (operator/layernorm.rs:140-205) */
-  LSC_OP_SOFTMAX = 14    /* Softmax over the last axis (operator/softmax.rs:106-169) */
+  LSC_OP_SOFTMAX = 14,   /* Softmax over the last axis (operator/softmax.rs:106-169) */
+  LSC_OP_ADD = 15        /* elementwise f32 Add (ir/operator.rs OperatorType::Add), with
+                            FusionType::AddReLU (ir/fusion.rs:20) as activation ReLU */
 } lsc_op_type;
 
 /* FusionType (ir/fusion.rs:8-23); LSC_FUSION_NONE = no FusionInfo */
@@ -362,6 +365,42 @@ lsc_status lsc_transpose_heads_f16(const void* x, void* y, int64_t x_batch_strid
  * yields NaN outputs. */
 lsc_status lsc_attention_f16(const void* qkv, int64_t batch, int64_t seq, int64_t heads, float alpha,
                              float* out_f32, int8_t* out_i8, float s_out, int32_t rounding, lsc_stream stream);
+
+/* ---- models and sessions (ONNX; FP32 NCHW graphs) ----------------------------------------
+ * An ONNX model loaded from memory (LightShipEngine_LoadModelFromMemory, lightship.h:186-198;
+ * OnnxLoader, model/onnx.rs).  Node attributes (strides, pads, dilations, group, epsilon,
+ * kernel_shape, transB, axis) are read; the reference's parser skips them (onnx.rs:613).
+ * Loading runs the graph optimizer's fusion pass (FusionPass, ir/optimizer.rs:505-890, with
+ * its single-consumer rule): Conv->BatchNormalization->Relu|Clip(0,6) becomes one Conv with
+ * FusionType::ConvBatchNorm and the activation, Conv->Relu ConvReLU, Add->Relu AddReLU,
+ * BatchNormalization->Relu BatchNormReLU.  Supported ONNX operators: Conv, BatchNormalization,
+ * Relu, Clip(0, 6), Add, MaxPool, GlobalAveragePool, Flatten, Reshape (constant shape), Gemm /
+ * MatMul (constant right operand -> FullyConnected), Softmax, LayerNormalization, Gelu; any
+ * other operator fails the load with LSC_ERROR_UNSUPPORTED_OPERATOR. */
+typedef struct lsc_model lsc_model;
+typedef struct lsc_session lsc_session;
+lsc_status lsc_model_load_onnx(const uint8_t* data, uint64_t size, lsc_model** out);
+void lsc_model_destroy(lsc_model* model);                  /* LightShipModel_Destroy */
+/* LightShipModel_GetMetadata (lightship.h:208-214): counts after fusion */
+lsc_status lsc_model_info(const lsc_model* model, uint32_t* n_inputs, uint32_t* n_outputs,
+                          uint32_t* n_nodes);
+/* LightShipModel_GetInputInfo / GetOutputInfo (lightship.h:226-258); shape needs
+ * LSC_MAX_DIMS entries; -1 marks a symbolic dimension */
+lsc_status lsc_model_io(const lsc_model* model, int32_t is_output, uint32_t index, const char** name,
+                        int32_t* dtype, int64_t* shape, uint32_t* ndim);
+/* The Backend operator node `index` of the fused graph lowers to (op_type -1: a view such as
+ * Flatten, no kernel), its name and its ONNX operator. */
+lsc_status lsc_model_node(const lsc_model* model, uint32_t index, lsc_op_desc* desc,
+                          const char** name, const char** onnx_op);
+/* LightShipEngine_CreateSession (lightship.h:283-297): compiles every node on `backend` (weights
+ * prepacked once) and takes one arena buffer per intermediate tensor; the model's inputs need
+ * static shapes.  The session keeps `model` and `backend` in use until it is destroyed. */
+lsc_status lsc_session_create(lsc_backend* backend, const lsc_model* model, lsc_session** out);
+void lsc_session_destroy(lsc_session* session); /* LightShipSession_Destroy */
+/* LightShipSession_Run (lightship.h:319-331): inputs and outputs in the model's order, f32,
+ * host or device memory; runs every node on `stream` (host outputs are complete on return). */
+lsc_status lsc_session_run(lsc_session* session, const lsc_tensor* inputs, uint32_t n_inputs,
+                           lsc_tensor* outputs, uint32_t n_outputs, lsc_stream stream);
 
 #ifdef __cplusplus
 }

@@ -123,6 +123,15 @@ SIGNATURES = {
                                   I64, I64, I64, P]),
     "lsc_transpose_heads_f16": (ST, [P, P, I64, I64, I64, I64, I64, I64, I64, I64, P]),
     "lsc_attention_f16": (ST, [P, I64, I64, I64, F32, P, P, F32, I32, P]),
+    "lsc_model_load_onnx": (ST, [C.c_char_p, C.c_uint64, C.POINTER(P)]),
+    "lsc_model_destroy": (None, [P]),
+    "lsc_model_info": (ST, [P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
+    "lsc_model_io": (ST, [P, I32, C.c_uint32, C.POINTER(C.c_char_p), C.POINTER(I32), C.POINTER(I64),
+                          C.POINTER(C.c_uint32)]),
+    "lsc_model_node": (ST, [P, C.c_uint32, C.POINTER(lsc_op_desc), C.POINTER(C.c_char_p), C.POINTER(C.c_char_p)]),
+    "lsc_session_create": (ST, [P, P, C.POINTER(P)]),
+    "lsc_session_destroy": (None, [P]),
+    "lsc_session_run": (ST, [P, C.POINTER(lsc_tensor), C.c_uint32, C.POINTER(lsc_tensor), C.c_uint32, P]),
 }
 
 _lib = None

@@ -72,6 +72,7 @@ class OperatorType(enum.IntEnum):
     GELU = 12
     LayerNorm = 13
     Softmax = 14
+    Add = 15
 
 
 class FusionType(enum.IntEnum):
@@ -339,6 +340,91 @@ class CudaBackend:
         return {"current": cur.value, "peak": peak.value, "capacity": cap.value}
 
 
+class OnnxModel:
+    """An ONNX model loaded from memory and fused (LightShipEngine_LoadModelFromMemory,
+    c-api/include/lightship.h:186-198): attributes read, Conv->BN->Relu and Add->Relu fused."""
+
+    def __init__(self, data: bytes):
+        h = C.c_void_p()
+        check(lib().lsc_model_load_onnx(data, len(data), C.byref(h)))
+        self._h = h
+
+    @staticmethod
+    def from_file(path: str) -> "OnnxModel":
+        with open(path, "rb") as f:
+            return OnnxModel(f.read())
+
+    def close(self):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            lib().lsc_model_destroy(h)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _counts(self):
+        ni, no, nn = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        check(lib().lsc_model_info(self._h, C.byref(ni), C.byref(no), C.byref(nn)))
+        return ni.value, no.value, nn.value
+
+    def _io(self, is_output: int, i: int):
+        name, dt, nd = C.c_char_p(), C.c_int32(), C.c_uint32()
+        shape = (C.c_int64 * _lib.MAX_DIMS)()
+        check(lib().lsc_model_io(self._h, is_output, i, C.byref(name), C.byref(dt), shape, C.byref(nd)))
+        return name.value.decode(), DataType(dt.value), [int(shape[k]) for k in range(nd.value)]
+
+    @property
+    def inputs(self):
+        return [self._io(0, i) for i in range(self._counts()[0])]
+
+    @property
+    def outputs(self):
+        return [self._io(1, i) for i in range(self._counts()[1])]
+
+    def nodes(self):
+        """(name, ONNX operator, lsc_op_desc) of every node of the fused graph."""
+        out = []
+        for i in range(self._counts()[2]):
+            d, name, op = _lib.lsc_op_desc(), C.c_char_p(), C.c_char_p()
+            check(lib().lsc_model_node(self._h, i, C.byref(d), C.byref(name), C.byref(op)))
+            out.append((name.value.decode(), op.value.decode(), d))
+        return out
+
+
+class Session:
+    """An inference session of an OnnxModel on a CudaBackend (LightShipEngine_CreateSession /
+    LightShipSession_Run, lightship.h:283-331)."""
+
+    def __init__(self, backend: CudaBackend, model: OnnxModel):
+        h = C.c_void_p()
+        check(lib().lsc_session_create(backend._h, model._h, C.byref(h)))
+        self._h = h
+        self._backend, self._model = backend, model  # both stay alive with the session
+
+    def close(self):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            lib().lsc_session_destroy(h)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def run(self, inputs: Sequence[Tensor], outputs: Sequence[Tensor], stream=None) -> None:
+        keep: list = []
+        cin = (_lib.lsc_tensor * max(1, len(inputs)))(*[t._to_c(keep) for t in inputs])
+        cout = (_lib.lsc_tensor * max(1, len(outputs)))(*[t._to_c(keep) for t in outputs])
+        st = C.c_void_p(stream) if isinstance(stream, int) else stream
+        check(lib().lsc_session_run(self._h, cin, len(inputs), cout, len(outputs), st))
+        for t, c in zip(outputs, cout):
+            t.shape = [int(c.shape[i]) for i in range(c.ndim)]
+
+
 __all__ = ["DataType", "StorageLayout", "OperatorType", "FusionType", "FusionInfo", "Activation",
            "Rounding", "OperatorDef", "Quantization", "Tensor", "GpuBackendConfig", "MemoryBlock",
-           "CompiledOperator", "CudaBackend", "LightShipError"]
+           "CompiledOperator", "CudaBackend", "LightShipError", "OnnxModel", "Session"]

@@ -437,10 +437,14 @@ lsc_status execute_conv(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_te
 // ------------------------------------------------------------------------------ pooling (INT8 NHWC)
 lsc_status compile_pool(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, bool global) {
   if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Missing input or output");
-  if (!is_int8(in[0].dtype))
-    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "pooling on the CUDA backend takes int8 NHWC input");
+  const bool f32 = in[0].dtype == LSC_DTYPE_F32;
+  if (!is_int8(in[0].dtype) && !f32)
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "pooling on the CUDA backend takes int8 NHWC or f32 NCHW input");
   const lsc_op_desc& d = op->desc;
-  op->kind = global ? OpKind::kAvgPoolI8 : OpKind::kMaxPoolI8;
+  if (f32)
+    op->kind = global ? OpKind::kAvgPoolF32 : OpKind::kMaxPoolF32;
+  else
+    op->kind = global ? OpKind::kAvgPoolI8 : OpKind::kMaxPoolI8;
   op->kh = d.kernel_h > 0 ? d.kernel_h : 1;
   op->kw = d.kernel_w > 0 ? d.kernel_w : 1;
   if (!global && (d.pad_h < 0 || d.pad_w < 0 || d.pad_h >= op->kh || d.pad_w >= op->kw))
@@ -457,6 +461,29 @@ lsc_status execute_pool(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_te
                         int n_out, Staging& s) {
   if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Missing input or output");
   const lsc_tensor& x = in[0];
+  if (op->kind == OpKind::kMaxPoolF32 || op->kind == OpKind::kAvgPoolF32) {
+    // f32 NCHW (Pool2d, operator/pooling.rs): [N, C, OH, OW] max, [N, C, 1, 1] global average
+    if (x.dtype != LSC_DTYPE_F32 || x.ndim != 4)
+      return set_error(LSC_ERROR_INVALID_ARGUMENT, "pooling takes a 4D f32 NCHW input here");
+    const int64_t n = x.shape[0], c = x.shape[1], h = x.shape[2], w = x.shape[3];
+    const void* xd = nullptr;
+    void* yd = nullptr;
+    lsc_status st = s.input(x, n * c * h * w * 4, &xd);
+    if (st) return st;
+    if (out[0].dtype != LSC_DTYPE_F32) return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "pooling output must be f32");
+    if (op->kind == OpKind::kAvgPoolF32) {
+      if ((st = s.output(out[0], n * c * 4, &yd))) return st;
+      set_shape(out[0], {n, c, 1, 1});
+      return launch_avgpool_f32(static_cast<const float*>(xd), static_cast<float*>(yd), n, c, h * w, s.st);
+    }
+    const int64_t oh = (h + 2 * op->ph - op->kh) / op->sh + 1, ow = (w + 2 * op->pw - op->kw) / op->sw + 1;
+    if (oh <= 0 || ow <= 0) return set_error(LSC_ERROR_SHAPE_MISMATCH, "MaxPool2d: window larger than the input");
+    if ((st = s.output(out[0], n * c * oh * ow * 4, &yd))) return st;
+    set_shape(out[0], {n, c, oh, ow});
+    return launch_maxpool_f32(static_cast<const float*>(xd), static_cast<float*>(yd), n, c, h, w, oh, ow,
+                              static_cast<int>(op->kh), static_cast<int>(op->kw), op->sh, op->sw, op->ph, op->pw,
+                              s.st);
+  }
   if (!is_int8(x.dtype) || x.ndim != 4)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "pooling takes a 4D int8 NHWC input");
   const int64_t n = x.shape[0], h = x.shape[1], w = x.shape[2], c = x.shape[3];
@@ -673,6 +700,42 @@ lsc_status compile_activation(lsc_op* op, const lsc_tensor* in, int n_in, int n_
   op->kind = OpKind::kActF32;
   op->act = act;
   return LSC_SUCCESS;
+}
+
+// Add (OperatorType::Add, backend/cpu.rs:468-517): y = a + b elementwise on equal shapes,
+// then the activation (FusionType::AddReLU, or the descriptor's activation).
+lsc_status compile_add(lsc_op* op, const lsc_tensor* in, int n_in, int n_out) {
+  if (n_in < 2 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Add requires 2 inputs and 1 output");
+  if (in[0].dtype != LSC_DTYPE_F32 || in[1].dtype != LSC_DTYPE_F32)
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "Add requires F32 inputs");
+  op->kind = OpKind::kAddF32;
+  op->act = op->desc.fusion == LSC_FUSION_ADD_RELU ? LSC_ACT_RELU : op->desc.activation;
+  if (op->act < LSC_ACT_NONE || op->act > LSC_ACT_GELU)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "Add: bad activation %d", op->act);
+  return LSC_SUCCESS;
+}
+
+lsc_status execute_add(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out, Staging& s) {
+  if (n_in < 2 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Add requires 2 inputs and 1 output");
+  const lsc_tensor& a = in[0];
+  const lsc_tensor& b = in[1];
+  if (a.dtype != LSC_DTYPE_F32 || b.dtype != LSC_DTYPE_F32 || out[0].dtype != LSC_DTYPE_F32)
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "Add requires F32 tensors");
+  const int64_t total = numel(a);
+  if (total < 0 || numel(b) != total)
+    return set_error(LSC_ERROR_SHAPE_MISMATCH, "Add: inputs hold %lld and %lld elements", (long long)total,
+                     (long long)numel(b));
+  const void* ad = nullptr;
+  const void* bd = nullptr;
+  void* yd = nullptr;
+  lsc_status st;
+  if ((st = s.input(a, total * 4, &ad)) || (st = s.input(b, total * 4, &bd)) ||
+      (st = s.output(out[0], total * 4, &yd)))
+    return st;
+  out[0].ndim = a.ndim;
+  for (int i = 0; i < a.ndim; ++i) out[0].shape[i] = a.shape[i];
+  return launch_add_f32(static_cast<const float*>(ad), static_cast<const float*>(bd), static_cast<float*>(yd), total,
+                        op->act, s.st);
 }
 
 lsc_status execute_activation(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out,

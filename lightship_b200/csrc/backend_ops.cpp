@@ -19,7 +19,7 @@ uint32_t supported_ops_mask() {
          (1u << LSC_OP_DEQUANTIZE) | (1u << LSC_OP_CONV2D) | (1u << LSC_OP_MATMUL) |
          (1u << LSC_OP_BATCHNORM) | (1u << LSC_OP_RELU) | (1u << LSC_OP_RELU6) |
          (1u << LSC_OP_SILU) | (1u << LSC_OP_MAXPOOL2D) | (1u << LSC_OP_GLOBAL_AVGPOOL2D) |
-         (1u << LSC_OP_GELU) | (1u << LSC_OP_LAYERNORM) | (1u << LSC_OP_SOFTMAX);
+         (1u << LSC_OP_GELU) | (1u << LSC_OP_LAYERNORM) | (1u << LSC_OP_SOFTMAX) | (1u << LSC_OP_ADD);
 }
 
 namespace {
@@ -357,6 +357,7 @@ lsc_status compile_op(lsc_backend* be, lsc_op* op, const lsc_tensor* in, int n_i
     case LSC_OP_GELU: return compile_activation(op, in, n_in, n_out, LSC_ACT_GELU);
     case LSC_OP_LAYERNORM: return compile_layernorm(op, in, n_in, out, n_out);
     case LSC_OP_SOFTMAX: return compile_softmax(op, in, n_in, n_out);
+    case LSC_OP_ADD: return compile_add(op, in, n_in, n_out);
     case LSC_OP_QUANTIZE: {
       if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Quantize needs 1 input and 1 output");
       if (in[0].dtype != LSC_DTYPE_F32)
@@ -418,7 +419,10 @@ lsc_status execute_op(lsc_backend* be, const lsc_op* op, const lsc_tensor* in, i
     case OpKind::kLayerNorm:
     case OpKind::kSoftmax: return execute_rownorm(op, in, n_in, out, n_out, s);
     case OpKind::kMaxPoolI8:
-    case OpKind::kAvgPoolI8: return execute_pool(op, in, n_in, out, n_out, s);
+    case OpKind::kAvgPoolI8:
+    case OpKind::kMaxPoolF32:
+    case OpKind::kAvgPoolF32: return execute_pool(op, in, n_in, out, n_out, s);
+    case OpKind::kAddF32: return execute_add(op, in, n_in, out, n_out, s);
     default: break;
   }
   return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "compiled operator kind %d not executable", static_cast<int>(op->kind));

@@ -37,6 +37,9 @@ enum class OpKind {
   kActF32,         // ReLU / ReLU6 / SiLU
   kMaxPoolI8,      // MaxPool2d on int8 NHWC
   kAvgPoolI8,      // GlobalAvgPool2d on int8 NHWC
+  kMaxPoolF32,     // MaxPool2d on f32 NCHW
+  kAvgPoolF32,     // GlobalAvgPool2d on f32 NCHW
+  kAddF32,         // elementwise Add (+ ReLU)
 };
 
 struct lsc_op {
@@ -140,6 +143,8 @@ lsc_status compile_pool(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, b
 lsc_status execute_pool(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out,
                         Staging& s);
 lsc_status compile_activation(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, int act);
+lsc_status compile_add(lsc_op* op, const lsc_tensor* in, int n_in, int n_out);
+lsc_status execute_add(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out, Staging& s);
 lsc_status compile_layernorm(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_tensor* out, int n_out);
 lsc_status compile_softmax(lsc_op* op, const lsc_tensor* in, int n_in, int n_out);
 lsc_status execute_rownorm(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out,
