@@ -870,6 +870,333 @@ lsc_status launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const
   }
 }
 
+// ------------------------------------------------------------------------------------------
+// Convolution with the operands swapped, for layers of exactly 128 output channels: the
+// filter is the 128-row A operand (TMEM lanes = output channels) and 256 output pixels, two
+// 128-pixel im2col loads per channel block, are the N = 256 B operand (TMEM columns =
+// pixels).  A K = 32 int8 MMA costs about the same at N = 128 as at N = 256 on B200, so
+// putting the pixels on the wide side does up to twice the work per instruction of the
+// 128 x 128 tiles the plain kernel uses for these layers.  The epilogue works per output
+// channel (one per thread); the four warps sharing a pixel range pass each 16-pixel x
+// 128-channel int8 block through a 2 KB shared-memory stage so that global accesses are
+// 16-byte pixel-row segments.  Same arithmetic, same bits.
+struct SwapCfg {
+  static constexpr int BM = 128;   // output channels (A rows)
+  static constexpr int BP = 256;   // output pixels per tile (B rows)
+  static constexpr int BK = 128;
+  static constexpr int STAGES = 4;
+  static constexpr int W_BYTES = BM * BK;
+  static constexpr int X_BYTES = BP * BK;
+  static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
+  static constexpr int EPI_WARPS = 16;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int TMEM_COLS = 2 * BP;  // double-buffered accumulator
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int OUT_STAGE_BYTES = 4 * 2048;  // per part: 16 pixels x 128 channels of int8
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + OUT_STAGE_BYTES;
+  static constexpr uint32_t IDESC = idesc_i8(BM, BP);
+  static_assert(SMEM_BYTES <= kSmemLimit, "shared memory budget");
+  static_assert((2 * STAGES + 5) * 8 + 8 <= BAR_BYTES, "barrier area");
+};
+
+template <int ACB>
+__device__ __forceinline__ uint64_t swap_x_desc(uint32_t x0, int kk) {
+  if constexpr (ACB == 128) {
+    return smem_desc_sw128_kmajor(x0 + kk * 32);
+  } else {
+    static_assert(ACB == 64, "swapped convolutions take 64- or 128-byte channel blocks");
+    return smem_desc_sw64_kmajor(x0 + (kk >> 1) * (SwapCfg::BP * 64) + (kk & 1) * 32);
+  }
+}
+
+template <int ACT, int ACB, int RND>
+__global__ void __launch_bounds__(SwapCfg::THREADS, 1)
+    contraction_i8_swap_kernel(const __grid_constant__ CUtensorMap tmX,
+                               const __grid_constant__ CUtensorMap tmW, const I8Params p) {
+  using S = SwapCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sW = smem;                             // [stages][128 rows][128 B]
+  uint8_t* sX = smem + S::STAGES * S::W_BYTES;    // [stages][chunks][256 rows][ACB]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::STAGES * S::STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S::STAGES;
+  uint64_t* tfull = bars + 2 * S::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int kblocks = (p.k + S::BK - 1) / S::BK;
+  const int num_tiles = (p.m + S::BP - 1) / S::BP;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S::STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], S::EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmW);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  griddep_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- TMA producer
+      uint32_t stage = 0, phase = 0;
+      int issued = 0;
+      bool ok = true;
+      griddep_wait();  // the activations are the previous kernel's output
+      constexpr int SUB = 128 / ACB;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        // filter-origin coordinates of each 128-pixel half's first pixel
+        int32_t cw[2], chh[2], cn[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int m0 = tile * S::BP + h * 128;
+          cn[h] = m0 / p.ohw;
+          const int rem = m0 - cn[h] * p.ohw;
+          const int oy = rem / p.ow;
+          const int ox = rem - oy * p.ow;
+          cw[h] = ox * p.sw - p.pw;
+          chh[h] = oy * p.sh - p.ph;
+        }
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
+          tma_load_2d(&tmW, &full[stage], sW + stage * S::W_BYTES, kb * S::BK, 0);
+          uint8_t* x_dst = sX + stage * S::X_BYTES;
+#pragma unroll
+          for (int i = 0; i < SUB; ++i) {
+            int j = kb * SUB + i;            // channel chunk index in (kh, kw, c) order
+            if (j >= p.total_chunks) j = 0;  // past the filter: weights are zero there
+            const int tap = j / p.chunks_per_tap;
+            const int c0 = (j - tap * p.chunks_per_tap) * ACB;
+            const int ky = tap / p.kw;
+            const int kx = tap - ky * p.kw;
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              tma_load_im2col_4d(&tmX, &full[stage], x_dst + i * (S::BP * ACB) + h * (128 * ACB), c0, cw[h], chh[h],
+                                 cn[h], static_cast<uint16_t>(kx * p.dw), static_cast<uint16_t>(ky * p.dh));
+          }
+          ++issued;
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        volatile uint32_t no_abort = 0;
+        const int outstanding = issued < S::STAGES ? issued : S::STAGES;
+        for (int i = 1; i <= outstanding; ++i) {
+          const int idx = issued - i;
+          mbar_wait(&full[idx % S::STAGES], static_cast<uint32_t>((idx / S::STAGES) & 1), &no_abort, p.err);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- MMA issuer
+      uint32_t stage = 0, phase = 0;
+      int local = 0;
+      bool ok = true, any_mma = false;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        if (!mbar_wait(&tempty[buf], static_cast<uint32_t>((local >> 1) & 1) ^ 1u, abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * S::BP);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t w0 = smem_u32(sW + stage * S::W_BYTES);
+          const uint32_t x0 = smem_u32(sX + stage * S::X_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < S::BK / 32; ++kk)
+            mma_i8(d_tmem, smem_desc_sw128_kmajor(w0 + kk * 32), swap_x_desc<ACB>(x0, kk), S::IDESC,
+                   (kb | kk) != 0 ? 1u : 0u);
+          any_mma = true;
+          mma_commit(&empty[stage]);
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) mma_commit(&tfull[buf]);
+      }
+      if (!ok && any_mma) {
+        volatile uint32_t no_abort = 0;
+        mma_commit(drain);
+        mbar_wait(drain, 0u, &no_abort, p.err);
+      }
+    }
+  } else {
+    // --------------------------------------------------------------- epilogue (one channel)
+    const int epi = warp - 2;
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may read
+    const int part = epi >> 2;     // which 64 of the tile's 256 pixels
+    const int ch = quarter * 32 + lane;
+    const int t = (epi & 3) * 32 + lane;  // thread index within the part (0..127)
+    uint8_t* stage = smem + S::STAGES * S::STAGE_BYTES + S::BAR_BYTES + part * 2048;
+    const uint32_t bar_id = 1u + static_cast<uint32_t>(part);
+    const float scale = __ldg(p.scale + ch);  // p.n == 128: every channel exists
+    const int32_t bias = p.bias ? __ldg(p.bias + ch) : 0;
+    griddep_wait();  // outputs and the residual belong to earlier kernels until they finish
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      if (!mbar_wait(&tfull[buf], static_cast<uint32_t>((local >> 1) & 1), abort_flag, p.err)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        const int col = part * 64 + c * 16;
+        const int pix0 = tile * S::BP + col;
+        uint32_t r[16];
+        tmem_ld_cols(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                         static_cast<uint32_t>(buf * S::BP + col), r);
+        tmem_ld_wait();
+        if (c == 3) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+        const int srow = t >> 3, scol = (t & 7) * 16;  // this thread's 16 bytes of a pixel row
+        const bool srow_ok = pix0 + srow < p.m;
+        int32_t acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = static_cast<int32_t>(r[j] + static_cast<uint32_t>(bias));
+        if (p.out_i32) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (pix0 + j < p.m) p.out_i32[static_cast<int64_t>(pix0 + j) * p.ldo + ch] = acc[j];
+        }
+        if (!p.out_f32 && !p.out_i8) continue;
+        float y[16];
+        const uint64_t sc2 = f2pack(scale, scale);
+#pragma unroll
+        for (int j = 0; j < 16; j += 2)
+          f2unpack(f2mul(f2pack(__int2float_rn(acc[j]), __int2float_rn(acc[j + 1])), sc2), y[j], y[j + 1]);
+        if (p.residual) {
+          // pixel rows in, channel columns out: 16-byte loads, then each lane its 16 bytes
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (srow_ok) v = __ldg(reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(pix0 + srow) * p.ldo + scol));
+          *reinterpret_cast<uint4*>(stage + srow * 128 + scol) = v;
+          named_bar_sync(bar_id, 128);
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            y[j] = __fadd_rn(y[j], __fmul_rn(__int2float_rn(static_cast<int32_t>(static_cast<int8_t>(stage[j * 128 + ch]))),
+                                             p.res_scale));
+          named_bar_sync(bar_id, 128);
+        }
+        // a ReLU feeding only the int8 output is applied inside the requantization's clamp
+        const bool relu_folded = ACT == LSC_ACT_RELU && !p.out_f32 && p.inv_s_out > 0.0f;
+        if (!relu_folded) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) y[j] = apply_act<ACT>(y[j]);
+        }
+        if (p.out_f32) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (pix0 + j < p.m) p.out_f32[static_cast<int64_t>(pix0 + j) * p.ldo + ch] = y[j];
+        }
+        if (p.out_i8) {
+          uint32_t pk[4];  // pk[q]: pixels 4q .. 4q+3 of this channel, one byte each
+          requant_pack_rnd<16, RND>(y, p.s_out, p.inv_s_out, relu_folded, pk);
+          uint32_t* st32 = reinterpret_cast<uint32_t*>(stage);  // [pixel quad][channel]
+#pragma unroll
+          for (int q = 0; q < 4; ++q) st32[q * 128 + ch] = pk[q];
+          named_bar_sync(bar_id, 128);
+          // byte (srow & 3) of the 16 words of channels scol .. scol+15 in quad srow / 4
+          const uint32_t* row = st32 + (srow >> 2) * 128 + scol;
+          const uint32_t sel = static_cast<uint32_t>(srow & 3);
+          uint32_t o[4];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const uint32_t b0 = row[4 * w + 0], b1 = row[4 * w + 1], b2 = row[4 * w + 2], b3 = row[4 * w + 3];
+            const uint32_t lo = __byte_perm(b0, b1, sel | ((sel + 4) << 4));
+            const uint32_t hi = __byte_perm(b2, b3, sel | ((sel + 4) << 4));
+            o[w] = __byte_perm(lo, hi, 0x5410);
+          }
+          if (srow_ok)
+            *reinterpret_cast<uint4*>(p.out_i8 + static_cast<int64_t>(pix0 + srow) * p.ldo + scol) =
+                make_uint4(o[0], o[1], o[2], o[3]);
+          named_bar_sync(bar_id, 128);
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+template <int ACT, int ACB, int RND>
+lsc_status launch_swap_cfg(const CUtensorMap& tx, const CUtensorMap& tw, const I8Params& p, const DeviceState& ds,
+                           cudaStream_t stream) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(contraction_i8_swap_kernel<ACT, ACB, RND>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, SwapCfg::SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(contraction_i8_swap)");
+  const int tiles = (p.m + SwapCfg::BP - 1) / SwapCfg::BP;
+  const int grid = tiles < ds.sm_count ? tiles : ds.sm_count;
+  LSC_CUDA_TRY(launch_dependent(ds.overlap_launches, contraction_i8_swap_kernel<ACT, ACB, RND>, dim3(grid),
+                                dim3(SwapCfg::THREADS), SwapCfg::SMEM_BYTES, stream, tx, tw, p));
+  return LSC_SUCCESS;
+}
+
+template <int ACB, int RND>
+lsc_status launch_swap_act(const CUtensorMap& tx, const CUtensorMap& tw, const I8Params& p, int act,
+                           const DeviceState& ds, cudaStream_t stream) {
+  switch (act) {
+    case LSC_ACT_RELU: return launch_swap_cfg<LSC_ACT_RELU, ACB, RND>(tx, tw, p, ds, stream);
+    case LSC_ACT_RELU6: return launch_swap_cfg<LSC_ACT_RELU6, ACB, RND>(tx, tw, p, ds, stream);
+    case LSC_ACT_SILU: return launch_swap_cfg<LSC_ACT_SILU, ACB, RND>(tx, tw, p, ds, stream);
+    default: return launch_swap_cfg<LSC_ACT_NONE, ACB, RND>(tx, tw, p, ds, stream);
+  }
+}
+
+template <int ACB>
+lsc_status launch_swap(const CUtensorMap& tx, const CUtensorMap& tw, const I8Params& p, int act,
+                       const DeviceState& ds, cudaStream_t stream) {
+  if (p.rounding == LSC_ROUND_HALF_EVEN) return launch_swap_act<ACB, LSC_ROUND_HALF_EVEN>(tx, tw, p, act, ds, stream);
+  return launch_swap_act<ACB, LSC_ROUND_HALF_AWAY>(tx, tw, p, act, ds, stream);
+}
+
 // Column tile width: the widest tile that does not waste most of its columns.
 // Column-tile width: the widest of 256/128/64 that does not waste a partial tile, narrowed
 // while the grid would leave most SMs idle (small M, e.g. a classifier layer).
@@ -1071,6 +1398,16 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
   p.res_scale = res_scale;
   if (reinterpret_cast<uintptr_t>(residual) & 15) p.vec_ok = 0;
   if (!p.vec_ok) p.wide = 0;
+  // exactly 128 output channels, at least two k-blocks and two waves of 256-pixel tiles: the
+  // operand-swapped kernel (pixels on the wide side of every MMA; the filter map's 128-row
+  // box serves as its A operand).  Measured on B200 at batch 256: layer1 convs 98 -> 85 us,
+  // layer2 3x3 convs 52-56 -> 43-52 us; a single k-block (the 1x1 downsample) or fewer than
+  // two waves (layer1 at batch 32) run faster on the plain kernel.
+  if (g.c_out == 128 && bn == 128 && p.vec_ok && (acb == 128 || acb == 64) && act != LSC_ACT_GELU &&
+      p.k >= 256 && (m + 255) / 256 >= 2 * ds->sm_count) {
+    if (acb == 128) return launch_swap<128>(ta, tw, p, act, *ds, stream);
+    return launch_swap<64>(ta, tw, p, act, *ds, stream);
+  }
   switch (acb) {
     case 128: return launch_bn<128>(bn, ta, tw, p, act, *ds, stream);
     case 64: return launch_bn<64>(bn, ta, tw, p, act, *ds, stream);

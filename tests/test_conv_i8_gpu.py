@@ -84,3 +84,17 @@ def test_conv_i8_stride1_tiles(cuda, n, h, w, c, co, k, p, d):
 def test_conv_i8_large_batch_ragged_tiles(cuda):
     """M = 5*13*13 = 845 output pixels: tiles straddle images and the last tile is ragged."""
     _conv_case(cuda, 5, 13, 13, 128, 256, 3, 1, 1, act=orc.ACT_RELU)
+
+
+@pytest.mark.parametrize("n,h,c,s,k,p,act,rounding", [
+    (25, 56, 128, 1, 3, 1, orc.ACT_RELU, orc.ROUND_HALF_EVEN),   # layer2 3x3 / grouped layer1
+    (25, 57, 128, 1, 3, 1, orc.ACT_NONE, orc.ROUND_HALF_AWAY),   # ragged last tile
+    (25, 112, 64, 2, 3, 1, orc.ACT_RELU, orc.ROUND_HALF_AWAY),   # layer2.0.conv1 (64-byte blocks)
+    (25, 56, 256, 1, 1, 0, orc.ACT_NONE, orc.ROUND_HALF_EVEN),   # 1x1, two k-blocks
+    (22, 60, 128, 1, 3, 1, orc.ACT_RELU6, orc.ROUND_HALF_EVEN),
+])
+def test_conv_i8_operand_swap(cuda, n, h, c, s, k, p, act, rounding):
+    """128 output channels, two or more k-blocks and at least two waves of 256-pixel tiles: the
+    convolution runs with the filter as the MMA's A operand and 256 output pixels as its B
+    operand; bit-exact int32, f32 and int8 outputs."""
+    _conv_case(cuda, n, h, h, c, 128, k, s, p, act=act, rounding=rounding, seed=11)

@@ -182,12 +182,13 @@ def test_quantize_input_space_to_depth(be, c, cp, extra):
     np.testing.assert_array_equal(q.numpy().reshape(want.shape), want)
 
 
-def test_conv_residual_kernel_level(cuda):
-    """lsc_conv2d_i8_nhwc with a residual, including a ragged output tile."""
+@pytest.mark.parametrize("n,h,c,co", [(3, 9, 64, 96), (24, 57, 128, 128)])
+def test_conv_residual_kernel_level(cuda, n, h, c, co):
+    """lsc_conv2d_i8_nhwc with a residual, including a ragged output tile; the second shape
+    runs on the operand-swapped kernel (128 output channels, many pixels)."""
     import torch
     from lightship_b200 import ops
-    rng = np.random.default_rng(4)
-    n, h, c, co = 3, 9, 64, 96
+    rng = np.random.default_rng(4 + n)
     x = rng.integers(-127, 128, size=(n, h, h, c), dtype=np.int8)
     w = rng.integers(-127, 128, size=(co, 3, 3, c), dtype=np.int8)
     r = rng.integers(-128, 128, size=(n, h, h, co), dtype=np.int8)
