@@ -679,7 +679,7 @@ def run_gpu(args):
                    "graph_branches": branches, "downsample_side_stream": bool(args.ds_side),
                    "l2": "flushed (256 MiB write) before every timed step", "seed": NET_SEED},
         "network_tops": img_ops * batch / (ms_max * 1e-3) / 1e12,
-        "roofline": {"bound": "tensor", "kernel": "contraction_i8_kernel (INT8 implicit-GEMM conv)",
+        "roofline": {"bound": "tensor", "kernel": "contraction_i8_kernel + contraction_i8_swap_kernel (INT8 implicit-GEMM conv)",
                      "achieved": conv_tops, "peak": int8_peak, "unit": "TOPS", "frac": conv_tops / int8_peak,
                      "traffic": load_traffic("contraction_i8_conv_layer1_b256.md"), "peak_source": peak_source,
                      "conv_share_of_step": conv_ms / ms if ms > 0 else None},
