@@ -153,7 +153,16 @@ def network_conv_ops(model):
 
 
 # --------------------------------------------------------------------------- CPU side
-def cpu_resnet_sample(images, scales=None, threads=0):
+def host_threads():
+    """Every host core this process may run on.  Passed explicitly to the CPU legs so that a
+    launcher's OMP_NUM_THREADS (torchrun sets 1 per rank) cannot shrink the CPU baseline."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_resnet_sample(images, scales=None, threads=None):
     """The reference CPU path (oracle port) on `images` images; returns (seconds, logits)."""
     from lightship_b200.resnet18 import build_params
     from oracle import oracle as orc
@@ -161,7 +170,7 @@ def cpu_resnet_sample(images, scales=None, threads=0):
     rng = np.random.default_rng(DATA_SEED)
     x = rng.normal(size=(images, 3, IMAGE, IMAGE)).astype(np.float32)
     t0 = time.perf_counter()
-    logits, sc, _ = orc.resnet18_int8(x, convs, blocks, fw, fb, scales, 0, threads)
+    logits, sc, _ = orc.resnet18_int8(x, convs, blocks, fw, fb, scales, 0, threads or host_threads())
     return time.perf_counter() - t0, logits, sc
 
 
@@ -187,7 +196,7 @@ def run_reference(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": RESNET_WORKLOAD, "images_per_step": images},
-            "cpu_baseline": {"value": value, "unit": "img/s", "cores": os.cpu_count(), "kind": "port",
+            "cpu_baseline": {"value": value, "unit": "img/s", "cores": host_threads(), "kind": "port",
                              "sample": f"{images} images per step through the oracle's quantized ResNet-18 "
                                        "(direct int8 convolutions, OpenMP)"},
             "e2e": {"value": value, "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -208,7 +217,7 @@ def cpu_gemm_rows(rows, a, w_kn, bias, scale, s_out):
     """The reference CPU chain on rows [0, rows) of A: NN triple loop then the epilogue."""
     from oracle import oracle as orc
     t0 = time.perf_counter()
-    acc = orc.gemm_i8_nn(a[:rows], w_kn)
+    acc = orc.gemm_i8_nn(a[:rows], w_kn, host_threads())
     orc.requant(acc, bias, scale, orc.ACT_NONE, s_out, orc.ROUND_HALF_EVEN)
     return time.perf_counter() - t0
 
@@ -227,19 +236,20 @@ def run_reference_gemm(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": GEMM_WORKLOAD, "sample_rows_per_step": rows},
-            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port",
+            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": host_threads(), "kind": "port",
                              "sample": f"rows 0..{rows - 1} of A per step, reference loop order, OpenMP over M"},
             "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
 
-def cpu_bert_sample(seqs, scales=None, threads=0):
+def cpu_bert_sample(seqs, scales=None, threads=None):
     """The oracle's quantized encoder block on `seqs` sequences of 384 tokens; returns seconds
     and the scales (calibrated from this sample when none are given)."""
     from lightship_b200.bert import HIDDEN, build_params
     from oracle import oracle as orc
     p = build_params(BERT_SEED)
+    threads = threads or host_threads()
     x = np.random.default_rng(DATA_SEED).standard_normal((seqs * BERT_SEQ, HIDDEN)).astype(np.float32)
     if scales is None:
         scales = {"q1": 1.0, "q2": 1.0, "q3": 1.0, "u": 1.0}
@@ -267,7 +277,7 @@ def run_reference_bert(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8+f16", "data": "synthetic",
             "config": {"workload": BERT_WORKLOAD, "sequences_per_step": seqs},
-            "cpu_baseline": {"value": value, "unit": "sequences/s", "cores": os.cpu_count(), "kind": "port",
+            "cpu_baseline": {"value": value, "unit": "sequences/s", "cores": host_threads(), "kind": "port",
                              "sample": f"{seqs} sequences of 384 tokens per step through the oracle's quantized "
                                        "encoder block (INT8 projections, f32 attention with f16 rounding points)"},
             "e2e": {"value": value, "unit": "sequences/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -408,6 +418,95 @@ def gemm_measure(torch, dev, steps, warmup):
     return res, s_out
 
 
+def vendor_gemm_measure(torch, dev, steps, warmup):
+    """Library yardsticks on the same box, same L2 flush: cuBLASLt's INT8 GEMM through
+    torch._int_mm at 4096^3 (int32 output, no epilogue: it writes 64 MB where the INT8 chain
+    writes 16 MB of int8) and cuBLAS bf16 at 4096^3.  Returns {name: (TOPS, ms)}."""
+    g = torch.Generator(device=dev).manual_seed(NET_SEED)
+    a = torch.randint(-127, 128, (GEMM_M, GEMM_K), dtype=torch.int8, device=dev, generator=g)
+    w = torch.randint(-127, 128, (GEMM_N, GEMM_K), dtype=torch.int8, device=dev, generator=g)
+    ab, wb = a.to(torch.bfloat16), w.to(torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+    for name, fn in (("cublaslt_int8_int_mm", lambda: torch._int_mm(a, w.t())),
+                     ("cublas_bf16_matmul", lambda: torch.matmul(ab, wb.t()))):
+        try:
+            for _ in range(warmup):
+                flush.zero_()
+                fn()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+            torch.cuda.synchronize(dev)
+            torch.cuda._sleep(20_000_000)
+            for s_, e_ in ev:
+                flush.zero_()
+                s_.record(stream)
+                fn()
+                e_.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = float(np.mean([s_.elapsed_time(e_) for s_, e_ in ev]))
+            res[name] = (GEMM_OPS / (ms * 1e-3) / 1e12, ms)
+        except Exception as exc:  # a library without the kernel on this build
+            res[name] = (None, repr(exc)[:120])
+    return res
+
+
+def tensor_rate_probe():
+    """tcgen05.mma issue rate on resident shared-memory operands (lsc_probe_tensor_rate), on
+    every SM at once: {shape: {cycles, ns, TOPS (whole GPU)}}."""
+    from lightship_b200 import _lib
+    lib = _lib.lib()
+    out = {}
+    for kind, kname in ((0, "i8"), (1, "f16")):
+        for pair in (0, 1):
+            for n in (64, 128, 256):
+                cyc, ns = C.c_double(), C.c_double()
+                st = lib.lsc_probe_tensor_rate(kind, n, pair, 8192, 148, 0, 0, 0, C.byref(cyc), C.byref(ns))
+                if st:
+                    out[f"{kname}_m{256 if pair else 128}_n{n}"] = {"error": _lib.last_error()}
+                    continue
+                m = 256 if pair else 128
+                k = 32 if kind == 0 else 16
+                units = 74 if pair else 148
+                ops = 2.0 * m * n * k * units / (ns.value * 1e-9) / 1e12
+                out[f"{kname}_m{m}_n{n}"] = {"cycles_per_mma": round(cyc.value, 1), "ns_per_mma": round(ns.value, 2),
+                                            "tops_all_sms": round(ops, 1)}
+    return out
+
+
+def pipeline_probes(torch, dev):
+    """What bounds a pipelined contraction kernel, one factor at a time (lsc_probe_tensor_rate
+    with a stage-release cadence, lsc_probe_tma_rate for operand delivery)."""
+    from lightship_b200 import _lib
+    lib = _lib.lib()
+    out = {"mma_issue_loop": {}, "tma": {}}
+    cases = [(0, 0, 0), (1, 0, 0), (1, 4, 0), (1, 4, 6), (2, 4, 0), (2, 4, 2), (2, 4, 6), (3, 4, 0), (3, 4, 6),
+             (4, 4, 6)]
+    for pair, n in ((0, 64), (0, 128), (0, 256), (1, 256)):
+        for mode, ce, lag in cases:
+            cyc, ns = C.c_double(), C.c_double()
+            st = lib.lsc_probe_tensor_rate(0, n, pair, 8192, 148, mode, ce, lag, C.byref(cyc), C.byref(ns))
+            key = f"i8_m{256 if pair else 128}_n{n}_mode{mode}_commit{ce}_lag{lag}"
+            out["mma_issue_loop"][key] = (round(cyc.value, 1) if st == 0 else _lib.last_error())
+    if os.environ.get("LSC_PROBE_MMA_ONLY"):
+        return out
+    for mb, pitch in ((64, 4096),):
+        buf = torch.empty(mb << 20, dtype=torch.uint8, device=dev)
+        buf.fill_(1)
+        for rows, chunks in ((128, 1), (128, 2)):
+            for mode, warps, depth in ((0, 1, 3), (0, 2, 2), (0, 4, 2), (2, 2, 2), (2, 4, 2), (2, 4, 1)):
+                if rows * 128 * chunks * warps * depth > 196608 or warps * depth > 16:
+                    continue
+                bpc, gbs = C.c_double(), C.c_double()
+                st = lib.lsc_probe_tma_rate(C.c_void_p(buf.data_ptr()), buf.numel(), pitch, rows, chunks, depth,
+                                            warps, 1, 2048, 148, mode, C.byref(bpc), C.byref(gbs))
+                key = f"rows{rows}x{chunks}_mode{mode}_producers{warps}_depth{depth}_same_ctas148"
+                out["tma"][key] = ({"B_per_clk_per_sm": round(bpc.value, 1), "GB_s": round(gbs.value)}
+                                   if st == 0 else _lib.last_error())
+        del buf
+    return out
+
+
 def auto_branches(per_gpu_batch):
     """Concurrent image groups for a per-GPU ResNet batch.  Measured on B200 (graph step time,
     batch 32 / 64 / 128 / 256): two groups 322 / 450 / 676 / 1132 us against one chain's
@@ -490,6 +589,14 @@ def run_gpu(args):
             print(json.dumps(line), flush=True)
         return 0
 
+    if args.workload == "probe":
+        if rank == 0:
+            print(json.dumps({"tensor_rate_probe": tensor_rate_probe(), "pipeline": pipeline_probes(torch, dev)}),
+                  flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+
     if args.workload == "bert":
         from lightship_b200.backend import CudaBackend, GpuBackendConfig
         if BERT_BATCH % world:
@@ -522,7 +629,7 @@ def run_gpu(args):
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             seqs = 16
             dt, _ = cpu_bert_sample(seqs, r["scales"])
-            line["cpu_baseline"] = {"value": seqs / dt, "unit": "sequences/s", "cores": os.cpu_count(),
+            line["cpu_baseline"] = {"value": seqs / dt, "unit": "sequences/s", "cores": host_threads(),
                                     "kind": "port", "sample": f"{seqs} sequences of 384 tokens through the "
                                                               f"oracle's quantized encoder block, {dt:.2f} s"}
         be.close()
@@ -695,7 +802,10 @@ def run_gpu(args):
     if rank == 0 and not args.no_gemm:
         variants, _ = gemm_measure(torch, dev, max(50, min(args.steps, 200)), 10)
         tops, gms = variants["i8"]
+        vendor = vendor_gemm_measure(torch, dev, max(50, min(args.steps, 200)), 10)
+        line["tensor_rate_probe"] = tensor_rate_probe()
         line["int8_gemm_4096"] = {"value": tops, "unit": "TOPS", "ms_per_launch": gms, "workload": GEMM_WORKLOAD,
+                                  "vendor": {k: {"TOPS": v[0], "ms_per_launch": v[1]} for k, v in vendor.items()},
                                   "roofline_frac": tops / int8_peak,
                                   "traffic": load_traffic("contraction_i8_gemm_4096.md"),
                                   "variants": {k: {"TOPS": v[0], "ms_per_launch": v[1],
@@ -711,7 +821,7 @@ def run_gpu(args):
         if world == 1 and not args.no_cpu_baseline:
             imgs = 24
             dt, _, _ = cpu_resnet_sample(imgs, dict(model.scales))
-            line["cpu_baseline"] = {"value": imgs / dt, "unit": "img/s", "cores": os.cpu_count(), "kind": "port",
+            line["cpu_baseline"] = {"value": imgs / dt, "unit": "img/s", "cores": host_threads(), "kind": "port",
                                     "sample": f"{imgs} images through the oracle's quantized ResNet-18 "
                                               f"(direct int8 convolutions, OpenMP), {dt:.2f} s"}
     del graph
@@ -731,7 +841,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["lightship", "reference"], default="lightship")
-    ap.add_argument("--workload", choices=["resnet18", "gemm", "bert"], default="resnet18")
+    ap.add_argument("--workload", choices=["resnet18", "gemm", "bert", "probe"], default="resnet18")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--branches", type=int, default=0,
                     help="image groups run concurrently inside the ResNet graph (0 = chosen by the per-GPU batch)")

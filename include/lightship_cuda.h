@@ -279,7 +279,10 @@ lsc_status lsc_conv2d_i8_nhwc(const int8_t* x, const int8_t* w, int64_t n, int64
 
 /* quantize_tensor, per-tensor (quantization/helpers.rs:11-50 with quantize_value :139-155):
  *   q = clamp(sat_i32(R(x / scale)) + zero_point, qmin, qmax)   (i32 add wraps)
- * qdtype: LSC_DTYPE_QINT8/I8 -> int8 out, QUINT8/U8 -> uint8, QINT32/I32 -> int32.
+ * qdtype sets the storage: LSC_DTYPE_QINT8/I8 -> int8 out, QUINT8/U8 -> uint8, QINT32/I32 ->
+ * int32.  The clamp range follows quantize_value: QINT8 [-128, 127], QINT32 the i32 range,
+ * every other dtype (QUINT8, and plain I8 / U8 / I32 by the reference's `_` arm) [0, 255];
+ * with I8 storage a code above 127 wraps as Rust's `as i8`.
  * R = LSC_ROUND_HALF_AWAY reproduces the reference; HALF_EVEN is offered as a variant. */
 lsc_status lsc_quantize_f32(const float* x, void* out, int64_t n, int32_t qdtype, float scale,
                             int32_t zero_point, int32_t rounding, lsc_stream stream);
@@ -297,7 +300,9 @@ lsc_status lsc_dequantize(const void* q, int32_t qdtype, float* out, int64_t n, 
 lsc_status lsc_dequantize_per_channel(const void* q, int32_t qdtype, float* out, int64_t n,
                                       const float* scales, const int32_t* zero_points,
                                       int32_t channels, int64_t inner, lsc_stream stream);
-/* find_scale_zp (quantization/helpers.rs:101-136) over a device f32 array.  Writes the scale
+/* find_scale_zp (quantization/helpers.rs:101-136) over a device f32 array.  qdtype is any
+ * lsc_dtype; (qmin, qmax) = QINT8 (-128, 127), QINT32 (INT32_MIN, INT32_MAX), any other
+ * (0, 255) as the reference's `_` arm.  Writes the scale
  * and zero point to device memory.  `workspace` is caller-provided device scratch of at
  * least lsc_find_scale_zp_workspace_size() bytes (4-byte aligned); calls that share a
  * workspace must be ordered on one stream. */
@@ -321,13 +326,55 @@ lsc_status lsc_find_scale_zp_per_channel_f32(const float* x, int64_t channels, i
  * cudaMalloc would synchronise the device and fail once the owner holds the memory.  It
  * takes no workspace and allocates nothing: its scratch is a static device array sized for
  * at most 16384 channels (192 KiB, held on every GPU that loads the library until exit);
- * more channels are rejected with LSC_ERROR_INVALID_ARGUMENT.  The first call on a device
- * looks up that array's address, so make it before any stream capture.  All calls share the
- * array: calls that overlap on the GPU race with each other; sequential calls do not. */
+ * more channels are rejected with LSC_ERROR_INVALID_ARGUMENT.  The array is reserved when
+ * the library's CUDA module is loaded on a device; under lazy module loading (the CUDA 12
+ * default) that is the first call, so make one call per device early, before the owner of
+ * the memory has reserved the GPU, and before any stream capture (the first call also looks
+ * up the array's address).  All calls share the array: calls that overlap on the GPU race
+ * with each other; sequential calls do not. */
 lsc_status lsc_find_scale_zp_per_channel_f32_noalloc(const float* x, int64_t channels,
                                                      int64_t per_channel, int32_t qdtype,
                                                      int32_t symmetric, float* scales_out,
                                                      int32_t* zero_points_out, lsc_stream stream);
+
+/* ---- test hook of the bounded device waits ----------------------------------------------
+ * No counterpart in the reference, which has no device waits; it tests the path that reports
+ * LightShipError::Timeout (common/error.rs:32-34).  The next `launches` lsc_gemm_i8 calls made
+ * by this thread that run on single CTAs (not CTA pairs) leave one operand copy of their first
+ * tile unissued and give each device wait `wait_limit_ns` (1 ms .. 2 s) instead of 2 s: the
+ * waits on that copy run out, the kernel drains what it issued, frees its tensor memory and
+ * returns, the outputs are incomplete, and the next lsc_check_device / lsc_synchronize returns
+ * LSC_ERROR_TIMEOUT.  Nothing faults; the device stays usable.  0 launches cancels. */
+lsc_status lsc_debug_withhold_copy(int32_t launches, uint64_t wait_limit_ns);
+
+/* ---- measurement -----------------------------------------------------------------------
+ * No counterpart in the reference.  The tensor pipe's issue rate on operands resident in
+ * shared memory: on `ctas` SMs at once (one CTA, or one CTA pair with cta_pair = 1, per SM),
+ * one thread issues `iters` tcgen05.mma instructions of M = 128 (256 for a pair) x N (64, 128
+ * or 256) x 32 bytes of K (kind 0: kind::i8; kind 1: kind::f16) and waits for them; returns
+ * the median over CTAs of clock cycles and nanoseconds per instruction.  `mode` selects the
+ * shape of the issue loop: 0 a flat loop; 1 the flat loop with an optional commit every
+ * `commit_every` instructions and a wait for the commit `wait_lag` (0..7) back; 2 k-blocks of
+ * four instructions with a commit per k-block and a bounded wait `wait_lag` k-blocks back; 3
+ * as 2 with the whole warp looping and one elected lane issuing; 4 as 2 with a plain spin in
+ * place of the timed wait.  The ceiling the contraction kernels' roofline fractions are read
+ * against.  Allocates a few bytes of device memory for the results and synchronises. */
+lsc_status lsc_probe_tensor_rate(int32_t kind, int32_t n, int32_t cta_pair, int32_t iters, int32_t ctas,
+                                 int32_t mode, int32_t commit_every, int32_t wait_lag,
+                                 double* cycles_per_mma, double* ns_per_mma);
+/* No counterpart in the reference.  Operand delivery into shared memory: on `ctas` SMs, one
+ * thread per CTA keeps `depth` (1..3) TMA tile loads of box_rows (64/128/256) x 128 bytes x
+ * `chunks` (1, 2 or 4 consecutive 128-byte column blocks, a 3-D box, at most 64 KB) in flight
+ * from the device buffer `src` (`bytes` long, rows `row_pitch` bytes apart, 128-byte
+ * aligned), all slots within 192 KB; `same` = 1 makes every CTA read the same rows.  The
+ * producers are lane 0 of as many warps (mode 0: waits as the kernels do, bounded and timed;
+ * mode 1: a non-suspending spin) or lanes of one warp (mode 2).  Returns bytes per SM
+ * clock (median
+ * CTA) and the whole GPU's GB/s.  With the issue-loop modes above, the two probes separate
+ * the MMA pipe, the stage-release cadence and operand delivery.  Synchronises the device. */
+lsc_status lsc_probe_tma_rate(const void* src, uint64_t bytes, int64_t row_pitch, int32_t box_rows,
+                              int32_t chunks, int32_t depth, int32_t producers, int32_t same, int32_t iters,
+                              int32_t ctas, int32_t mode, double* bytes_per_clock, double* gbytes_per_s);
 
 /* ---- FP16 attention products (transformer block) ---------------------------------------
  * Batched C[bb][m][n] = alpha * sum_k A[bb][m][k] * B[bb][n][k] on the tensor cores (f16

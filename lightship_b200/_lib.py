@@ -119,6 +119,11 @@ SIGNATURES = {
     "lsc_find_scale_zp_per_channel_workspace_size": (C.c_uint64, [I64]),
     "lsc_find_scale_zp_per_channel_f32": (ST, [P, I64, I64, I32, I32, P, C.c_uint64, P, P, P]),
     "lsc_find_scale_zp_per_channel_f32_noalloc": (ST, [P, I64, I64, I32, I32, P, P, P]),
+    "lsc_debug_withhold_copy": (ST, [I32, C.c_uint64]),
+    "lsc_probe_tensor_rate": (ST, [I32, I32, I32, I32, I32, I32, I32, I32, C.POINTER(C.c_double),
+                                   C.POINTER(C.c_double)]),
+    "lsc_probe_tma_rate": (ST, [P, C.c_uint64, I64, I32, I32, I32, I32, I32, I32, I32, I32, C.POINTER(C.c_double),
+                                C.POINTER(C.c_double)]),
     "lsc_gemm_f16_batched": (ST, [P, I64, I64, I64, I64, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, F32, P, I32,
                                   I64, I64, I64, P]),
     "lsc_transpose_heads_f16": (ST, [P, P, I64, I64, I64, I64, I64, I64, I64, I64, P]),

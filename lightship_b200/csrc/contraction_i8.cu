@@ -67,6 +67,11 @@ struct I8Params {
   // keeps the whole [BN x K] weight tile in shared memory, loaded once per CTA (one N tile)
   int32_t a_stages;
   int32_t w_resident;
+  // bounded-wait limit of the single-CTA kernel, and its test hook: when withhold_kb >= 0,
+  // CTA 0 never issues the copies of k-block withhold_kb of its first tile (the waits on that
+  // stage then run out after wait_ns and the launch reports LSC_ERROR_TIMEOUT)
+  unsigned long long wait_ns = kWaitLimitNs;
+  int32_t withhold_kb = -1;
 };
 
 constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per block (227 KB)
@@ -372,6 +377,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       uint32_t stage = 0, phase = 0;
       int issued = 0;
       bool ok = true;
+      bool withheld = false;
       if (wres) {
         // the whole weight tile (one N tile: nb = 0) once, on its own barrier; the weights are
         // constant, so they are requested before the wait for the previous kernel
@@ -393,9 +399,19 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
           chh = oy * p.sh - p.ph;
         }
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, p.wait_ns)) {
             ok = false;
             break;
+          }
+          if (p.withhold_kb == kb && blockIdx.x == 0 && tile == static_cast<int>(blockIdx.x)) {
+            // test hook: this stage's copies are never issued, so nothing completes `full`
+            withheld = true;
+            ++issued;
+            if (++stage == static_cast<uint32_t>(stages)) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
           }
           mbar_arrive_expect_tx(&full[stage], wres ? C::A_BYTES : C::STAGE_BYTES);
           uint8_t* a_dst = sA + stage * C::A_BYTES;
@@ -423,17 +439,18 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
           }
         }
       }
-      if (!ok) {
-        // Let the copies already in flight land before the CTA can exit.
+      if (!ok || withheld) {
+        // Let the copies already in flight land before the CTA can exit (after a withheld
+        // copy the MMA warp stops consuming stages, so nothing else waits for them).
         volatile uint32_t no_abort = 0;
         const int outstanding = issued < stages ? issued : stages;
         for (int i = 1; i <= outstanding; ++i) {
           const int idx = issued - i;
           const int s = idx % stages;
           const uint32_t ph = static_cast<uint32_t>((idx / stages) & 1);
-          mbar_wait(&full[s], ph, &no_abort, p.err);
+          mbar_wait(&full[s], ph, &no_abort, p.err, p.wait_ns);
         }
-        if (wres) mbar_wait(wfull, 0u, &no_abort, p.err);
+        if (wres) mbar_wait(wfull, 0u, &no_abort, p.err, p.wait_ns);
       }
     }
   } else if (warp == 1) {
@@ -443,18 +460,18 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       int local = 0;
       bool ok = true;
       bool any_mma = false;
-      if (wres && !mbar_wait(wfull, 0u, abort_flag, p.err)) ok = false;
+      if (wres && !mbar_wait(wfull, 0u, abort_flag, p.err, p.wait_ns)) ok = false;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
         const int buf = local & 1;
         const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
-        if (!mbar_wait(&tempty[buf], buf_phase ^ 1u, abort_flag, p.err)) {
+        if (!mbar_wait(&tempty[buf], buf_phase ^ 1u, abort_flag, p.err, p.wait_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * C::BN);
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -480,7 +497,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
         // Wait for the MMAs already issued before TMEM is released.
         volatile uint32_t no_abort = 0;
         mma_commit(drain);
-        mbar_wait(drain, 0u, &no_abort, p.err);
+        mbar_wait(drain, 0u, &no_abort, p.err, p.wait_ns);
       }
     }
   } else {
@@ -511,7 +528,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
       const int row = mb * C::BM + row_in_tile;
       if constexpr (EXT) prefetch_residual(p, row, nb * C::BN + part * C::COLS_PER_EPI_WARP, C::COLS_PER_EPI_WARP);
-      if (!mbar_wait(&tfull[buf], buf_phase, abort_flag, p.err)) break;
+      if (!mbar_wait(&tfull[buf], buf_phase, abort_flag, p.err, p.wait_ns)) break;
       tc_fence_after();
       constexpr int CHUNKS = C::COLS_PER_EPI_WARP / C::EPI_W;
 #pragma unroll 1
@@ -1257,6 +1274,15 @@ void fill_outputs(I8Params& p, const int32_t* bias, const float* scale, float s_
   p.err = err;
 }
 
+// Test hook of the bounded waits (lsc_debug_withhold_copy): the next `launches` INT8 GEMM
+// launches on this thread that run on the single-CTA kernel withhold one operand copy and
+// wait at most wait_ns.
+struct WithholdRequest {
+  int32_t launches = 0;
+  unsigned long long wait_ns = kWaitLimitNs;
+};
+thread_local WithholdRequest t_withhold;
+
 }  // namespace
 
 lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k,
@@ -1311,6 +1337,11 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
       if (p.out_f16 && (reinterpret_cast<uintptr_t>(p.out_f16) & 31) == 0 && ldo % 16 == 0) p.wide |= 2;
       if (p.res_f32 && (reinterpret_cast<uintptr_t>(p.res_f32) & 31) == 0 && ldo % 8 == 0) p.wide |= 4;
     }
+  }
+  if (!pair && t_withhold.launches > 0) {
+    --t_withhold.launches;
+    p.withhold_kb = 0;
+    p.wait_ns = t_withhold.wait_ns;
   }
   if (p.out_f16 || p.res_f32) {
     if (pair) return launch_pair<true>(ta, tw, p, act, *ds, stream);
@@ -1403,8 +1434,10 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
   // box serves as its A operand).  Measured on B200 at batch 256: layer1 convs 98 -> 85 us,
   // layer2 3x3 convs 52-56 -> 43-52 us; a single k-block (the 1x1 downsample) or fewer than
   // two waves (layer1 at batch 32) run faster on the plain kernel.
+  // The swap kernel's epilogue has no f16 output and no f32 residual: a convolution that asks
+  // for either stays on the plain kernel.
   if (g.c_out == 128 && bn == 128 && p.vec_ok && (acb == 128 || acb == 64) && act != LSC_ACT_GELU &&
-      p.k >= 256 && (m + 255) / 256 >= 2 * ds->sm_count) {
+      !p.out_f16 && !p.res_f32 && p.k >= 256 && (m + 255) / 256 >= 2 * ds->sm_count) {
     if (acb == 128) return launch_swap<128>(ta, tw, p, act, *ds, stream);
     return launch_swap<64>(ta, tw, p, act, *ds, stream);
   }
@@ -1417,6 +1450,15 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
 }
 
 }  // namespace lsc
+
+extern "C" lsc_status lsc_debug_withhold_copy(int32_t launches, uint64_t wait_limit_ns) {
+  if (launches < 0 || wait_limit_ns < 1000000ull || wait_limit_ns > lsc::kWaitLimitNs)
+    return lsc::set_error(LSC_ERROR_INVALID_ARGUMENT,
+                          "debug_withhold_copy: launches >= 0 and a wait limit of 1 ms to 2 s");
+  lsc::t_withhold.launches = launches;
+  lsc::t_withhold.wait_ns = wait_limit_ns;
+  return LSC_SUCCESS;
+}
 
 extern "C" lsc_status lsc_conv2d_i8_nhwc(const int8_t* x, const int8_t* w, int64_t n, int64_t h,
                                          int64_t wd, int64_t c, int64_t c_out, int64_t kh,

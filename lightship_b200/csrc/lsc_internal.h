@@ -70,6 +70,10 @@ DeviceState* device_state(int device);
 lsc_status encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
                           uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                           uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+lsc_status encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                          const uint64_t dims[3], const uint64_t strides_bytes[2],
+                          const uint32_t box[3], const uint32_t elem_strides[3],
+                          CUtensorMapSwizzle swizzle);
 lsc_status encode_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
                           const uint64_t dims[4], const uint64_t strides_bytes[3],
                           const uint32_t box[4], const uint32_t elem_strides[4],

@@ -17,13 +17,15 @@ struct QRange {
   int32_t lo, hi;
 };
 
+// Clamp range of quantize_value / find_scale_zp (helpers.rs:109-114, :140-151): only the
+// quantized types have their own range; every other dtype, plain I8 and I32 included, takes
+// the `_` arm (0, 255).  The storage type is separate: I8 / QINT8 store int8 (a code above
+// 127 wraps as Rust's `as i8`), I32 / QINT32 int32, U8 / QUINT8 uint8.
 __host__ __device__ inline QRange qrange(int qdtype) {
   switch (qdtype) {
-    case LSC_DTYPE_QINT8:
-    case LSC_DTYPE_I8: return {-128, 127};
-    case LSC_DTYPE_QINT32:
-    case LSC_DTYPE_I32: return {INT32_MIN, INT32_MAX};
-    default: return {0, 255};  // QUInt8 / U8 and the reference's `_` arm
+    case LSC_DTYPE_QINT8: return {-128, 127};
+    case LSC_DTYPE_QINT32: return {INT32_MIN, INT32_MAX};
+    default: return {0, 255};  // QUInt8 and the reference's `_` arm
   }
 }
 
@@ -347,6 +349,9 @@ lsc_status launch_find_scale_zp(const float* x, int64_t n, int qdtype, int symme
   if (!scale_out || !zp_out)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "find_scale_zp: null output");
   if (n > 0 && !x) return set_error(LSC_ERROR_INVALID_ARGUMENT, "find_scale_zp: null input");
+  // find_scale_zp takes any DataType (helpers.rs:101): non-quantized types use (0, 255)
+  if (qdtype < LSC_DTYPE_F32 || qdtype > LSC_DTYPE_QINT32)
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "find_scale_zp: dtype %d", qdtype);
   if (!workspace || workspace_bytes < kFindScaleZpWorkspace ||
       (reinterpret_cast<uintptr_t>(workspace) & 3))
     return set_error(LSC_ERROR_INVALID_ARGUMENT,
@@ -391,7 +396,8 @@ lsc_status launch_find_scale_zp_rows(const float* x, int64_t rows, int64_t cols,
   if (rows == 0) return LSC_SUCCESS;
   if (!scales || !zps) return set_error(LSC_ERROR_INVALID_ARGUMENT, "find_scale_zp_per_channel: null output");
   if (cols > 0 && !x) return set_error(LSC_ERROR_INVALID_ARGUMENT, "find_scale_zp_per_channel: null input");
-  if (!valid_qdtype(qdtype))
+  // find_scale_zp takes any DataType (helpers.rs:101): non-quantized types use (0, 255)
+  if (qdtype < LSC_DTYPE_F32 || qdtype > LSC_DTYPE_QINT32)
     return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "find_scale_zp_per_channel: dtype %d", qdtype);
   if (!ws || ws_bytes < find_scale_zp_rows_workspace(rows) || (reinterpret_cast<uintptr_t>(ws) & 3))
     return set_error(LSC_ERROR_INVALID_ARGUMENT,
@@ -476,30 +482,64 @@ uint64_t lsc_find_scale_zp_per_channel_workspace_size(int64_t channels) {
 // -- and must not call cudaMalloc: it synchronises the device and fails once the owner
 // holds the memory.  This variant needs no caller workspace.  Its scratch is a file-scope
 // device array of kNoAllocMaxChannels * 12 bytes (192 KiB), which every GPU that loads
-// this library holds until the process exits.
+// this library holds until the process exits.  The array is reserved when the CUDA module
+// of this library is loaded into a context; with lazy module loading (the CUDA 12 default)
+// that happens at the first call, so a caller that cannot allocate makes one call per device
+// early, before the memory owner has reserved the GPU.
 namespace {
 constexpr int64_t kNoAllocMaxChannels = 16384;
 static __device__ __align__(256) uint32_t g_fsz_noalloc_scratch[3 * kNoAllocMaxChannels];
 
 std::mutex g_noalloc_mu;
-uint32_t* g_noalloc_ptr[64] = {};
+struct NoAllocSlot {
+  CUcontext ctx = nullptr;  // the context the address below belongs to
+  uint32_t* ptr = nullptr;
+};
+NoAllocSlot g_noalloc_slot[64];
 
-// Device address of the scratch array for the current device.  The host-side name of a
-// __device__ array is not a device address, so the address is queried once per device,
-// with that device current, and cached.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+CtxGetCurrentFn ctx_get_current_fn() {
+  static std::once_flag once;
+  static CtxGetCurrentFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
+// Device address of the scratch array in the current device's context.  The host-side name
+// of a __device__ array is not a device address, so the address is queried with the device
+// current and cached together with the context it was taken in: after a cudaDeviceReset the
+// primary context (and the module holding the array) is created anew, the cached context no
+// longer matches, and the address is looked up again.
 lsc_status noalloc_scratch(uint32_t** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return set_error(LSC_ERROR_INVALID_ARGUMENT, "device %d out of range", dev);
+  CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+  if (!get_ctx) return set_error(LSC_ERROR_DEVICE_ERROR, "cuCtxGetCurrent unavailable");
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS)
+    return set_error(LSC_ERROR_DEVICE_ERROR, "find_scale_zp_per_channel_noalloc: cuCtxGetCurrent failed");
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  NoAllocSlot& slot = g_noalloc_slot[dev];
+  if (!ctx || !slot.ptr || slot.ctx != ctx) {
+    // the lookup also makes the runtime bind the device's primary context to this thread
+    // when none was current yet
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_fsz_noalloc_scratch);
     if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(find_scale_zp scratch)");
-    g_noalloc_ptr[dev] = static_cast<uint32_t*>(p);
+    if (!ctx && (get_ctx(&ctx) != CUDA_SUCCESS || !ctx))
+      return set_error(LSC_ERROR_DEVICE_ERROR, "find_scale_zp_per_channel_noalloc: no current CUDA context");
+    slot.ctx = ctx;
+    slot.ptr = static_cast<uint32_t*>(p);
   }
-  *out = g_noalloc_ptr[dev];
+  *out = slot.ptr;
   return LSC_SUCCESS;
 }
 }  // namespace
@@ -508,9 +548,10 @@ extern "C" {
 
 // Same results as lsc_find_scale_zp_per_channel_f32, with the library's own static scratch
 // in place of the caller's workspace.  The first call on a device looks up the scratch
-// address (make it before any stream capture).  Every call shares the one array: calls
-// that overlap on the GPU (e.g. on two streams) race; each call re-initialises the part it
-// uses, so back-to-back calls are independent.
+// address and, under lazy module loading, loads the module that holds the array (make it
+// before any stream capture, and before the memory owner has reserved the device).  Every
+// call shares the one array: calls that overlap on the GPU (e.g. on two streams) race; each
+// call re-initialises the part it uses, so back-to-back calls are independent.
 lsc_status lsc_find_scale_zp_per_channel_f32_noalloc(const float* x, int64_t channels,
                                                      int64_t per_channel, int32_t qdtype,
                                                      int32_t symmetric, float* scales_out,

@@ -176,6 +176,17 @@ lsc_status encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const voi
   return encode(map, dtype, 2, base, dims, strides, box, estr, swizzle);
 }
 
+lsc_status encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                          const uint64_t dims[3], const uint64_t strides_bytes[2],
+                          const uint32_t box[3], const uint32_t elem_strides[3],
+                          CUtensorMapSwizzle swizzle) {
+  const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  const cuuint64_t s[2] = {strides_bytes[0], strides_bytes[1]};
+  const cuuint32_t b[3] = {box[0], box[1], box[2]};
+  const cuuint32_t e[3] = {elem_strides[0], elem_strides[1], elem_strides[2]};
+  return encode(map, dtype, 3, base, d, s, b, e, swizzle);
+}
+
 lsc_status encode_tmap_4d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
                           const uint64_t dims[4], const uint64_t strides_bytes[3],
                           const uint32_t box[4], const uint32_t elem_strides[4],

@@ -20,6 +20,7 @@ ROUND_HALF_AWAY = 0
 ROUND_HALF_EVEN = 1
 ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SILU, ACT_GELU = 0, 1, 2, 3, 4
 QUINT8, QINT8, QINT32 = 0, 1, 2
+OTHER = 3  # any non-quantized DataType: the `_` arm of helpers.rs:109-114 / :140-151, (0, 255)
 
 
 def build() -> str:

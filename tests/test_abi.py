@@ -91,3 +91,14 @@ def test_backend_create_reports_missing_device():
     st = _lib.lib().lsc_backend_create(C.byref(cfg), C.byref(h))
     assert st == _lib.ERROR_BACKEND_NOT_AVAILABLE
     assert not h.value
+
+
+def test_withhold_hook_argument_checks():
+    """The bounded-wait test hook takes a launch count and a 1 ms .. 2 s wait limit; setting it
+    launches nothing (0 cancels)."""
+    lib = _lib.lib()
+    assert lib.lsc_debug_withhold_copy(-1, 10_000_000) == _lib.ERROR_INVALID_ARGUMENT
+    assert lib.lsc_debug_withhold_copy(1, 10) == _lib.ERROR_INVALID_ARGUMENT
+    assert lib.lsc_debug_withhold_copy(1, 3_000_000_000) == _lib.ERROR_INVALID_ARGUMENT
+    assert lib.lsc_debug_withhold_copy(1, 10_000_000) == _lib.SUCCESS
+    assert lib.lsc_debug_withhold_copy(0, 10_000_000) == _lib.SUCCESS

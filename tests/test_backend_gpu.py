@@ -108,28 +108,34 @@ def test_fc_int8_from_f32_weights_quantizes_per_channel(backend):
     np.testing.assert_array_equal(y.numpy().reshape(m, n).view(np.uint32), want[1].view(np.uint32))
 
 
-@pytest.mark.parametrize("qdtype,zp", [(9, 0), (8, 128), (10, 3)])
+@pytest.mark.parametrize("qdtype,zp", [(9, 0), (8, 128), (10, 3), (3, 5), (5, -7)])
 @pytest.mark.parametrize("rounding", [0, 1])
 def test_quantize_dequantize_ops(backend, qdtype, zp, rounding):
+    """Quantize / Dequantize operators against quantize_value / dequantize_value
+    (helpers.rs:139-160).  Plain I8 (3) and I32 (5) take the reference's `_` arm: the clamp
+    range is (0, 255) whatever the storage, and an I8 code above 127 wraps as `as i8`."""
     from lightship_b200.backend import (DataType, OperatorDef, OperatorType, Quantization,
                                         Rounding, Tensor)
     rng = np.random.default_rng(qdtype * 10 + rounding)
     x = rng.normal(0, 3, size=(2, 3, 17, 19)).astype(np.float32)
     x.ravel()[:6] = [0.25, -0.25, 0.75, 1e30, -1e30, np.nan]  # ties at scale 0.5, saturation, NaN
     scale = 0.5
-    npdt = {9: np.int8, 8: np.uint8, 10: np.int32}[qdtype]
+    npdt = {9: np.int8, 8: np.uint8, 10: np.int32, 3: np.int8, 5: np.int32}[qdtype]
     xt = Tensor("x", list(x.shape), DataType.F32, x)
     qt = Tensor("q", [1], DataType(qdtype), np.zeros(x.size, npdt), quantization=Quantization([scale], [zp]))
     op = backend.compile_operator(OperatorDef("q", OperatorType.Quantize, rounding=Rounding(rounding)),
                                   None, [xt], [qt])
     backend.execute(op, [xt], [qt])
-    oq = {9: orc.QINT8, 8: orc.QUINT8, 10: orc.QINT32}[qdtype]
-    if rounding == 0:
+    oq = {9: orc.QINT8, 8: orc.QUINT8, 10: orc.QINT32}.get(qdtype, orc.OTHER)
+    if rounding == 0 and oq != orc.OTHER:
         want = orc.quantize_tensor(x, scale, zp, oq)
+    elif rounding == 0:
+        want = np.array([orc.quantize_value(float(v), scale, zp, oq) for v in x.ravel()],
+                        np.int64).astype(npdt).reshape(x.shape)
     else:  # half-even variant of quantize_value
         t = (x / np.float32(scale)).astype(np.float32)
         r = np.rint(t)
-        lo, hi = {9: (-128, 127), 8: (0, 255), 10: (-2**31, 2**31 - 1)}[qdtype]
+        lo, hi = {9: (-128, 127), 10: (-2**31, 2**31 - 1)}.get(qdtype, (0, 255))
         ri = np.where(np.isnan(r), 0, np.clip(r, -2**31, 2**31 - 1)).astype(np.int64)
         ri = np.where(r >= 2**31, 2**31 - 1, ri)
         s = (ri + zp + 2**31) % 2**32 - 2**31  # wrapping i32 add
@@ -142,7 +148,11 @@ def test_quantize_dequantize_ops(backend, qdtype, zp, rounding):
     yt = Tensor("y", [1], DataType.F32, np.zeros(x.size, np.float32))
     dop = backend.compile_operator(OperatorDef("dq", OperatorType.Dequantize), None, [qin], [yt])
     backend.execute(dop, [qin], [yt])
-    np.testing.assert_array_equal(yt.numpy().reshape(x.shape), orc.dequantize_tensor(want, scale, zp, oq))
+    if oq != orc.OTHER:
+        want_y = orc.dequantize_tensor(want, scale, zp, oq)
+    else:  # dequantize_value on the stored integers: (q as f32 - zp as f32) * scale
+        want_y = (want.astype(np.float32) - np.float32(zp)) * np.float32(scale)
+    np.testing.assert_array_equal(yt.numpy().reshape(x.shape), want_y)
 
 
 def test_quantize_per_channel_nchw(backend):
@@ -160,7 +170,7 @@ def test_quantize_per_channel_nchw(backend):
     np.testing.assert_array_equal(qt.numpy().reshape(x.shape), want)
 
 
-@pytest.mark.parametrize("symmetric,qdtype", [(1, 9), (0, 8), (1, 8), (0, 10)])
+@pytest.mark.parametrize("symmetric,qdtype", [(1, 9), (0, 8), (1, 8), (0, 10), (1, 3), (0, 3), (1, 5), (0, 5)])
 def test_find_scale_zp_device(cuda, symmetric, qdtype):
     import torch
     from lightship_b200 import _lib
@@ -177,7 +187,7 @@ def test_find_scale_zp_device(cuda, symmetric, qdtype):
         _lib.check(lib.lsc_find_scale_zp_f32(tx.data_ptr(), x.size, qdtype, symmetric, ws.data_ptr(), 16,
                                              s.data_ptr(), z.data_ptr(),
                                              torch.cuda.current_stream().cuda_stream))
-        oq = {9: orc.QINT8, 8: orc.QUINT8, 10: orc.QINT32}[qdtype]
+        oq = {9: orc.QINT8, 8: orc.QUINT8, 10: orc.QINT32}.get(qdtype, orc.OTHER)
         ws_, wz = orc.find_scale_zp(x, oq, bool(symmetric))
         assert s.item() == np.float32(ws_) and z.item() == wz, (x[:4], s.item(), ws_, z.item(), wz)
 
@@ -238,7 +248,7 @@ def test_backend_destroyed_before_its_operators(cuda):
 
 @pytest.mark.parametrize("rows,cols,symmetric,qdtype", [(64, 576, 1, 9), (1000, 512, 1, 9),
                                                         (3, 200_003, 0, 8), (7, 1, 0, 10),
-                                                        (5, 0, 1, 9)])
+                                                        (5, 0, 1, 9), (9, 333, 0, 3), (4, 100, 1, 5)])
 def test_find_scale_zp_per_channel(cuda, rows, cols, symmetric, qdtype):
     """find_scale_zp per output channel (weights [Cout, K]), including rows split over
     several blocks, NaN entries, an all-zero row and empty rows."""
@@ -258,7 +268,7 @@ def test_find_scale_zp_per_channel(cuda, rows, cols, symmetric, qdtype):
     _lib.check(lib.lsc_find_scale_zp_per_channel_f32(tx.data_ptr(), rows, cols, qdtype, symmetric,
                                                      ws.data_ptr(), ws_bytes, s.data_ptr(), z.data_ptr(),
                                                      torch.cuda.current_stream().cuda_stream))
-    oq = {9: orc.QINT8, 8: orc.QUINT8, 10: orc.QINT32}[qdtype]
+    oq = {9: orc.QINT8, 8: orc.QUINT8, 10: orc.QINT32}.get(qdtype, orc.OTHER)
     want = [orc.find_scale_zp(x[r], oq, bool(symmetric)) for r in range(rows)]
     assert s.cpu().numpy().tolist() == [np.float32(w[0]) for w in want]
     assert z.cpu().numpy().tolist() == [w[1] for w in want]

@@ -66,6 +66,19 @@ def test_quantize_value_semantics():
     assert orc.quantize_value(1e30, 1.0, 128, orc.QUINT8) == 0
 
 
+def test_non_quantized_dtypes_take_the_default_arm():
+    """quantize_value and find_scale_zp send every dtype other than QUInt8 / QInt8 / QInt32
+    (plain I8, I32, ...) to the `_` arm, (qmin, qmax) = (0, 255) (helpers.rs:109-114,
+    :140-151)."""
+    assert orc.quantize_value(-3.0, 1.0, 0, orc.OTHER) == 0
+    assert orc.quantize_value(200.0, 1.0, 0, orc.OTHER) == 200
+    assert orc.quantize_value(1000.0, 1.0, 0, orc.OTHER) == 255
+    s, z = orc.find_scale_zp(f32([-2.0, 1.0]), orc.OTHER, True)
+    assert z == 0 and s == np.float32(2.0) / np.float32(255.0)
+    s, z = orc.find_scale_zp(f32([-2.0, 1.0]), orc.OTHER, False)
+    assert s == np.float32(3.0) / np.float32(255.0)
+
+
 def test_rounding_modes_on_ties():
     ties = f32([0.5, 1.5, 2.5, -0.5, -1.5, -2.5])
     away = [orc.lib().orc_round(float(t), orc.ROUND_HALF_AWAY) for t in ties]

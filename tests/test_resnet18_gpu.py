@@ -202,3 +202,31 @@ def test_conv_residual_kernel_level(cuda, n, h, c, co):
     ops.check_device()
     np.testing.assert_array_equal(y.cpu().numpy().view(np.uint32), want[1].view(np.uint32))
     np.testing.assert_array_equal(q.cpu().numpy(), want[0])
+
+
+@pytest.mark.parametrize("batch", [32, 256])
+def test_resnet18_int8_bit_exact_at_benchmark_batches(be, cuda, batch):
+    """The network at the per-GPU batches the benchmark times (256 on one GPU, 32 per GPU on
+    eight): tile widths, the operand-swapped kernel and weight residency are chosen from the
+    batch, so these are different kernels from the batch-2 test.  Run as the benchmark runs it
+    (one captured graph, downsample convs on a side stream); images are independent once the
+    activation scales are fixed, so the first and last four images of the batch are checked
+    against the oracle, logits and every block output."""
+    import torch
+    from lightship_b200.resnet18 import ResNet18Int8
+    model = ResNet18Int8(be, batch, cuda, image=224, seed=11)
+    rng = np.random.default_rng(batch)
+    x = rng.normal(size=(batch, 3, 224, 224)).astype(np.float32)
+    xd = torch.from_numpy(x).to(cuda)
+    model.calibrate(xd)
+    g = model.capture(xd, branches=1, concurrent_downsample=True)
+    model.logits.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    logits = model.logits.cpu().numpy()
+    pick = np.r_[0:4, batch - 4:batch]
+    want, acts = oracle_resnet18(np.ascontiguousarray(x[pick]), model, 0)
+    np.testing.assert_array_equal(logits[pick].view(np.uint32), want.view(np.uint32))
+    for name in [f"layer{s}.{b}.conv2" for s in (1, 2, 3, 4) for b in (0, 1)] + ["conv1", "pool"]:
+        np.testing.assert_array_equal(model.buf[name].cpu().numpy()[pick], acts[name], err_msg=name)
+    del g

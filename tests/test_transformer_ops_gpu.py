@@ -191,11 +191,16 @@ def test_layernorm_int8_output(be, dtype, rounding):
     assert (qd.cpu().numpy() != 0).mean() > 0.9
 
 
-@pytest.mark.parametrize("m,n,k,act", [(384, 2304, 768, 0), (300, 200, 96, 4), (1024, 768, 3072, 0), (129, 40, 64, 1)])
+@pytest.mark.parametrize("m,n,k,act", [(384, 2304, 768, 0), (300, 200, 96, 4), (1024, 768, 3072, 0), (129, 40, 64, 1),
+                                       (2048, 1024, 256, 1), (12288, 2304, 768, 0), (12288, 768, 3072, 0),
+                                       (12288, 768, 768, 0)])
 def test_fully_connected_f16_output_and_f32_residual(be, cuda, m, n, k, act):
     """The INT8 FullyConnected writing f16 (the QKV projection feeding FP16 attention) and
     adding an f32 residual before the activation (output projection, FFN down): vector
-    stores on full chunks, scalar stores on ragged N; CTA pairs at the wide shapes."""
+    stores on full chunks, scalar stores on ragged N.  The shapes with N > 256 and at least 32
+    tiles of 256 x 256 run on CTA pairs: 2048 x 1024 (exactly 32 pair tiles) and the BERT
+    block's own projections at batch 32 x seq 384 = 12288 tokens (QKV 432 pair tiles, FFN down
+    and output projection 144); the others on single CTAs."""
     import torch
     from lightship_b200.backend import Activation, DataType, OperatorDef, OperatorType, Quantization, Tensor
     rng = np.random.default_rng(m * 7 + n)
@@ -212,11 +217,11 @@ def test_fully_connected_f16_output_and_f32_residual(be, cuda, m, n, k, act):
                              [xa, Tensor("w", [n, k], DataType.F32, w), Tensor("b", [n], DataType.F32, bias)], outs)
     rt = Tensor("r", [m, n], DataType.F32, torch.from_numpy(res).to(cuda))
     be.execute(op, [xa, rt], outs)
-    want = orc.fc_i8_f32_weights(a, s_a, w, bias)[1] + res
-    want = orc.act(want, act)
+    chain = orc.fc_i8_f32_weights(a, s_a, w, bias)[1]
+    want = orc.act(chain + res, act)
     np.testing.assert_array_equal(y32.cpu().numpy().view(np.uint32), want.view(np.uint32))
     np.testing.assert_array_equal(y16.cpu().numpy().view(np.uint16), want.astype(np.float16).view(np.uint16))
     # without the residual the same operator reproduces the plain chain
     be.execute(op, [xa], outs)
-    plain = orc.act(orc.fc_i8_f32_weights(a, s_a, w, bias)[1], act)
+    plain = orc.act(chain, act)
     np.testing.assert_array_equal(y32.cpu().numpy().view(np.uint32), plain.view(np.uint32))

@@ -2,9 +2,10 @@
 cudaMalloc (code embedded in a host runtime that owns the GPU's memory, where an allocation
 would synchronise the device and fail once that memory is reserved).
 
-It is checked through the C ABI against the workspace-taking entry point on two calls in a
-row: the shared static scratch must not carry state from one call into the next.  This file
-is collected last so a failure here cannot hide the other tests' results."""
+It is checked through the C ABI against the workspace-taking entry point and against the
+oracle's find_scale_zp applied to every channel, on consecutive calls: the shared static
+scratch must not carry state from one call into the next.  This file is collected last so a
+failure here cannot hide the other tests' results."""
 import numpy as np
 import pytest
 
@@ -33,6 +34,17 @@ def _noalloc_call(lib, _lib, tx, rows, cols, qdtype, symmetric, cuda, stream):
     return s, z
 
 
+def _oracle_per_channel(x, qdtype, symmetric):
+    """find_scale_zp (quantization/helpers.rs:101-136) of the oracle on each row of x."""
+    from oracle import oracle as orc
+    od = {9: orc.QINT8, 8: orc.QUINT8, 10: orc.QINT32}.get(qdtype, orc.OTHER)
+    s = np.empty(x.shape[0], np.float32)
+    z = np.empty(x.shape[0], np.int32)
+    for r in range(x.shape[0]):
+        s[r], z[r] = orc.find_scale_zp(np.ascontiguousarray(x[r]), od, bool(symmetric))
+    return s, z
+
+
 def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(cuda):
     import torch
     from lightship_b200 import _lib
@@ -52,6 +64,9 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(cuda):
         torch.cuda.synchronize()
         assert torch.equal(got_s, want_s)
         assert torch.equal(got_z, want_z)
+        orc_s, orc_z = _oracle_per_channel(x, qdtype, symmetric)
+        assert np.array_equal(got_s.cpu().numpy().view(np.uint32), orc_s.view(np.uint32))
+        assert np.array_equal(got_z.cpu().numpy(), orc_z)
     # and once more on the first input after the second
     tx1 = torch.from_numpy(x1).to(cuda)
     want_s, want_z = _reference_call(lib, _lib, tx1, 512, 70_000, 9, 1, cuda, stream)
