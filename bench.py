@@ -490,20 +490,61 @@ def pipeline_probes(torch, dev):
             out["mma_issue_loop"][key] = (round(cyc.value, 1) if st == 0 else _lib.last_error())
     if os.environ.get("LSC_PROBE_MMA_ONLY"):
         return out
-    for mb, pitch in ((64, 4096),):
-        buf = torch.empty(mb << 20, dtype=torch.uint8, device=dev)
-        buf.fill_(1)
-        for rows, chunks in ((128, 1), (128, 2)):
-            for mode, warps, depth in ((0, 1, 3), (0, 2, 2), (0, 4, 2), (2, 2, 2), (2, 4, 2), (2, 4, 1)):
-                if rows * 128 * chunks * warps * depth > 196608 or warps * depth > 16:
-                    continue
-                bpc, gbs = C.c_double(), C.c_double()
-                st = lib.lsc_probe_tma_rate(C.c_void_p(buf.data_ptr()), buf.numel(), pitch, rows, chunks, depth,
-                                            warps, 1, 2048, 148, mode, C.byref(bpc), C.byref(gbs))
-                key = f"rows{rows}x{chunks}_mode{mode}_producers{warps}_depth{depth}_same_ctas148"
-                out["tma"][key] = ({"B_per_clk_per_sm": round(bpc.value, 1), "GB_s": round(gbs.value)}
-                                   if st == 0 else _lib.last_error())
+    for n, h in ((256, 14), (256, 56), (32, 7)):
+        buf = torch.ones(n * h * h * 128, dtype=torch.uint8, device=dev)
+        for depth, prods in ((2, 1), (3, 1), (2, 2), (2, 4), (3, 4)):
+            bpc, gbs = C.c_double(), C.c_double()
+            st = lib.lsc_probe_im2col_rate(C.c_void_p(buf.data_ptr()), n, h, h, depth, prods, 4096, 148,
+                                           C.byref(bpc), C.byref(gbs))
+            out["tma"][f"im2col_n{n}_h{h}_producers{prods}_depth{depth}"] = (
+                {"B_per_clk_per_sm": round(bpc.value, 1), "GB_s": round(gbs.value)} if st == 0 else _lib.last_error())
         del buf
+    return out
+
+
+# ResNet-18 convolution shapes (name, batch-256 input H, C_in, C_out, k, stride, residual)
+CONV_SHAPES = [("layer1.conv", 56, 64, 64, 3, 1, True), ("layer2.0.conv1", 56, 64, 128, 3, 2, False),
+               ("layer2.conv", 28, 128, 128, 3, 1, True), ("layer3.conv", 14, 256, 256, 3, 1, True),
+               ("layer4.conv", 7, 512, 512, 3, 1, True), ("layer4.0.downsample", 14, 256, 512, 1, 2, False)]
+
+
+def conv_measure(torch, dev, batch, steps, warmup, only=()):
+    """Each ResNet-18 convolution shape alone through lsc_conv2d_i8_nhwc (ReLU, requantized int8
+    output, the block's int8 residual where it has one), L2 flushed before every launch:
+    {name: (us per launch, TOPS)}."""
+    from lightship_b200 import ops
+    g = torch.Generator(device=dev).manual_seed(7)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+    for name, h, ci, co, k, st, res in CONV_SHAPES:
+        if only and name not in only:
+            continue
+        x = torch.randint(-127, 128, (batch, h, h, ci), dtype=torch.int8, device=dev, generator=g)
+        w = torch.randint(-127, 128, (co, k, k, ci), dtype=torch.int8, device=dev, generator=g)
+        scale = torch.full((co,), 1e-4, dtype=torch.float32, device=dev)
+        pad = k // 2
+        ho = (h + 2 * pad - k) // st + 1
+        r = torch.randint(-127, 128, (batch, ho, ho, co), dtype=torch.int8, device=dev, generator=g) if res else None
+
+        def launch():
+            ops.conv2d_i8_nhwc(x, w, scale, None, stride=(st, st), pad=(pad, pad), s_out=0.05, act=1,
+                               residual=r, residual_scale=0.02)
+        for _ in range(warmup):
+            flush.zero_()
+            launch()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        torch.cuda.synchronize(dev)
+        torch.cuda._sleep(20_000_000)
+        for s_, e_ in ev:
+            flush.zero_()
+            s_.record(stream)
+            launch()
+            e_.record(stream)
+        torch.cuda.synchronize(dev)
+        us = 1e3 * float(np.mean([s_.elapsed_time(e_) for s_, e_ in ev]))
+        ops_n = 2.0 * batch * ho * ho * co * k * k * ci
+        out[name] = (round(us, 2), round(ops_n / (us * 1e-6) / 1e12, 1))
     return out
 
 
@@ -587,6 +628,18 @@ def run_gpu(args):
             dist.destroy_process_group()
         if rank == 0:
             print(json.dumps(line), flush=True)
+        return 0
+
+    if args.workload == "conv":
+        if rank == 0:
+            only = tuple(args.only.split(",")) if args.only else ()
+            res = {"batch": args.batch, "conv": conv_measure(torch, dev, args.batch, args.steps, args.warmup, only)}
+            if not only:
+                res["gemm_4096"] = {k: (round(v[1] * 1e3, 2), round(v[0], 1))
+                                    for k, v in gemm_measure(torch, dev, args.steps, args.warmup)[0].items()}
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
         return 0
 
     if args.workload == "probe":
@@ -841,7 +894,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["lightship", "reference"], default="lightship")
-    ap.add_argument("--workload", choices=["resnet18", "gemm", "bert", "probe"], default="resnet18")
+    ap.add_argument("--workload", choices=["resnet18", "gemm", "bert", "probe", "conv"], default="resnet18")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--branches", type=int, default=0,
                     help="image groups run concurrently inside the ResNet graph (0 = chosen by the per-GPU batch)")
@@ -851,6 +904,7 @@ def main():
                     help="global ResNet batch (default 256, the benchmark's; smaller only for profiling)")
     ap.add_argument("--no-gemm", action="store_true", help="skip the 4096^3 GEMM sub-measurement")
     ap.add_argument("--no-bert", action="store_true", help="skip the encoder-block sub-measurement")
+    ap.add_argument("--only", default="", help="--workload conv: comma-separated shape names to run")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -372,6 +372,13 @@ lsc_status lsc_probe_tensor_rate(int32_t kind, int32_t n, int32_t cta_pair, int3
  * clock (median
  * CTA) and the whole GPU's GB/s.  With the issue-loop modes above, the two probes separate
  * the MMA pipe, the stage-release cadence and operand delivery.  Synchronises the device. */
+/* No counterpart in the reference.  The same for im2col loads, the convolutions' A operand:
+ * `src` is an NHWC int8 tensor [n, h, w, 128] (128-byte aligned); every load brings 128 output
+ * pixels x 128 channels of one tap of a 3x3, padding-1 filter (16 KB); `producers` (1..4)
+ * warps keep `depth` loads each in flight. */
+lsc_status lsc_probe_im2col_rate(const void* src, int64_t n, int64_t h, int64_t w, int32_t depth,
+                                 int32_t producers, int32_t iters, int32_t ctas, double* bytes_per_clock,
+                                 double* gbytes_per_s);
 lsc_status lsc_probe_tma_rate(const void* src, uint64_t bytes, int64_t row_pitch, int32_t box_rows,
                               int32_t chunks, int32_t depth, int32_t producers, int32_t same, int32_t iters,
                               int32_t ctas, int32_t mode, double* bytes_per_clock, double* gbytes_per_s);

@@ -122,6 +122,8 @@ SIGNATURES = {
     "lsc_debug_withhold_copy": (ST, [I32, C.c_uint64]),
     "lsc_probe_tensor_rate": (ST, [I32, I32, I32, I32, I32, I32, I32, I32, C.POINTER(C.c_double),
                                    C.POINTER(C.c_double)]),
+    "lsc_probe_im2col_rate": (ST, [P, I64, I64, I64, I32, I32, I32, I32, C.POINTER(C.c_double),
+                                   C.POINTER(C.c_double)]),
     "lsc_probe_tma_rate": (ST, [P, C.c_uint64, I64, I32, I32, I32, I32, I32, I32, I32, I32, C.POINTER(C.c_double),
                                 C.POINTER(C.c_double)]),
     "lsc_gemm_f16_batched": (ST, [P, I64, I64, I64, I64, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, F32, P, I32,

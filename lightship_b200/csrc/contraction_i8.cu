@@ -21,6 +21,7 @@
 //               dependent chains overlapped.  The accumulator buffer is released right after
 //               its last TMEM read so the next tile's MMAs overlap this tile's epilogue math.
 #include <math.h>
+#include <stdlib.h>
 #include <stdio.h>
 
 #include <mutex>
@@ -76,6 +77,69 @@ struct I8Params {
 
 constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per block (227 KB)
 
+// ---- several producer threads ------------------------------------------------------------
+// One thread completes only about one TMA tensor load per ~600 cycles on B200, whatever the
+// box size up to 64 KB (measured with lsc_probe_tma_rate: ~25 B/clk per SM with 16 KB boxes
+// from one thread, ~97 B/clk from four), while a 128 x 256 x 32 int8 MMA takes 128 cycles.  So
+// the loads of every k-block are spread over kProducers threads (lane 0 of each producer warp):
+// load j of k-block iteration `it` (counted over the CTA's tiles in consumption order) belongs
+// to producer (it * L + j) % kProducers, L = loads per k-block, and the producer of load 0
+// posts the stage's byte count.  Another producer's bytes may land first; the mbarrier's
+// tx-count then goes negative for a while, and the phase still completes only after that
+// arrive.  The ring needs at least kProducers stages (so a producer's parity wait on `empty`
+// cannot alias a phase two rounds back).  The producers are lanes 0-1 of warps 0-1: separate
+// threads are what matters (measured: two lanes of one warp deliver 44 B/clk, two warps 49),
+// and 19 warps keep the 96 registers per thread that a fifth warp on one SM sub-partition
+// (21 warps) would cut to 80.
+constexpr int kProducerWarps = 2;
+constexpr int kProducerLanes = 2;
+constexpr int kProducers = kProducerWarps * kProducerLanes;
+
+// Shared-memory record the MMA warp reads to drain the loads still in flight after an abort.
+struct ProducerLog {
+  int32_t slot_it[8];  // the iteration whose loads were posted into each ring slot
+  uint32_t done;       // producer threads that have left their loop
+};
+
+__device__ __forceinline__ void producer_log_init(ProducerLog* lg) {
+  for (int i = 0; i < 8; ++i) lg->slot_it[i] = -1;
+  lg->done = 0u;
+}
+
+// The owner of a k-block iteration's load 0, once every load of the iteration it took part in
+// is issued, notes the iteration in the log; every producer leaving its loop counts itself out.
+__device__ __forceinline__ void producer_leave(ProducerLog* lg) {
+  __threadfence_block();
+  atomicAdd(&lg->done, 1u);
+}
+
+// After an abort (MMA thread): waits (bounded) until every producer has left its loop, then for
+// each of the `stages` iterations from it_next on whose loads were posted waits for them to
+// land, so no copy is still writing shared memory when the CTA exits.
+__device__ __noinline__ void drain_in_flight(uint64_t* full, int stages, int it_next, ProducerLog* lg,
+                                             uint32_t* err, unsigned long long wait_ns) {
+  volatile uint32_t* done = &lg->done;
+  const unsigned long long t0 = globaltimer_ns();
+  while (*done < static_cast<uint32_t>(kProducers)) {
+    if (globaltimer_ns() - t0 > wait_ns) {
+      if (err) atomicOr(err, LSC_DEVERR_TIMEOUT);
+      break;
+    }
+  }
+  volatile uint32_t no_abort = 0;
+  volatile int32_t* slot_it = lg->slot_it;
+  for (int d = 0; d < stages; ++d) {
+    const int i = it_next + d;
+    const int st = i % stages;
+    if (slot_it[st] == i) mbar_wait(&full[st], static_cast<uint32_t>((i / stages) & 1), &no_abort, err, wait_ns);
+  }
+}
+
+// Index, among this producer's loads of iteration `it`, of its first load (>= L: none).
+__device__ __forceinline__ int first_load_of(int pr, int it, int L) {
+  return (pr - (it * L) % kProducers + kProducers) % kProducers;
+}
+
 template <int BN_>
 struct I8Cfg {
   static constexpr int BM = 128;
@@ -89,7 +153,8 @@ struct I8Cfg {
   // EPI_WARPS epilogue warps: EPI_WARPS / 4 per TMEM lane quarter, each taking that share of
   // the tile's columns in chunks of EPI_W
   static constexpr int EPI_WARPS = 16;
-  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int MMA_WARP = kProducerWarps;  // producer warps, then the MMA warp, then epilogue
+  static constexpr int THREADS = 32 * (kProducerWarps + 1 + EPI_WARPS);
   static constexpr int COLS_PER_EPI_WARP = BN / (EPI_WARPS / 4);
   static constexpr int EPI_W = 16;
   static constexpr int MAX_STAGES = 8;  // barrier slots
@@ -100,8 +165,8 @@ struct I8Cfg {
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + EPI_COL_BYTES;
   static constexpr uint32_t IDESC = idesc_i8(BM, BN);
   static_assert(SMEM_BYTES <= kSmemLimit, "shared memory budget");
-  static_assert((2 * MAX_STAGES + 6) * 8 + 8 <= BAR_BYTES, "barrier area");
-  static_assert(STAGES <= MAX_STAGES, "barrier slots");
+  static_assert((2 * MAX_STAGES + 6) * 8 + 8 <= 192 && 192 + sizeof(ProducerLog) <= BAR_BYTES, "barrier area");
+  static_assert(STAGES <= MAX_STAGES && STAGES >= kProducers && RES_STAGES >= kProducers, "ring slots");
   // shared memory with the weights resident: RES_STAGES A slots, kblocks W tiles
   static constexpr int res_smem_bytes(int kblocks) {
     return RES_STAGES * A_BYTES + kblocks * B_BYTES + 1024 + BAR_BYTES + EPI_COL_BYTES;
@@ -114,13 +179,17 @@ struct PairCfg {
   static constexpr int STAGES = 6;
   static constexpr int EPI_WARPS = 16;
   static constexpr int EPI_W = 16;
-  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int MMA_WARP = kProducerWarps;  // producer warps, the MMA warp, the epilogue
+  static constexpr int THREADS = 32 * (kProducerWarps + 1 + EPI_WARPS);
   static constexpr int COLS_PER_EPI_WARP = 256 / (EPI_WARPS / 4);
   static constexpr int BAR_BYTES = 256;
   static constexpr int EPI_COL_BYTES = EPI_WARPS * COLS_PER_EPI_WARP * 8;
   static constexpr int SMEM_BYTES = STAGES * (2 * 128 * 128) + 1024 + BAR_BYTES + EPI_COL_BYTES;
   static_assert(SMEM_BYTES <= kSmemLimit, "shared memory budget");
-  static_assert((2 * STAGES + 5) * 8 + 8 <= BAR_BYTES, "barrier area");
+  static constexpr int LOG_OFFSET = 160;  // ProducerLog within the barrier area
+  static_assert((2 * STAGES + 5) * 8 + 8 <= LOG_OFFSET && LOG_OFFSET + sizeof(ProducerLog) <= BAR_BYTES,
+                "barrier area");
+  static_assert(STAGES >= kProducers, "ring slots");
 };
 
 
@@ -133,6 +202,14 @@ __device__ __forceinline__ void prefetch_residual(const I8Params& p, int row, in
     if (col0 + i < p.n) asm volatile("prefetch.global.L2 [%0];" ::"l"(rp + col0 + i));
 }
 
+// This thread's 16 int8 residual values of columns [col0, col0 + 16) when the epilogue will read
+// them as one vector (zero otherwise): loaded a chunk ahead, so the load's latency overlaps the
+// accumulator's wait and the previous chunk's arithmetic instead of stalling the chunk.
+__device__ __forceinline__ uint4 load_residual16(const I8Params& p, int row, int col0) {
+  if (!p.residual || row >= p.m || !p.vec_ok || col0 + 16 > p.n) return make_uint4(0u, 0u, 0u, 0u);
+  return __ldg(reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(row) * p.ldo + col0));
+}
+
 // Epilogue for W consecutive columns of one output row held by this thread; cs / cb are the
 // chunk's per-column scales and biases staged in shared memory (zero past the last column).
 // Each output is stored as soon as it is final (i32, then f32, then int8) so the
@@ -141,7 +218,8 @@ __device__ __forceinline__ void prefetch_residual(const I8Params& p, int row, in
 // their registers and instructions for the int8 path.
 template <int ACT, int W, bool EXT>
 __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t (&r)[W],
-                                               const float* cs, const int32_t* cb, int row, int col0) {
+                                               const float* cs, const int32_t* cb, int row, int col0,
+                                               const uint4* res_pre = nullptr) {
   static_assert(W % 16 == 0, "chunks are whole 16-byte int8 vectors");
   if (row >= p.m) return;
   const bool vec = (col0 + W <= p.n) && p.vec_ok;
@@ -179,7 +257,7 @@ __device__ __forceinline__ void epilogue_chunk(const I8Params& p, const uint32_t
     if (vec) {
 #pragma unroll
       for (int v = 0; v < W / 16; ++v) {
-        const uint4 rv = __ldg(reinterpret_cast<const uint4*>(p.residual + base) + v);
+        const uint4 rv = res_pre ? res_pre[v] : __ldg(reinterpret_cast<const uint4*>(p.residual + base) + v);
         const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -333,6 +411,7 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
   uint64_t* wfull = drain + 1;  // resident weights landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wfull + 1);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  ProducerLog* plog = reinterpret_cast<ProducerLog*>(after_w + 192);
   uint8_t* epi_cols = after_w + C::BAR_BYTES;
 
   const int warp = threadIdx.x >> 5;
@@ -348,15 +427,16 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       mbar_init(&tempty[i], C::EPI_WARPS);
     }
     mbar_init(drain, 1);
-    mbar_init(wfull, 1);
+    mbar_init(wfull, kProducers);
     *abort_flag = 0u;
+    producer_log_init(plog);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
   }
-  if (warp == 1) {
+  if (warp == C::MMA_WARP) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -371,20 +451,27 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
   const int n_tiles = (p.n + C::BN - 1) / C::BN;
   const int num_tiles = m_tiles * n_tiles;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------- TMA producer
-      uint32_t stage = 0, phase = 0;
-      int issued = 0;
+  if (warp < kProducerWarps) {
+    if (lane < kProducerLanes) {
+      // ------------------------------------------------------------- TMA producers
+      const int pr = warp * kProducerLanes + lane;
       bool ok = true;
-      bool withheld = false;
       if (wres) {
-        // the whole weight tile (one N tile: nb = 0) once, on its own barrier; the weights are
-        // constant, so they are requested before the wait for the previous kernel
-        mbar_arrive_expect_tx(wfull, static_cast<uint32_t>(kblocks * C::B_BYTES));
-        for (int kb = 0; kb < kblocks; ++kb) tma_load_2d(&tmW, wfull, sW + kb * C::B_BYTES, kb * C::BK, 0);
+        // the whole weight tile (one N tile: nb = 0) once, on its own barrier, spread over the
+        // producers; the weights are constant, so they are requested before the wait for the
+        // previous kernel
+        uint32_t mine = 0;
+        for (int kb = pr; kb < kblocks; kb += kProducers) mine += C::B_BYTES;
+        mbar_arrive_expect_tx(wfull, mine);
+        for (int kb = pr; kb < kblocks; kb += kProducers) tma_load_2d(&tmW, wfull, sW + kb * C::B_BYTES, kb * C::BK, 0);
       }
       griddep_wait();  // A is the previous kernel's output
+      constexpr int SUB = ACB > 0 ? 128 / ACB : 1;  // A loads per k-block
+      const int L = SUB + (wres ? 0 : 1);          // then the W load
+      const uint32_t stage_bytes = wres ? C::A_BYTES : C::STAGE_BYTES;
+      int it = 0;
+      int ring_stage = 0;  // it % stages and (it / stages) & 1, kept incrementally
+      uint32_t ring_phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int mb = tile % m_tiles, nb = tile / m_tiles;
         // filter-origin coordinates of the tile's first output pixel (convolution only)
@@ -398,111 +485,112 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
           cw = ox * p.sw - p.pw;
           chh = oy * p.sh - p.ph;
         }
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int stage = ring_stage;
+          const uint32_t phase = ring_phase;
+          if (++ring_stage == stages) {
+            ring_stage = 0;
+            ring_phase ^= 1u;
+          }
+          const int j0 = first_load_of(pr, it, L);
+          if (j0 >= L) continue;
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, p.wait_ns)) {
             ok = false;
             break;
           }
-          if (p.withhold_kb == kb && blockIdx.x == 0 && tile == static_cast<int>(blockIdx.x)) {
-            // test hook: this stage's copies are never issued, so nothing completes `full`
-            withheld = true;
-            ++issued;
-            if (++stage == static_cast<uint32_t>(stages)) {
-              stage = 0;
-              phase ^= 1u;
-            }
-            continue;
-          }
-          mbar_arrive_expect_tx(&full[stage], wres ? C::A_BYTES : C::STAGE_BYTES);
+          // test hook: the loads of this k-block are never issued, so nothing completes `full`
+          if (p.withhold_kb == kb && blockIdx.x == 0 && tile == static_cast<int>(blockIdx.x)) continue;
+          if (j0 == 0) mbar_arrive_expect_tx(&full[stage], stage_bytes);
           uint8_t* a_dst = sA + stage * C::A_BYTES;
-          if constexpr (ACB == 0) {
-            tma_load_2d(&tmA, &full[stage], a_dst, kb * C::BK, mb * C::BM);
-          } else {
-            constexpr int SUB = 128 / ACB;
-#pragma unroll
-            for (int i = 0; i < SUB; ++i) {
-              int j = kb * SUB + i;  // channel chunk index in (kh, kw, c) order
-              if (j >= p.total_chunks) j = 0;  // past the filter: weights are zero there
-              const int tap = j / p.chunks_per_tap;
-              const int c0 = (j - tap * p.chunks_per_tap) * ACB;
+          for (int j = j0; j < L; j += kProducers) {
+            if (j == SUB) {
+              tma_load_2d(&tmW, &full[stage], sW + stage * C::B_BYTES, kb * C::BK, nb * C::BN);
+            } else if constexpr (ACB == 0) {
+              tma_load_2d(&tmA, &full[stage], a_dst, kb * C::BK, mb * C::BM);
+            } else {
+              int jc = kb * SUB + j;  // channel chunk index in (kh, kw, c) order
+              if (jc >= p.total_chunks) jc = 0;  // past the filter: weights are zero there
+              const int tap = jc / p.chunks_per_tap;
+              const int c0 = (jc - tap * p.chunks_per_tap) * ACB;
               const int ky = tap / p.kw;
               const int kx = tap - ky * p.kw;
-              tma_load_im2col_4d(&tmA, &full[stage], a_dst + i * (C::BM * ACB), c0, cw, chh, cn,
+              tma_load_im2col_4d(&tmA, &full[stage], a_dst + j * (C::BM * ACB), c0, cw, chh, cn,
                                  static_cast<uint16_t>(kx * p.dw), static_cast<uint16_t>(ky * p.dh));
             }
           }
-          if (!wres) tma_load_2d(&tmW, &full[stage], sW + stage * C::B_BYTES, kb * C::BK, nb * C::BN);
-          ++issued;
-          if (++stage == static_cast<uint32_t>(stages)) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          if (j0 == 0) plog->slot_it[stage] = it;
         }
       }
-      if (!ok || withheld) {
-        // Let the copies already in flight land before the CTA can exit (after a withheld
-        // copy the MMA warp stops consuming stages, so nothing else waits for them).
-        volatile uint32_t no_abort = 0;
-        const int outstanding = issued < stages ? issued : stages;
-        for (int i = 1; i <= outstanding; ++i) {
-          const int idx = issued - i;
-          const int s = idx % stages;
-          const uint32_t ph = static_cast<uint32_t>((idx / stages) & 1);
-          mbar_wait(&full[s], ph, &no_abort, p.err, p.wait_ns);
+      producer_leave(plog);
+    }
+  } else if (warp == C::MMA_WARP) {
+    // --------------------------------------------------------------- MMA issuer
+    // The whole warp runs the loop, waits together and agrees on the outcome (__all_sync); one
+    // elected lane issues.  Measured on B200: a lone lane issuing tcgen05.mma while the rest of
+    // its warp is parked takes ~450 cycles per k-block of four, the converged warp ~370.
+    // Shared-memory descriptors are the stage-0 descriptors plus the byte offset / 16 in their
+    // start-address field (shared addresses stay below 2^18, so the field cannot carry).
+    int it = 0;
+    int stage = 0;  // it % stages and (it / stages) & 1, kept incrementally
+    uint32_t phase = 0;
+    int local = 0;
+    bool ok = true;
+    bool any_mma = false;
+    uint64_t a_kk[C::BK / 32], w_kk[C::BK / 32];
+#pragma unroll
+    for (int kk = 0; kk < C::BK / 32; ++kk) {
+      a_kk[kk] = a_desc<ACB>(smem_u32(sA), kk);
+      w_kk[kk] = smem_desc_sw128_kmajor(smem_u32(sW) + kk * 32);
+    }
+    if (wres) ok = __all_sync(0xFFFFFFFFu, mbar_wait(wfull, 0u, abort_flag, p.err, p.wait_ns));
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&tempty[buf], buf_phase ^ 1u, abort_flag, p.err, p.wait_ns));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * C::BN);
+      for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&full[stage], phase, abort_flag, p.err, p.wait_ns));
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t ao = static_cast<uint64_t>(stage * (C::A_BYTES >> 4));
+        const uint64_t wo = static_cast<uint64_t>((wres ? kb : stage) * (C::B_BYTES >> 4));
+        if (elect_one()) {
+#pragma unroll
+          for (int kk = 0; kk < C::BK / 32; ++kk)
+            mma_i8(d_tmem, a_kk[kk] + ao, w_kk[kk] + wo, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+          mma_commit(&empty[stage]);
         }
-        if (wres) mbar_wait(wfull, 0u, &no_abort, p.err, p.wait_ns);
+        __syncwarp();
+        any_mma = true;
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) {
+        if (elect_one()) mma_commit(&tfull[buf]);
+        __syncwarp();
       }
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------- MMA issuer
-      uint32_t stage = 0, phase = 0;
-      int local = 0;
-      bool ok = true;
-      bool any_mma = false;
-      if (wres && !mbar_wait(wfull, 0u, abort_flag, p.err, p.wait_ns)) ok = false;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
-        const int buf = local & 1;
-        const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
-        if (!mbar_wait(&tempty[buf], buf_phase ^ 1u, abort_flag, p.err, p.wait_ns)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * C::BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, p.wait_ns)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
-          const uint32_t w0 = smem_u32(sW + (wres ? kb : static_cast<int>(stage)) * C::B_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < C::BK / 32; ++kk) {
-            const uint64_t ad = a_desc<ACB>(a0, kk);
-            const uint64_t wd = smem_desc_sw128_kmajor(w0 + kk * 32);
-            mma_i8(d_tmem, ad, wd, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
-          }
-          any_mma = true;
-          mma_commit(&empty[stage]);
-          if (++stage == static_cast<uint32_t>(stages)) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (ok) mma_commit(&tfull[buf]);
-      }
-      if (!ok && any_mma) {
-        // Wait for the MMAs already issued before TMEM is released.
+    if (!ok) {
+      // Let the copies in flight land and the MMAs already issued finish before TMEM and the
+      // shared memory are released.
+      if (elect_one()) {
+        drain_in_flight(full, stages, it, plog, p.err, p.wait_ns);
         volatile uint32_t no_abort = 0;
-        mma_commit(drain);
-        mbar_wait(drain, 0u, &no_abort, p.err, p.wait_ns);
+        if (wres) mbar_wait(wfull, 0u, &no_abort, p.err, p.wait_ns);
+        if (any_mma) {
+          mma_commit(drain);
+          mbar_wait(drain, 0u, &no_abort, p.err, p.wait_ns);
+        }
       }
+      __syncwarp();
     }
   } else {
     // --------------------------------------------------------------- epilogue
-    const int epi = warp - 2;       // 0..EPI_WARPS-1
+    const int epi = warp - C::MMA_WARP - 1;  // 0..EPI_WARPS-1
     const int quarter = warp & 3;   // TMEM lane quarter this warp may read
     const int part = epi >> 2;      // which share of the tile's columns
     const int row_in_tile = quarter * 32 + lane;
@@ -528,6 +616,9 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
       const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
       const int row = mb * C::BM + row_in_tile;
       if constexpr (EXT) prefetch_residual(p, row, nb * C::BN + part * C::COLS_PER_EPI_WARP, C::COLS_PER_EPI_WARP);
+      static_assert(C::EPI_W == 16, "one 16-byte residual vector per chunk");
+      const int col_first = nb * C::BN + part * C::COLS_PER_EPI_WARP;
+      uint4 res_next = load_residual16(p, row, col_first);  // before the accumulator is ready
       if (!mbar_wait(&tfull[buf], buf_phase, abort_flag, p.err, p.wait_ns)) break;
       tc_fence_after();
       constexpr int CHUNKS = C::COLS_PER_EPI_WARP / C::EPI_W;
@@ -538,6 +629,8 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
                                static_cast<uint32_t>(buf * C::BN + tcol);
         uint32_t r[C::EPI_W];
         tmem_ld_cols(taddr, r);
+        const uint4 res_cur = res_next;
+        if (c + 1 < CHUNKS) res_next = load_residual16(p, row, col_first + (c + 1) * C::EPI_W);
         tmem_ld_wait();
         if (c == CHUNKS - 1) {
           tc_fence_before();
@@ -545,13 +638,13 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
           if (lane == 0) mbar_arrive(&tempty[buf]);
         }
         epilogue_chunk<ACT, C::EPI_W, EXT>(p, r, w_scale + c * C::EPI_W, w_bias + c * C::EPI_W, row,
-                                           nb * C::BN + tcol);
+                                           nb * C::BN + tcol, &res_cur);
       }
     }
   }
 
   __syncthreads();
-  if (warp == 1) {
+  if (warp == C::MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
@@ -599,6 +692,7 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  ProducerLog* plog = reinterpret_cast<ProducerLog*>(reinterpret_cast<uint8_t*>(bars) + P::LOG_OFFSET);
   uint8_t* epi_cols = reinterpret_cast<uint8_t*>(bars) + P::BAR_BYTES;
 
   const int warp = threadIdx.x >> 5;
@@ -617,13 +711,14 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
     }
     mbar_init(drain, 1);
     *abort_flag = 0u;
+    producer_log_init(plog);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
   }
-  if (warp == 1) {
+  if (warp == P::MMA_WARP) {
     tmem_alloc_pair(tmem_slot, 2 * PN);
     tmem_relinquish_pair();
   }
@@ -642,87 +737,108 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
   const int num_tiles = m_tiles * n_tiles;
   const int kblocks = (p.k + C::BK - 1) / C::BK;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------- TMA producer
-      uint32_t stage = 0, phase = 0;
-      int issued = 0;
+  if (warp < kProducerWarps) {
+    if (lane < kProducerLanes) {
+      // ------------------------------------------------------------- TMA producers (both CTAs)
+      // Each CTA loads its own halves; they complete on the even CTA's `full`, where the even
+      // CTA's owner of load 0 posts the pair's byte count.
+      const int pr = warp * kProducerLanes + lane;
       bool ok = true;
       griddep_wait();  // A is the previous kernel's output
+      constexpr int L = 2;  // A rows, W rows
+      int it = 0;
+      int ring_stage = 0;
+      uint32_t ring_phase = 0;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
         const int mb = tile % m_tiles, nb = tile / m_tiles;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int stage = ring_stage;
+          const uint32_t phase = ring_phase;
+          if (++ring_stage == STAGES) {
+            ring_stage = 0;
+            ring_phase ^= 1u;
+          }
+          const int j0 = first_load_of(pr, it, L);
+          if (j0 >= L) continue;
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
             ok = false;
             break;
           }
-          if (even) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + WROWS * C::BK));
+          if (even && j0 == 0) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + WROWS * C::BK));
           const uint32_t fb = full_even + stage * 8;
-          tma_load_2d_pair(&tmA, fb, sA + stage * A_BYTES, kb * C::BK, mb * 256 + static_cast<int>(rank) * ROWS);
-          tma_load_2d_pair(&tmW, fb, sW + stage * W_BYTES, kb * C::BK, nb * PN + static_cast<int>(rank) * WROWS);
-          ++issued;
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
+          for (int j = j0; j < L; j += kProducers) {
+            if (j == 0)
+              tma_load_2d_pair(&tmA, fb, sA + stage * A_BYTES, kb * C::BK, mb * 256 + static_cast<int>(rank) * ROWS);
+            else
+              tma_load_2d_pair(&tmW, fb, sW + stage * W_BYTES, kb * C::BK, nb * PN + static_cast<int>(rank) * WROWS);
           }
+          if (j0 == 0) plog->slot_it[stage] = it;
         }
       }
-      if (!ok && even) {
-        // Let the pair's copies in flight land (they complete on these barriers).
-        volatile uint32_t no_abort = 0;
-        const int outstanding = issued < STAGES ? issued : STAGES;
-        for (int i = 1; i <= outstanding; ++i) {
-          const int idx = issued - i;
-          mbar_wait(&full[idx % STAGES], static_cast<uint32_t>((idx / STAGES) & 1), &no_abort, p.err);
-        }
-      }
+      producer_leave(plog);
     }
-  } else if (warp == 1) {
-    if (lane == 0 && even) {
-      // ------------------------------------------------------------- MMA issuer (even CTA)
-      uint32_t stage = 0, phase = 0;
+  } else if (warp == P::MMA_WARP) {
+    if (even) {
+      // ----------------------------------------------------------- MMA issuer (even CTA, converged warp)
+      int it = 0;
+      int stage = 0;
+      uint32_t phase = 0;
       int local = 0;
       bool ok = true;
       bool any_mma = false;
+      uint64_t a_kk[C::BK / 32], w_kk[C::BK / 32];
+#pragma unroll
+      for (int kk = 0; kk < C::BK / 32; ++kk) {
+        a_kk[kk] = smem_desc_sw128_kmajor(smem_u32(sA) + kk * 32);
+        w_kk[kk] = smem_desc_sw128_kmajor(smem_u32(sW) + kk * 32);
+      }
       for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++local) {
         const int buf = local & 1;
         const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
-        if (!mbar_wait(&tempty[buf], buf_phase ^ 1u, abort_flag, p.err)) {
-          ok = false;
-          break;
-        }
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&tempty[buf], buf_phase ^ 1u, abort_flag, p.err));
+        if (!ok) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * PN);
-        for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
-            ok = false;
-            break;
-          }
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&full[stage], phase, abort_flag, p.err));
+          if (!ok) break;
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
-          const uint32_t w0 = smem_u32(sW + stage * W_BYTES);
+          const uint64_t ao = static_cast<uint64_t>(stage * (A_BYTES >> 4));
+          const uint64_t wo = static_cast<uint64_t>(stage * (W_BYTES >> 4));
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < C::BK / 32; ++kk)
-            mma_i8_pair(d_tmem, smem_desc_sw128_kmajor(a0 + kk * 32), smem_desc_sw128_kmajor(w0 + kk * 32), IDESC,
-                        (kb | kk) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < C::BK / 32; ++kk)
+              mma_i8_pair(d_tmem, a_kk[kk] + ao, w_kk[kk] + wo, IDESC, (kb | kk) != 0 ? 1u : 0u);
+            mma_commit_pair(&empty[stage], 0x3);
+          }
+          __syncwarp();
           any_mma = true;
-          mma_commit_pair(&empty[stage], 0x3);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if (ok) mma_commit_pair(&tfull[buf], 0x3);
+        if (ok) {
+          if (elect_one()) mma_commit_pair(&tfull[buf], 0x3);
+          __syncwarp();
+        }
       }
-      if (!ok && any_mma) {
-        volatile uint32_t no_abort = 0;
-        mma_commit_pair(drain, 0x1);
-        mbar_wait(drain, 0u, &no_abort, p.err);
+      if (!ok) {
+        // the pair's copies in flight complete on these barriers; the MMAs issued must finish
+        if (elect_one()) {
+          drain_in_flight(full, STAGES, it, plog, p.err, kWaitLimitNs);
+          if (any_mma) {
+            volatile uint32_t no_abort = 0;
+            mma_commit_pair(drain, 0x1);
+            mbar_wait(drain, 0u, &no_abort, p.err);
+          }
+        }
+        __syncwarp();
       }
     }
   } else {
     // --------------------------------------------------------------- epilogue (own rows)
-    const int epi = warp - 2;
+    const int epi = warp - P::MMA_WARP - 1;
     const int quarter = warp & 3;
     const int part = epi >> 2;
     const int row_in_tile = quarter * 32 + lane;
@@ -772,7 +888,7 @@ __global__ void __launch_bounds__(PairCfg::THREADS, 1)
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // no CTA leaves while its peer may still signal its barriers
-  if (warp == 1) {
+  if (warp == P::MMA_WARP) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, 2 * PN);
   }
@@ -906,14 +1022,18 @@ struct SwapCfg {
   static constexpr int X_BYTES = BP * BK;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
   static constexpr int EPI_WARPS = 16;
-  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int MMA_WARP = kProducerWarps;  // producer warps, the MMA warp, the epilogue
+  static constexpr int THREADS = 32 * (kProducerWarps + 1 + EPI_WARPS);
   static constexpr int TMEM_COLS = 2 * BP;  // double-buffered accumulator
   static constexpr int BAR_BYTES = 256;
   static constexpr int OUT_STAGE_BYTES = 4 * 2048;  // per part: 16 pixels x 128 channels of int8
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES + OUT_STAGE_BYTES;
   static constexpr uint32_t IDESC = idesc_i8(BM, BP);
   static_assert(SMEM_BYTES <= kSmemLimit, "shared memory budget");
-  static_assert((2 * STAGES + 5) * 8 + 8 <= BAR_BYTES, "barrier area");
+  static constexpr int LOG_OFFSET = 128;  // ProducerLog within the barrier area
+  static_assert((2 * STAGES + 5) * 8 + 8 <= LOG_OFFSET && LOG_OFFSET + sizeof(ProducerLog) <= BAR_BYTES,
+                "barrier area");
+  static_assert(STAGES >= kProducers, "ring slots");
 };
 
 template <int ACB>
@@ -944,6 +1064,7 @@ __global__ void __launch_bounds__(SwapCfg::THREADS, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  ProducerLog* plog = reinterpret_cast<ProducerLog*>(reinterpret_cast<uint8_t*>(bars) + S::LOG_OFFSET);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -961,13 +1082,14 @@ __global__ void __launch_bounds__(SwapCfg::THREADS, 1)
     }
     mbar_init(drain, 1);
     *abort_flag = 0u;
+    producer_log_init(plog);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmW);
   }
-  if (warp == 1) {
+  if (warp == S::MMA_WARP) {
     tmem_alloc(tmem_slot, S::TMEM_COLS);
     tmem_relinquish();
   }
@@ -977,14 +1099,17 @@ __global__ void __launch_bounds__(SwapCfg::THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   griddep_launch_dependents();
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------- TMA producer
-      uint32_t stage = 0, phase = 0;
-      int issued = 0;
+  if (warp < kProducerWarps) {
+    if (lane < kProducerLanes) {
+      // ------------------------------------------------------------- TMA producers
+      const int pr = warp * kProducerLanes + lane;
       bool ok = true;
       griddep_wait();  // the activations are the previous kernel's output
       constexpr int SUB = 128 / ACB;
+      constexpr int L = 1 + 2 * SUB;  // the filter block, then two 128-pixel halves per channel block
+      int it = 0;
+      int ring_stage = 0;
+      uint32_t ring_phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         // filter-origin coordinates of each 128-pixel half's first pixel
         int32_t cw[2], chh[2], cn[2];
@@ -998,87 +1123,99 @@ __global__ void __launch_bounds__(SwapCfg::THREADS, 1)
           cw[h] = ox * p.sw - p.pw;
           chh[h] = oy * p.sh - p.ph;
         }
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int stage = ring_stage;
+          const uint32_t phase = ring_phase;
+          if (++ring_stage == S::STAGES) {
+            ring_stage = 0;
+            ring_phase ^= 1u;
+          }
+          const int j0 = first_load_of(pr, it, L);
+          if (j0 >= L) continue;
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
-          tma_load_2d(&tmW, &full[stage], sW + stage * S::W_BYTES, kb * S::BK, 0);
+          if (j0 == 0) mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
           uint8_t* x_dst = sX + stage * S::X_BYTES;
-#pragma unroll
-          for (int i = 0; i < SUB; ++i) {
-            int j = kb * SUB + i;            // channel chunk index in (kh, kw, c) order
-            if (j >= p.total_chunks) j = 0;  // past the filter: weights are zero there
-            const int tap = j / p.chunks_per_tap;
-            const int c0 = (j - tap * p.chunks_per_tap) * ACB;
-            const int ky = tap / p.kw;
-            const int kx = tap - ky * p.kw;
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
+          for (int j = j0; j < L; j += kProducers) {
+            if (j == 0) {
+              tma_load_2d(&tmW, &full[stage], sW + stage * S::W_BYTES, kb * S::BK, 0);
+            } else {
+              const int i = (j - 1) >> 1, h = (j - 1) & 1;
+              int jc = kb * SUB + i;             // channel chunk index in (kh, kw, c) order
+              if (jc >= p.total_chunks) jc = 0;  // past the filter: weights are zero there
+              const int tap = jc / p.chunks_per_tap;
+              const int c0 = (jc - tap * p.chunks_per_tap) * ACB;
+              const int ky = tap / p.kw;
+              const int kx = tap - ky * p.kw;
               tma_load_im2col_4d(&tmX, &full[stage], x_dst + i * (S::BP * ACB) + h * (128 * ACB), c0, cw[h], chh[h],
                                  cn[h], static_cast<uint16_t>(kx * p.dw), static_cast<uint16_t>(ky * p.dh));
+            }
           }
-          ++issued;
-          if (++stage == S::STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          if (j0 == 0) plog->slot_it[stage] = it;
         }
       }
-      if (!ok) {
-        volatile uint32_t no_abort = 0;
-        const int outstanding = issued < S::STAGES ? issued : S::STAGES;
-        for (int i = 1; i <= outstanding; ++i) {
-          const int idx = issued - i;
-          mbar_wait(&full[idx % S::STAGES], static_cast<uint32_t>((idx / S::STAGES) & 1), &no_abort, p.err);
-        }
-      }
+      producer_leave(plog);
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------- MMA issuer
-      uint32_t stage = 0, phase = 0;
-      int local = 0;
-      bool ok = true, any_mma = false;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
-        const int buf = local & 1;
-        if (!mbar_wait(&tempty[buf], static_cast<uint32_t>((local >> 1) & 1) ^ 1u, abort_flag, p.err)) {
-          ok = false;
-          break;
-        }
+  } else if (warp == S::MMA_WARP) {
+    // ------------------------------------------------------------- MMA issuer (converged warp, one elected lane)
+    int it = 0;
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    bool ok = true, any_mma = false;
+    uint64_t w_kk[S::BK / 32], x_kk[S::BK / 32];
+#pragma unroll
+    for (int kk = 0; kk < S::BK / 32; ++kk) {
+      w_kk[kk] = smem_desc_sw128_kmajor(smem_u32(sW) + kk * 32);
+      x_kk[kk] = swap_x_desc<ACB>(smem_u32(sX), kk);
+    }
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&tempty[buf], static_cast<uint32_t>((local >> 1) & 1) ^ 1u, abort_flag,
+                                             p.err));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * S::BP);
+      for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&full[stage], phase, abort_flag, p.err));
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * S::BP);
-        for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t w0 = smem_u32(sW + stage * S::W_BYTES);
-          const uint32_t x0 = smem_u32(sX + stage * S::X_BYTES);
+        const uint64_t wo = static_cast<uint64_t>(stage * (S::W_BYTES >> 4));
+        const uint64_t xo = static_cast<uint64_t>(stage * (S::X_BYTES >> 4));
+        if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < S::BK / 32; ++kk)
-            mma_i8(d_tmem, smem_desc_sw128_kmajor(w0 + kk * 32), swap_x_desc<ACB>(x0, kk), S::IDESC,
-                   (kb | kk) != 0 ? 1u : 0u);
-          any_mma = true;
+            mma_i8(d_tmem, w_kk[kk] + wo, x_kk[kk] + xo, S::IDESC, (kb | kk) != 0 ? 1u : 0u);
           mma_commit(&empty[stage]);
-          if (++stage == S::STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
         }
-        if (ok) mma_commit(&tfull[buf]);
+        __syncwarp();
+        any_mma = true;
+        if (++stage == S::STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
-      if (!ok && any_mma) {
-        volatile uint32_t no_abort = 0;
-        mma_commit(drain);
-        mbar_wait(drain, 0u, &no_abort, p.err);
+      if (ok) {
+        if (elect_one()) mma_commit(&tfull[buf]);
+        __syncwarp();
       }
+    }
+    if (!ok) {
+      if (elect_one()) {
+        drain_in_flight(full, S::STAGES, it, plog, p.err, kWaitLimitNs);
+        if (any_mma) {
+          volatile uint32_t no_abort = 0;
+          mma_commit(drain);
+          mbar_wait(drain, 0u, &no_abort, p.err);
+        }
+      }
+      __syncwarp();
     }
   } else {
     // --------------------------------------------------------------- epilogue (one channel)
-    const int epi = warp - 2;
+    const int epi = warp - S::MMA_WARP - 1;
     const int quarter = warp & 3;  // TMEM lane quarter this warp may read
     const int part = epi >> 2;     // which 64 of the tile's 256 pixels
     const int ch = quarter * 32 + lane;
@@ -1173,7 +1310,7 @@ __global__ void __launch_bounds__(SwapCfg::THREADS, 1)
   }
 
   __syncthreads();
-  if (warp == 1) {
+  if (warp == S::MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::TMEM_COLS);
   }

@@ -322,10 +322,114 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
+// The same for im2col loads (the convolutions' A operand): an NHWC int8 tensor of 128
+// channels, 3x3 filter, padding 1, stride 1; load g brings the 128 output pixels from
+// (g * 128) mod (N*H*W) on, filter tap g mod 9, 128 channels: 16 KB.
+__global__ void __launch_bounds__(128, 1)
+    im2col_rate_probe_kernel(const __grid_constant__ CUtensorMap tm, int n, int h, int w, int depth, int iters,
+                             unsigned long long* cycles, unsigned long long* nanos, uint32_t* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTmaProbeSmemBytes);
+  volatile uint32_t* abort_flag = reinterpret_cast<uint32_t*>(full + kTmaProbeMaxSlots);
+  const int producers = blockDim.x >> 5;
+  const int pr = threadIdx.x >> 5;
+  constexpr uint32_t kBytes = 128u * 128u;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTmaProbeMaxSlots; ++i) mbar_init(&full[i], 1);
+    *abort_flag = 0u;
+    fence_barrier_init();
+    tma_prefetch_desc(&tm);
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) != 0) return;
+  uint64_t* my_full = full + pr * depth;
+  uint8_t* my_slots = smem + static_cast<size_t>(pr) * depth * kBytes;
+  const int pixels = n * h * w;
+  const int per = iters / producers;
+  bool ok = true;
+  const unsigned long long g0 = globaltimer_ns();
+  const long long c0 = clock64();
+  for (int i = 0; i < per + depth && ok; ++i) {
+    if (i >= depth) {
+      const int j = i - depth;
+      ok = mbar_wait(&my_full[j % depth], static_cast<uint32_t>((j / depth) & 1), abort_flag, err);
+    }
+    if (i < per) {
+      const int slot = i % depth;
+      const int g = (static_cast<int>(blockIdx.x) * per + i) * producers + pr;
+      const int m0 = static_cast<int>((static_cast<long long>(g) * 128) % pixels);
+      const int cn = m0 / (h * w);
+      const int rem = m0 - cn * h * w;
+      const int oy = rem / w, ox = rem - oy * w;
+      const int tap = g % 9;
+      mbar_arrive_expect_tx(&my_full[slot], kBytes);
+      tma_load_im2col_4d(&tm, &my_full[slot], my_slots + slot * kBytes, 0, ox - 1, oy - 1, cn,
+                         static_cast<uint16_t>(tap % 3), static_cast<uint16_t>(tap / 3));
+    }
+  }
+  const long long c1 = clock64();
+  const unsigned long long g1 = globaltimer_ns();
+  if (!ok) {
+    volatile uint32_t no_abort = 0;
+    for (int j = per > depth ? per - depth : 0; j < per; ++j)
+      mbar_wait(&my_full[j % depth], static_cast<uint32_t>((j / depth) & 1), &no_abort, err);
+  }
+  if (threadIdx.x == 0) {
+    cycles[blockIdx.x] = ok ? static_cast<unsigned long long>(c1 - c0) : 0ull;
+    nanos[blockIdx.x] = ok ? g1 - g0 : 0ull;
+  }
+}
+
 }  // namespace
 }  // namespace lsc
 
 using namespace lsc;
+
+extern "C" lsc_status lsc_probe_im2col_rate(const void* src, int64_t n, int64_t h, int64_t w, int32_t depth,
+                                            int32_t producers, int32_t iters, int32_t ctas, double* bytes_per_clock,
+                                            double* gbytes_per_s) {
+  if (!src || (reinterpret_cast<uintptr_t>(src) & 127) || n < 1 || h < 3 || w < 3 || n * h * w > (1 << 26) ||
+      depth < 1 || producers < 1 || producers > 4 || depth * producers > kTmaProbeMaxSlots ||
+      16384LL * depth * producers > kTmaProbeSmemBytes || iters < producers || iters > (1 << 20) || ctas < 1 ||
+      !bytes_per_clock || !gbytes_per_s)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "probe_im2col_rate: bad arguments");
+  DeviceState* ds = current_device_state();
+  if (!ds) return LSC_ERROR_DEVICE_ERROR;
+  if (ds->cc_major != 10) return set_error(LSC_ERROR_BACKEND_NOT_AVAILABLE, "probe_im2col_rate: needs sm_100");
+  const int units = ctas < ds->sm_count ? ctas : ds->sm_count;
+  const uint64_t dims[4] = {128, static_cast<uint64_t>(w), static_cast<uint64_t>(h), static_cast<uint64_t>(n)};
+  const uint64_t strides[3] = {128, static_cast<uint64_t>(w * 128), static_cast<uint64_t>(h * w * 128)};
+  const int lower[2] = {-1, -1};
+  const int upper[2] = {-1, -1};
+  const uint32_t estr[4] = {1, 1, 1, 1};
+  CUtensorMap tm;
+  lsc_status st = encode_tmap_im2col(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, src, dims, strides, lower, upper, 128, 128,
+                                     estr, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  const int smem = kTmaProbeSmemBytes + 1024 + 256;
+  LSC_CUDA_TRY(cudaFuncSetAttribute(im2col_rate_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  unsigned long long* buf = nullptr;
+  LSC_CUDA_TRY(cudaMalloc(&buf, 2 * sizeof(unsigned long long) * units));
+  im2col_rate_probe_kernel<<<units, 32 * producers, smem>>>(tm, static_cast<int>(n), static_cast<int>(h),
+                                                             static_cast<int>(w), depth, iters, buf, buf + units,
+                                                             ds->err_word);
+  cudaError_t e = cudaGetLastError();
+  std::vector<unsigned long long> hv(2 * units);
+  if (e == cudaSuccess) e = cudaMemcpy(hv.data(), buf, hv.size() * sizeof(hv[0]), cudaMemcpyDeviceToHost);
+  cudaFree(buf);
+  if (e != cudaSuccess) return cuda_error(e, "probe_im2col_rate");
+  std::vector<unsigned long long> c(hv.begin(), hv.begin() + units), t(hv.begin() + units, hv.end());
+  if (std::find(c.begin(), c.end(), 0ull) != c.end())
+    return set_error(LSC_ERROR_TIMEOUT, "probe_im2col_rate: a load wait ran out");
+  std::sort(c.begin(), c.end());
+  std::sort(t.begin(), t.end());
+  const double moved = static_cast<double>(iters / producers * producers) * 16384.0;
+  *bytes_per_clock = moved / static_cast<double>(c[units / 2]);
+  *gbytes_per_s = moved * units / static_cast<double>(t[units / 2]);
+  return LSC_SUCCESS;
+}
 
 extern "C" lsc_status lsc_probe_tma_rate(const void* src, uint64_t bytes, int64_t row_pitch, int32_t box_rows,
                                          int32_t chunks, int32_t depth, int32_t producers, int32_t same, int32_t iters,
