@@ -456,6 +456,52 @@ void lsc_session_destroy(lsc_session* session); /* LightShipSession_Destroy */
 lsc_status lsc_session_run(lsc_session* session, const lsc_tensor* inputs, uint32_t n_inputs,
                            lsc_tensor* outputs, uint32_t n_outputs, lsc_stream stream);
 
+/* ---- INT8 sessions ---------------------------------------------------------------------
+ * LightShipEngine_CreateSession (lightship.h:283-297) with the backend's precision choice.
+ * precision LSC_PRECISION_F32 is lsc_session_create.  LSC_PRECISION_INT8 compiles an ONNX CNN
+ * (Conv with BatchNormalization / Relu / Clip fused, residual Add(+Relu), MaxPool,
+ * GlobalAveragePool, Flatten / Reshape, a final Gemm / MatMul classifier; one f32 NCHW input
+ * of static shape) into the INT8 chain: per-output-channel INT8 filters with BN folded, the
+ * residual Add fused into the convolution that feeds it, per-tensor activation scales
+ * calibrated with find_scale_zp (quantization/helpers.rs:101-136) on `calibration` (an f32
+ * batch of the input's shape, host or device), int8 NHWC activations carved from one arena
+ * block by live range (plan_memory = 1) or one buffer each (0), and the whole network captured
+ * by the library as a CUDA graph, with a convolution that reads the same tensor as the one
+ * before it on a second stream (concurrent = 1).  The output is the classifier's f32 logits. */
+#define LSC_PRECISION_F32 0
+#define LSC_PRECISION_INT8 1
+typedef struct lsc_session_options {
+  int32_t precision;             /* LSC_PRECISION_* */
+  int32_t rounding;              /* INT8 requantize rounding LSC_ROUND_*, -1 = the backend's default */
+  int32_t concurrent;            /* 1 = independent sibling convolutions on a second stream */
+  int32_t plan_memory;           /* 1 = activations share one block by live range */
+  const lsc_tensor* calibration; /* INT8: the calibration batch */
+} lsc_session_options;
+lsc_status lsc_session_create_ex(lsc_backend* backend, const lsc_model* model, const lsc_session_options* options,
+                                 lsc_session** out);
+/* LightShipSession_Run, pipelined (INT8 sessions): enqueues one run on `stream` and returns.
+ * Host inputs are uploaded on the session's own copy stream into one of two input slots, so
+ * the next call's upload overlaps this call's network; the output is written when the stream
+ * reaches it (a host output should be pinned memory).  Host inputs must stay unchanged until
+ * the stream has passed this call.  Calls on one session must use one stream. */
+lsc_status lsc_session_run_async(lsc_session* session, const lsc_tensor* inputs, uint32_t n_inputs,
+                                 lsc_tensor* outputs, uint32_t n_outputs, lsc_stream stream);
+/* The device buffer behind input slot 0 (is_output = 0) or the output (1) of an INT8 session.
+ * An lsc_session_run whose input data is this buffer, or whose output data is the output
+ * buffer, copies nothing for it.  No counterpart in the reference (its tensors are host bytes). */
+lsc_status lsc_session_io_buffer(lsc_session* session, int32_t is_output, uint32_t index, void** device_ptr,
+                                 uint64_t* bytes);
+/* The INT8 session's activation memory: the planned block (peak, MemoryPlan::peak_memory in
+ * executor/plan.rs:67-118) against the sum of one buffer per activation (total_memory), and
+ * the number of activations. */
+lsc_status lsc_session_memory_plan(const lsc_session* session, uint64_t* planned_bytes, uint64_t* unplanned_bytes,
+                                   uint32_t* values);
+/* An INT8 session's activation `tensor_name` (an ONNX tensor name; the quantized input is the
+ * input's name + ":q"): its calibrated scale, its device buffer and an NHWC int8 description.
+ * With plan_memory = 1 the buffer may hold a later activation once the run has moved on. */
+lsc_status lsc_session_value(const lsc_session* session, const char* tensor_name, float* scale, void** device_ptr,
+                             lsc_tensor* desc);
+
 #ifdef __cplusplus
 }
 #endif

@@ -32,6 +32,7 @@ DTYPE_F32, DTYPE_F16 = 0, 1  # lsc_dtype
 ROUND_HALF_AWAY, ROUND_HALF_EVEN = 0, 1
 FP32_3XTF32, FP32_TF32 = 0, 1
 MEM_HOST, MEM_DEVICE = 0, 1
+PRECISION_F32, PRECISION_INT8 = 0, 1
 MAX_DIMS = 8
 
 
@@ -74,6 +75,11 @@ class lsc_op_desc(C.Structure):
                 ("bn_epsilon", C.c_float), ("output_scale", C.c_float), ("output_dtype", C.c_int32),
                 ("kernel_h", C.c_int32), ("kernel_w", C.c_int32),
                 ("pad_h_end_delta", C.c_int32), ("pad_w_end_delta", C.c_int32)]
+
+
+class lsc_session_options(C.Structure):
+    _fields_ = [("precision", C.c_int32), ("rounding", C.c_int32), ("concurrent", C.c_int32),
+                ("plan_memory", C.c_int32), ("calibration", C.POINTER(lsc_tensor))]
 
 
 class lsc_memory_block(C.Structure):
@@ -139,6 +145,11 @@ SIGNATURES = {
     "lsc_session_create": (ST, [P, P, C.POINTER(P)]),
     "lsc_session_destroy": (None, [P]),
     "lsc_session_run": (ST, [P, C.POINTER(lsc_tensor), C.c_uint32, C.POINTER(lsc_tensor), C.c_uint32, P]),
+    "lsc_session_create_ex": (ST, [P, P, C.POINTER(lsc_session_options), C.POINTER(P)]),
+    "lsc_session_run_async": (ST, [P, C.POINTER(lsc_tensor), C.c_uint32, C.POINTER(lsc_tensor), C.c_uint32, P]),
+    "lsc_session_io_buffer": (ST, [P, I32, C.c_uint32, C.POINTER(P), C.POINTER(C.c_uint64)]),
+    "lsc_session_memory_plan": (ST, [P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)]),
+    "lsc_session_value": (ST, [P, C.c_char_p, C.POINTER(C.c_float), C.POINTER(P), C.POINTER(lsc_tensor)]),
 }
 
 _lib = None

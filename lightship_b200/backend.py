@@ -396,12 +396,31 @@ class OnnxModel:
 
 class Session:
     """An inference session of an OnnxModel on a CudaBackend (LightShipEngine_CreateSession /
-    LightShipSession_Run, lightship.h:283-331)."""
+    LightShipSession_Run, lightship.h:283-331).
 
-    def __init__(self, backend: CudaBackend, model: OnnxModel):
+    ``precision="int8"`` compiles the model into the INT8 chain (``lsc_session_create_ex``):
+    activation scales calibrated on ``calibration`` (an f32 Tensor of the input's shape), int8
+    activations planned into one arena block by live range, the network captured by the
+    library as a CUDA graph with sibling convolutions on a second stream."""
+
+    def __init__(self, backend: CudaBackend, model: OnnxModel, precision: str = "f32",
+                 calibration: Optional[Tensor] = None, rounding: Optional[Rounding] = None,
+                 concurrent: bool = True, plan_memory: bool = True):
         h = C.c_void_p()
-        check(lib().lsc_session_create(backend._h, model._h, C.byref(h)))
+        if precision == "f32":
+            check(lib().lsc_session_create(backend._h, model._h, C.byref(h)))
+        elif precision == "int8":
+            if calibration is None:
+                raise ValueError("an INT8 session needs a calibration batch")
+            keep: list = []
+            cal = calibration._to_c(keep)
+            opts = _lib.lsc_session_options(_lib.PRECISION_INT8, -1 if rounding is None else int(rounding),
+                                            int(concurrent), int(plan_memory), C.pointer(cal))
+            check(lib().lsc_session_create_ex(backend._h, model._h, C.byref(opts), C.byref(h)))
+        else:
+            raise ValueError(f"unknown precision {precision!r}")
         self._h = h
+        self.precision = precision
         self._backend, self._model = backend, model  # both stay alive with the session
 
     def close(self):
@@ -416,13 +435,38 @@ class Session:
             pass
 
     def run(self, inputs: Sequence[Tensor], outputs: Sequence[Tensor], stream=None) -> None:
+        self._run(lib().lsc_session_run, inputs, outputs, stream)
+
+    def run_async(self, inputs: Sequence[Tensor], outputs: Sequence[Tensor], stream=None) -> None:
+        """Enqueues one run on ``stream`` (INT8 sessions; see ``lsc_session_run_async``)."""
+        self._run(lib().lsc_session_run_async, inputs, outputs, stream)
+
+    def _run(self, fn, inputs, outputs, stream):
         keep: list = []
         cin = (_lib.lsc_tensor * max(1, len(inputs)))(*[t._to_c(keep) for t in inputs])
         cout = (_lib.lsc_tensor * max(1, len(outputs)))(*[t._to_c(keep) for t in outputs])
         st = C.c_void_p(stream) if isinstance(stream, int) else stream
-        check(lib().lsc_session_run(self._h, cin, len(inputs), cout, len(outputs), st))
+        check(fn(self._h, cin, len(inputs), cout, len(outputs), st))
         for t, c in zip(outputs, cout):
             t.shape = [int(c.shape[i]) for i in range(c.ndim)]
+
+    def io_buffer(self, is_output: bool):
+        """(device pointer, bytes) of the INT8 session's input slot 0 or its output buffer."""
+        p, n = C.c_void_p(), C.c_uint64()
+        check(lib().lsc_session_io_buffer(self._h, int(is_output), 0, C.byref(p), C.byref(n)))
+        return p.value, n.value
+
+    def memory_plan(self) -> dict:
+        a, b, v = C.c_uint64(), C.c_uint64(), C.c_uint32()
+        check(lib().lsc_session_memory_plan(self._h, C.byref(a), C.byref(b), C.byref(v)))
+        return {"planned_bytes": a.value, "unplanned_bytes": b.value, "values": v.value}
+
+    def value(self, name: str) -> dict:
+        """An INT8 activation: its calibrated scale, device pointer and NHWC shape."""
+        sc, p, t = C.c_float(), C.c_void_p(), _lib.lsc_tensor()
+        check(lib().lsc_session_value(self._h, name.encode(), C.byref(sc), C.byref(p), C.byref(t)))
+        return {"scale": sc.value, "ptr": p.value, "shape": [int(t.shape[i]) for i in range(t.ndim)],
+                "nbytes": int(t.nbytes)}
 
 
 __all__ = ["DataType", "StorageLayout", "OperatorType", "FusionType", "FusionInfo", "Activation",

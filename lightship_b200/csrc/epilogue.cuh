@@ -28,15 +28,55 @@ __device__ __forceinline__ float act_relu6(float x) {
   return r;
 }
 
-// x / (1 + exp(-x)) with the reference's +-20 cut-offs.  exp is evaluated in double and
-// rounded once to f32, which gives the correctly rounded expf for all but a vanishing set
-// of inputs; the reference's expf is glibc's (error < 0.502 ulp).  The two are compared
-// over the whole [-20, 20] float range by the tests.
+// 2^(i/32) for the libm-equivalent expf below (bits, exponent field lowered by i/32).
+static __device__ const uint64_t kExpfTab[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+
+// expf as the host's libm computes it, so that SiLU matches Rust's f32::exp (which lowers to
+// the platform expf: glibc on Linux) bit for bit.  The method is the table-driven exp2f design
+// of Szabolcs Nagy in ARM's optimized-routines, which glibc (sysdeps/ieee754/flt-32/e_expf.c,
+// since 2.28) and musl use: with N = 32, k = round(x * N / ln2) (by adding 1.5 * 2^52),
+// r = x * N / ln2 - k in [-1/2, 1/2], exp(x) = 2^(k/N) * 2^(r/N) where 2^(k/N) is the table
+// entry 2^((k mod N)/N) with k/N added to its exponent, and 2^(r/N) ~ 1 + c2 r + c1 r^2 + c0 r^3,
+// all in double, rounded once to float.  The coefficients are the published polynomial
+// (ln2-based, scaled by 1/N^i); the table holds 2^(i/32) correctly rounded to double with
+// i * 2^52 / 32 subtracted from its bits.  Valid for |x| < 88 (SiLU needs |x| <= 20).
+// Checked on every float in [-20, 20] against glibc's expf (tests/expf_check.c), and on the
+// device through the SiLU operator against the oracle.
+__device__ __forceinline__ float expf_libm(float x) {
+  constexpr double kInvLn2N = 0x1.71547652b82fep+0 * 32;
+  constexpr double kShift = 0x1.8p+52;
+  constexpr double kC0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32;
+  constexpr double kC1 = 0x1.ebfce50fac4f3p-3 / 32 / 32;
+  constexpr double kC2 = 0x1.62e42ff0c52d6p-1 / 32;
+  const double xd = static_cast<double>(x);
+  const double kds = __fma_rn(kInvLn2N, xd, kShift);
+  const uint64_t ki = static_cast<uint64_t>(__double_as_longlong(kds));
+  const double kd = __dsub_rn(kds, kShift);
+  const double r = __fma_rn(kInvLn2N, xd, -kd);
+  const uint64_t t = __ldg(&kExpfTab[ki & 31u]) + (ki << 47);
+  const double s = __longlong_as_double(static_cast<long long>(t));
+  const double z = __fma_rn(kC0, r, kC1);
+  const double r2 = __dmul_rn(r, r);
+  const double y = __fma_rn(z, r2, __fma_rn(kC2, r, 1.0));
+  return __double2float_rn(__dmul_rn(y, s));
+}
+
+// x / (1 + exp(-x)) with the reference's +-20 cut-offs (silu.rs:47-61), exp as the host libm's.
+// A NaN input comes back as itself, quieted: the host's division returns its first operand's
+// NaN, while the device's would return the canonical NaN.
 __device__ __forceinline__ float act_silu(float x) {
+  if (x != x) return __uint_as_float(__float_as_uint(x) | 0x00400000u);
   if (x > 20.0f) return x;
   if (x < -20.0f) return 0.0f;
-  const float e = __double2float_rn(exp(-static_cast<double>(x)));
-  return __fdiv_rn(x, __fadd_rn(1.0f, e));
+  return __fdiv_rn(x, __fadd_rn(1.0f, expf_libm(-x)));
 }
 
 // RN(x / c) for the constants c = 3, 5, 7 and |x| < 2^17, without a division: q = RN(x * z),

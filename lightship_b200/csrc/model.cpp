@@ -27,6 +27,7 @@
 #include <math.h>
 #include <string.h>
 
+#include <algorithm>
 #include <map>
 #include <memory>
 #include <new>
@@ -574,9 +575,13 @@ lsc_tensor host_f32(const char* name, const std::vector<int64_t>& shape, const f
 
 }  // namespace
 
+struct QSession;                      // the INT8 session (below)
+void destroy_qsession(QSession* q);
+
 struct lsc_session {
   lsc_backend* be = nullptr;
   const lsc_model* model = nullptr;
+  QSession* q = nullptr;               // set for INT8 sessions
   std::map<std::string, int> ids;
   std::vector<Value> values;
   struct Step {
@@ -586,6 +591,7 @@ struct lsc_session {
   std::vector<Step> steps;
   std::vector<lsc_memory_block> blocks;
   ~lsc_session() {
+    destroy_qsession(q);
     for (auto& s : steps)
       if (s.op) lsc_op_destroy(s.op);
     for (auto& b : blocks) lsc_deallocate(be, &b);
@@ -792,6 +798,735 @@ lsc_status build_session(lsc_session& s, const lsc_model& m) {
 
 }  // namespace
 
+// ------------------------------------------------------------------------------ INT8 session
+// An ONNX CNN compiled into the INT8 chain (Engine::create_session with a quantized backend):
+//   lowering      Conv (+ folded BatchNorm, + ReLU / ReLU6) -> INT8 NHWC convolution with the
+//                 filter quantized per output channel; an Add (+ ReLU) whose one operand is a
+//                 convolution read by nothing else -> that convolution's fused residual
+//                 (FusionType::AddReLU, ir/fusion.rs:20); MaxPool -> int8 max pool (the max
+//                 commutes with the positive per-tensor scale); GlobalAveragePool -> int8
+//                 average pool; Flatten / Reshape -> views; Gemm / MatMul with a constant
+//                 weight -> INT8 FullyConnected with f32 output (the model's output).  The f32
+//                 NCHW graph input is quantized to int8 NHWC (channels stored as a multiple of
+//                 16); a first convolution of stride 2 over at most 4 channels runs as the
+//                 stride-1 convolution of the space-to-depth input (2 x 2 pixel blocks folded
+//                 into channels, the width rounded up to a multiple of 4 so it can run
+//                 pixel-grouped), which sums the same products.
+//   calibration   per-tensor symmetric scales (find_scale_zp, quantization/helpers.rs:101-136)
+//                 of the input and of every layer's dequantized f32 output on a calibration
+//                 batch, layer by layer, each layer then run again with its int8 output.
+//   memory plan   every int8 activation gets an offset in one arena block: values whose
+//                 live ranges (first write .. last read, in schedule order) overlap never share
+//                 bytes; largest first, lowest fitting offset (the reference's MemoryPlan,
+//                 executor/plan.rs:67-118, computes no offsets: scheduler.rs:196-226).
+//   schedule      node order, with a convolution that reads the same tensor as the one before
+//                 it (a ResNet block's downsample beside its first convolution) on a second
+//                 stream; its consumer waits for it (GraphExecutor::execute_parallel,
+//                 executor/graph_executor.rs:240-320, runs independent nodes concurrently).
+//   run           the schedule captured once as a CUDA graph per input slot (two slots, so
+//                 step i+1's input upload can overlap step i in lsc_session_run_async); the
+//                 kernels keep their programmatic dependent launches inside the graph.
+namespace {
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+struct QVal {
+  std::string name;
+  int64_t n = 0, h = 0, w = 0, c = 0;  // logical NHWC (c = the model's channels)
+  int64_t w_store = 0, c_store = 0;    // stored width / channels
+  float scale = 1.0f;
+  bool flat = false;                   // [n, c] (pooled / flattened)
+  int64_t offset = -1;                 // in the activation block
+  int def = -1, last = -1;             // schedule positions
+  int64_t bytes() const { return flat ? n * c_store : n * h * w_store * c_store; }
+};
+
+struct QStep {
+  enum Kind { kInput, kConv, kMaxPool, kAvgPool, kFc } kind = kConv;
+  int node = -1;           // model node index (the conv / pool / fc)
+  int in = -1, res = -1, out = -1;
+  int act = LSC_ACT_NONE;  // conv activation (after the residual)
+  bool side = false;       // runs on the second stream beside the step before it
+  int pos = 0;             // schedule position (liveness)
+  lsc_op* op = nullptr;
+  // stem (space-to-depth) geometry
+  bool s2d = false;
+  int64_t s2d_pad = 0, s2d_extra = 0;
+};
+
+}  // namespace
+
+struct QSession {
+  lsc_backend* be = nullptr;
+  int rounding = LSC_ROUND_HALF_AWAY;
+  bool concurrent = true;
+  bool plan_memory = true;
+  std::vector<QVal> vals;
+  std::vector<QStep> steps;
+  std::map<std::string, int> val_of;  // tensor name -> value id
+  std::vector<int64_t> in_shape;      // f32 NCHW
+  int64_t out_classes = 0;
+  float in_scale = 1.0f;
+  void* in_slot[2] = {nullptr, nullptr};
+  void* out_buf = nullptr;
+  void* act_block = nullptr;       // planned activations (plan_memory) ...
+  std::vector<void*> act_blocks;   // ... or one block per value
+  uint64_t planned_bytes = 0, unplanned_bytes = 0;
+  cudaStream_t cap_stream = nullptr, side_stream = nullptr, copy_stream = nullptr;
+  std::vector<cudaEvent_t> fork_ev, join_ev;
+  cudaEvent_t slot_loaded[2] = {nullptr, nullptr}, slot_free[2] = {nullptr, nullptr};
+  cudaGraphExec_t exec[2] = {nullptr, nullptr};
+  int next_slot = 0;
+  ~QSession() {
+    for (auto& e : exec)
+      if (e) cudaGraphExecDestroy(e);
+    for (auto e : fork_ev) cudaEventDestroy(e);
+    for (auto e : join_ev) cudaEventDestroy(e);
+    for (int k = 0; k < 2; ++k) {
+      if (slot_loaded[k]) cudaEventDestroy(slot_loaded[k]);
+      if (slot_free[k]) cudaEventDestroy(slot_free[k]);
+    }
+    if (cap_stream) cudaStreamDestroy(cap_stream);
+    if (side_stream) cudaStreamDestroy(side_stream);
+    if (copy_stream) cudaStreamDestroy(copy_stream);
+    for (auto& s : steps)
+      if (s.op) lsc_op_destroy(s.op);
+    if (be) {
+      for (void* p : {in_slot[0], in_slot[1], out_buf, act_block})
+        if (p) be->arena.free(p);
+      for (void* p : act_blocks) be->arena.free(p);
+    }
+  }
+  void* ptr(int v) const {
+    return plan_memory ? static_cast<char*>(act_block) + vals[v].offset : act_blocks[v];
+  }
+};
+
+namespace {
+
+lsc_tensor q_tensor(const QVal& v, void* data, float* scale_slot) {
+  lsc_tensor t{};
+  t.name = v.name.c_str();
+  if (v.flat) {
+    t.ndim = 2;
+    t.shape[0] = v.n;
+    t.shape[1] = v.c_store;
+  } else {
+    t.ndim = 4;
+    t.shape[0] = v.n;
+    t.shape[1] = v.h;
+    t.shape[2] = v.w_store;
+    t.shape[3] = v.c_store;
+  }
+  t.dtype = LSC_DTYPE_QINT8;
+  t.layout = LSC_LAYOUT_NHWC;
+  t.location = LSC_MEM_DEVICE;
+  t.data = data;
+  t.nbytes = static_cast<uint64_t>(v.bytes());
+  *scale_slot = v.scale;
+  t.quant.scale = scale_slot;
+  t.quant.count = 1;
+  t.quant.bit_width = 8;
+  return t;
+}
+
+lsc_tensor f32_dev(const char* name, std::initializer_list<int64_t> shape, void* data) {
+  lsc_tensor t{};
+  t.name = name;
+  t.ndim = 0;
+  uint64_t n = 1;
+  for (auto d : shape) {
+    t.shape[t.ndim++] = d;
+    n *= static_cast<uint64_t>(d);
+  }
+  t.dtype = LSC_DTYPE_F32;
+  t.layout = LSC_LAYOUT_NCHW;
+  t.location = LSC_MEM_DEVICE;
+  t.data = data;
+  t.nbytes = n * 4;
+  return t;
+}
+
+// The filter of a stride-2 convolution re-expressed over the space-to-depth input: tap
+// (r, s) = (2a + dy, 2b + dx) of the k x k filter moves to tap (a, b), channel (dy*2 + dx)*C + c
+// of a ceil(k/2) x ceil(k/2) filter; taps past k are zero.
+std::vector<float> s2d_filter(const std::vector<float>& w, int64_t co, int64_t c, int64_t k) {
+  const int64_t kk = (k + 1) / 2;
+  std::vector<float> w2(static_cast<size_t>(co * 4 * c * kk * kk), 0.0f);
+  for (int64_t o = 0; o < co; ++o)
+    for (int64_t dy = 0; dy < 2; ++dy)
+      for (int64_t dx = 0; dx < 2; ++dx)
+        for (int64_t a = 0; a < kk; ++a)
+          for (int64_t b = 0; b < kk; ++b) {
+            const int64_t r = 2 * a + dy, s = 2 * b + dx;
+            if (r >= k || s >= k) continue;
+            for (int64_t ci = 0; ci < c; ++ci)
+              w2[static_cast<size_t>(((o * 4 * c + (dy * 2 + dx) * c + ci) * kk + a) * kk + b)] =
+                  w[static_cast<size_t>(((o * c + ci) * k + r) * k + s)];
+          }
+  return w2;
+}
+
+// Lowers the fused graph to INT8 steps (shapes only; operators are compiled at calibration).
+lsc_status lower_int8(QSession& q, const lsc_model& m) {
+  if (m.inputs.size() != 1 || m.outputs.size() != 1)
+    return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: one graph input and one output expected");
+  const GraphIO& gi = m.inputs[0];
+  if (gi.dtype != LSC_DTYPE_F32 || gi.shape.size() != 4)
+    return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "INT8 session: the input must be f32 NCHW");
+  for (auto d : gi.shape)
+    if (d <= 0) return set_error(LSC_ERROR_SHAPE_MISMATCH, "INT8 session: the input needs static dimensions");
+  q.in_shape = gi.shape;
+  const int64_t N = gi.shape[0];
+  std::map<std::string, int> alias;  // view tensor -> value id
+  auto find = [&](const std::string& t) -> int {
+    auto a = alias.find(t);
+    if (a != alias.end()) return a->second;
+    auto it = q.val_of.find(t);
+    return it == q.val_of.end() ? -1 : it->second;
+  };
+  auto add_val = [&](const std::string& name, int64_t h, int64_t w, int64_t c) -> int {
+    QVal v;
+    v.name = name;
+    v.n = N;
+    v.h = h;
+    v.w = w;
+    v.c = c;
+    v.w_store = w;
+    v.c_store = c;  // layer outputs are stored as computed; the quantized input is padded below
+    q.vals.push_back(v);
+    const int id = static_cast<int>(q.vals.size()) - 1;
+    q.val_of[name] = id;
+    return id;
+  };
+  // how many nodes read a tensor
+  auto readers = [&](const std::string& t) {
+    int c = 0;
+    for (const auto& n : m.nodes)
+      for (const auto& x : n.in)
+        if (x == t) ++c;
+    for (const auto& o : m.outputs)
+      if (o.name == t) ++c;
+    return c;
+  };
+  std::set<size_t> absorbed;  // Add nodes fused into a convolution
+  bool input_quantized = false;
+  bool have_fc = false;
+  for (size_t k = 0; k < m.nodes.size(); ++k) {
+    if (absorbed.count(k)) continue;
+    const Node& n = m.nodes[k];
+    const lsc_op_desc& d = m.descs[k];
+    if (have_fc) return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: node '%s' after the classifier", n.name.c_str());
+    if (d.op_type == -1) {  // Flatten / Reshape of a pooled [N, C(,1,1)] tensor
+      const int src = find(n.in[0]);
+      if (src < 0) return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: view '%s' of an unknown tensor", n.name.c_str());
+      if (!q.vals[src].flat)
+        return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: only pooled tensors can be reshaped ('%s')", n.name.c_str());
+      alias[n.out[0]] = src;
+      continue;
+    }
+    QStep st;
+    st.node = static_cast<int>(k);
+    if (d.op_type == LSC_OP_CONV2D) {
+      if (d.groups != 1 && d.groups != 0)
+        return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: grouped Conv '%s'", n.name.c_str());
+      const OnnxTensor& wt = m.inits.at(n.in[1]);
+      const int64_t co = wt.dims[0], ci = wt.dims[1], kh = wt.dims[2], kw = wt.dims[3];
+      int in = -1;
+      if (n.in[0] == gi.name) {
+        if (input_quantized) return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: the input feeds two nodes");
+        input_quantized = true;
+        QStep qs;
+        qs.kind = QStep::kInput;
+        const int64_t H = gi.shape[2], W = gi.shape[3], C = gi.shape[1];
+        const int64_t p = d.pad_h;
+        const bool s2d = d.stride_h == 2 && d.stride_w == 2 && kh == kw && d.pad_w == p && C <= 4 &&
+                         d.dilation_h == 1 && d.dilation_w == 1 && (H + 2 * p) % 2 == 0 && (W + 2 * p) % 2 == 0 &&
+                         d.pad_h_end_delta == 0 && d.pad_w_end_delta == 0 &&
+                         (H + 2 * p - kh) / 2 + 1 == (H + 2 * p) / 2 - (kh + 1) / 2 + 1 &&
+                         (W + 2 * p - kw) / 2 + 1 == (W + 2 * p) / 2 - (kw + 1) / 2 + 1;
+        if (s2d) {
+          const int64_t hs = (H + 2 * p) / 2, ws = (W + 2 * p) / 2;
+          const int x = add_val(gi.name + ":q", hs, ws, 4 * C);
+          q.vals[x].w_store = round_up(ws, 4);
+          q.vals[x].c_store = 16;
+          qs.s2d = st.s2d = true;
+          qs.s2d_pad = st.s2d_pad = p;
+          qs.s2d_extra = st.s2d_extra = q.vals[x].w_store - ws;
+          qs.out = x;
+        } else {
+          qs.out = add_val(gi.name + ":q", H, W, C);
+          q.vals[qs.out].c_store = round_up(C, 16);
+        }
+        q.steps.push_back(qs);
+        in = qs.out;
+      } else {
+        in = find(n.in[0]);
+        if (in < 0) return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: Conv '%s' reads an unknown tensor", n.name.c_str());
+      }
+      const QVal& x = q.vals[in];
+      if (!st.s2d && x.c != ci)
+        return set_error(LSC_ERROR_SHAPE_MISMATCH, "INT8 session: Conv '%s' expects %lld channels", n.name.c_str(), (long long)ci);
+      if (x.flat || x.c_store % 16 != 0)
+        return set_error(LSC_ERROR_UNSUPPORTED_LAYOUT,
+                         "INT8 session: Conv '%s' reads %lld channels; int8 activations need a multiple of 16",
+                         n.name.c_str(), (long long)x.c_store);
+      int64_t oh, ow;
+      if (st.s2d) {
+        oh = x.h - (kh + 1) / 2 + 1;
+        ow = x.w - (kw + 1) / 2 + 1;
+      } else {
+        oh = (x.h + 2 * d.pad_h + d.pad_h_end_delta - d.dilation_h * (kh - 1) - 1) / d.stride_h + 1;
+        ow = (x.w + 2 * d.pad_w + d.pad_w_end_delta - d.dilation_w * (kw - 1) - 1) / d.stride_w + 1;
+      }
+      st.kind = QStep::kConv;
+      st.in = in;
+      st.act = d.activation;
+      std::string out_name = n.out[0];
+      // a following Add (+ ReLU) that only this convolution feeds becomes its residual
+      if (readers(n.out[0]) == 1 && d.activation == LSC_ACT_NONE) {
+        for (size_t j = k + 1; j < m.nodes.size(); ++j) {
+          const Node& a = m.nodes[j];
+          if (m.descs[j].op_type != LSC_OP_ADD) {
+            bool reads = false;
+            for (const auto& t : a.in) reads |= t == n.out[0];
+            if (reads) break;
+            continue;
+          }
+          if (a.in.size() != 2 || (a.in[0] != n.out[0] && a.in[1] != n.out[0])) continue;
+          const std::string& other = a.in[0] == n.out[0] ? a.in[1] : a.in[0];
+          const int r = find(other);
+          if (r < 0 || q.vals[r].flat || q.vals[r].h != oh || q.vals[r].w != ow || q.vals[r].c != co) break;
+          st.res = r;
+          // Add + Relu arrives as FusionType::AddReLU (or an explicit activation)
+          st.act = m.descs[j].fusion == LSC_FUSION_ADD_RELU ? LSC_ACT_RELU : m.descs[j].activation;
+          out_name = a.out[0];
+          absorbed.insert(j);
+          break;
+        }
+      }
+      st.out = add_val(out_name, oh, ow, co);
+      q.steps.push_back(st);
+      continue;
+    }
+    if (d.op_type == LSC_OP_MAXPOOL2D) {
+      const int in = find(n.in[0]);
+      if (in < 0 || q.vals[in].flat) return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: MaxPool '%s' input", n.name.c_str());
+      const QVal& x = q.vals[in];
+      st.kind = QStep::kMaxPool;
+      st.in = in;
+      st.out = add_val(n.out[0], (x.h + 2 * d.pad_h - d.kernel_h) / d.stride_h + 1,
+                       (x.w + 2 * d.pad_w - d.kernel_w) / d.stride_w + 1, x.c);
+      q.steps.push_back(st);
+      continue;
+    }
+    if (d.op_type == LSC_OP_GLOBAL_AVGPOOL2D) {
+      const int in = find(n.in[0]);
+      if (in < 0 || q.vals[in].flat) return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: GlobalAveragePool '%s' input", n.name.c_str());
+      st.kind = QStep::kAvgPool;
+      st.in = in;
+      st.out = add_val(n.out[0], 1, 1, q.vals[in].c);
+      q.vals[st.out].flat = true;
+      q.steps.push_back(st);
+      continue;
+    }
+    if (d.op_type == LSC_OP_FULLY_CONNECTED) {
+      const int in = find(n.in[0]);
+      if (in < 0 || !q.vals[in].flat) return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: FullyConnected '%s' needs a pooled input", n.name.c_str());
+      if (n.out[0] != m.outputs[0].name)
+        return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: the classifier '%s' must produce the graph output", n.name.c_str());
+      st.kind = QStep::kFc;
+      st.in = in;
+      have_fc = true;
+      q.steps.push_back(st);
+      continue;
+    }
+    return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: operator %s ('%s') has no INT8 lowering",
+                     n.op.c_str(), n.name.c_str());
+  }
+  if (!have_fc) return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: the graph must end in a Gemm / MatMul classifier");
+  return LSC_SUCCESS;
+}
+
+// Schedule positions, second-stream steps and each value's live range.
+void schedule_int8(QSession& q) {
+  int pos = 0;
+  int prev_conv_in = -1;
+  for (size_t i = 0; i < q.steps.size(); ++i) {
+    QStep& s = q.steps[i];
+    s.side = false;
+    // a convolution reading the same tensor as the convolution just before it runs beside it
+    if (q.concurrent && s.kind == QStep::kConv && i > 0 && q.steps[i - 1].kind == QStep::kConv &&
+        !q.steps[i - 1].side && s.in == prev_conv_in && s.res < 0) {
+      s.side = true;
+      s.pos = q.steps[i - 1].pos;
+    } else {
+      s.pos = ++pos;
+    }
+    prev_conv_in = s.kind == QStep::kConv ? s.in : -1;
+  }
+  for (auto& v : q.vals) v.def = v.last = -1;
+  for (auto& s : q.steps) {
+    if (s.out >= 0) q.vals[s.out].def = s.pos;
+    for (int r : {s.in, s.res})
+      if (r >= 0) q.vals[r].last = std::max(q.vals[r].last, s.pos);
+  }
+  for (auto& v : q.vals)
+    if (v.last < v.def) v.last = v.def;
+}
+
+// Offsets in one block: largest first, lowest offset clear of every placed value whose live
+// range overlaps.
+uint64_t plan_offsets(QSession& q) {
+  std::vector<int> order(q.vals.size());
+  for (size_t i = 0; i < order.size(); ++i) order[i] = static_cast<int>(i);
+  std::sort(order.begin(), order.end(), [&](int a, int b) { return q.vals[a].bytes() > q.vals[b].bytes(); });
+  std::vector<int> placed;
+  uint64_t total = 0;
+  for (int id : order) {
+    QVal& v = q.vals[id];
+    const int64_t size = round_up(v.bytes(), 256);
+    std::vector<std::pair<int64_t, int64_t>> busy;
+    for (int p : placed) {
+      const QVal& u = q.vals[p];
+      if (u.def <= v.last && v.def <= u.last) busy.emplace_back(u.offset, u.offset + round_up(u.bytes(), 256));
+    }
+    std::sort(busy.begin(), busy.end());
+    int64_t off = 0;
+    for (const auto& b : busy) {
+      if (off + size <= b.first) break;
+      off = std::max(off, b.second);
+    }
+    v.offset = off;
+    placed.push_back(id);
+    total = std::max<uint64_t>(total, static_cast<uint64_t>(off + size));
+  }
+  return total;
+}
+
+// find_scale_zp (symmetric, QInt8) of a device f32 array, read back to the host.
+lsc_status calibrate_scale(lsc_backend* be, const float* x, int64_t n, cudaStream_t st, float* scale) {
+  lsc_memory_block b{};
+  lsc_status s = lsc_allocate(be, 64, 256, &b);
+  if (s) return s;
+  char* base = static_cast<char*>(b.ptr);
+  s = lsc::launch_find_scale_zp(x, n, LSC_DTYPE_QINT8, 1, base, 16, reinterpret_cast<float*>(base + 16),
+                                reinterpret_cast<int32_t*>(base + 32), st);
+  if (!s) {
+    cudaError_t e = cudaMemcpyAsync(scale, base + 16, 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) s = lsc::cuda_error(e, "calibration scale");
+  }
+  lsc_deallocate(be, &b);
+  return s;
+}
+
+// Compiles every step with the calibrated scales, running the calibration batch through
+// the network layer by layer (`x` device f32 NCHW of the input shape).
+lsc_status calibrate_int8(QSession& q, const lsc_model& m, const float* x, cudaStream_t st) {
+  lsc_backend* be = q.be;
+  const int64_t in_count = count_of(q.in_shape);
+  lsc_status s = calibrate_scale(be, x, in_count, st, &q.in_scale);
+  if (s) return s;
+  int64_t scratch_elems = 0;
+  for (const auto& v : q.vals) scratch_elems = std::max(scratch_elems, v.n * v.h * v.w * v.c_store);
+  scratch_elems = std::max(scratch_elems, q.in_shape[0] * 4096);
+  lsc_memory_block sb{};
+  if ((s = lsc_allocate(be, static_cast<uint64_t>(scratch_elems) * 4, 256, &sb))) return s;
+  float* scratch = static_cast<float*>(sb.ptr);
+  auto fail = [&](lsc_status e) {
+    lsc_deallocate(be, &sb);
+    return e;
+  };
+  float sc_a = 0.0f, sc_b = 0.0f, sc_c = 0.0f;
+  for (auto& stp : q.steps) {
+    const Node* n = stp.node >= 0 ? &m.nodes[stp.node] : nullptr;
+    if (stp.kind == QStep::kInput) {
+      QVal& o = q.vals[stp.out];
+      o.scale = q.in_scale;
+      lsc_op_desc d = base_desc(LSC_OP_QUANTIZE);
+      d.rounding = q.rounding;
+      if (stp.s2d) {
+        d.stride_h = d.stride_w = 2;
+        d.pad_h = d.pad_w = static_cast<int32_t>(stp.s2d_pad);
+        d.pad_w_end_delta = static_cast<int32_t>(2 * stp.s2d_extra);
+      }
+      lsc_tensor xi = f32_dev("input", {q.in_shape[0], q.in_shape[1], q.in_shape[2], q.in_shape[3]},
+                              const_cast<float*>(x));
+      lsc_tensor xo = q_tensor(o, q.ptr(stp.out), &sc_a);
+      if ((s = lsc_compile_operator(be, &d, &xi, 1, &xo, 1, &stp.op))) return fail(s);
+      if ((s = lsc_execute(be, stp.op, &xi, 1, &xo, 1, st))) return fail(s);
+      continue;
+    }
+    if (stp.kind == QStep::kConv) {
+      const QVal& xv = q.vals[stp.in];
+      QVal& ov = q.vals[stp.out];
+      const OnnxTensor& wt = m.inits.at(n->in[1]);
+      const int64_t co = wt.dims[0], ci = wt.dims[1], kh = wt.dims[2];
+      lsc_op_desc d = m.descs[stp.node];
+      d.activation = stp.act;
+      d.rounding = q.rounding;
+      d.output_dtype = LSC_DTYPE_QINT8;
+      d.output_scale = 1.0f;
+      std::vector<float> w2;
+      std::vector<int64_t> wshape = wt.dims;
+      const float* wdata = wt.f.data();
+      if (stp.s2d) {
+        w2 = s2d_filter(wt.f, co, ci, kh);
+        const int64_t kk = (kh + 1) / 2;
+        wshape = {co, 4 * ci, kk, kk};
+        wdata = w2.data();
+        d.stride_h = d.stride_w = 1;
+        d.pad_h = d.pad_w = 0;
+        d.pad_h_end_delta = 0;
+        d.pad_w_end_delta = -static_cast<int32_t>(stp.s2d_extra);
+      }
+      std::vector<lsc_tensor> cin;
+      cin.push_back(q_tensor(xv, q.ptr(stp.in), &sc_a));
+      cin.push_back(host_f32(n->in[1].c_str(), wshape, wdata));
+      std::vector<float> zero_bias;
+      if (n->in.size() > 2 && !n->in[2].empty()) {
+        const OnnxTensor& bt = m.inits.at(n->in[2]);
+        cin.push_back(host_f32(n->in[2].c_str(), bt.dims, bt.f.data()));
+      } else {
+        zero_bias.assign(static_cast<size_t>(co), 0.0f);
+        cin.push_back(host_f32("bias", {co}, zero_bias.data()));
+      }
+      for (const auto& b : n->bn) {
+        const OnnxTensor& t = m.inits.at(b);
+        cin.push_back(host_f32(b.c_str(), t.dims, t.f.data()));
+      }
+      lsc_tensor yo = q_tensor(ov, q.ptr(stp.out), &sc_b);
+      if ((s = lsc_compile_operator(be, &d, cin.data(), static_cast<int32_t>(cin.size()), &yo, 1, &stp.op)))
+        return fail(s);
+      std::vector<lsc_tensor> ein{q_tensor(xv, q.ptr(stp.in), &sc_a)};
+      if (stp.res >= 0) ein.push_back(q_tensor(q.vals[stp.res], q.ptr(stp.res), &sc_c));
+      lsc_tensor yf = f32_dev(ov.name.c_str(), {ov.n, ov.h, ov.w, ov.c_store}, scratch);
+      yf.layout = LSC_LAYOUT_NHWC;
+      if ((s = lsc_execute(be, stp.op, ein.data(), static_cast<int32_t>(ein.size()), &yf, 1, st))) return fail(s);
+      if ((s = calibrate_scale(be, scratch, ov.n * ov.h * ov.w * ov.c_store, st, &ov.scale))) return fail(s);
+      yo = q_tensor(ov, q.ptr(stp.out), &sc_b);
+      if ((s = lsc_execute(be, stp.op, ein.data(), static_cast<int32_t>(ein.size()), &yo, 1, st))) return fail(s);
+      continue;
+    }
+    if (stp.kind == QStep::kMaxPool) {
+      const QVal& xv = q.vals[stp.in];
+      QVal& ov = q.vals[stp.out];
+      ov.scale = xv.scale;
+      lsc_op_desc d = m.descs[stp.node];
+      lsc_tensor xi = q_tensor(xv, q.ptr(stp.in), &sc_a);
+      lsc_tensor xo = q_tensor(ov, q.ptr(stp.out), &sc_b);
+      if ((s = lsc_compile_operator(be, &d, &xi, 1, &xo, 1, &stp.op))) return fail(s);
+      if ((s = lsc_execute(be, stp.op, &xi, 1, &xo, 1, st))) return fail(s);
+      continue;
+    }
+    if (stp.kind == QStep::kAvgPool) {
+      const QVal& xv = q.vals[stp.in];
+      QVal& ov = q.vals[stp.out];
+      lsc_op_desc d = m.descs[stp.node];
+      d.rounding = q.rounding;
+      d.output_scale = 1.0f;
+      lsc_tensor xi = q_tensor(xv, q.ptr(stp.in), &sc_a);
+      lsc_tensor yf = f32_dev(ov.name.c_str(), {ov.n, ov.c_store}, scratch);
+      if ((s = lsc_compile_operator(be, &d, &xi, 1, &yf, 1, &stp.op))) return fail(s);
+      if ((s = lsc_execute(be, stp.op, &xi, 1, &yf, 1, st))) return fail(s);
+      if ((s = calibrate_scale(be, scratch, ov.n * ov.c_store, st, &ov.scale))) return fail(s);
+      lsc_tensor yo = q_tensor(ov, q.ptr(stp.out), &sc_b);
+      if ((s = lsc_execute(be, stp.op, &xi, 1, &yo, 1, st))) return fail(s);
+      continue;
+    }
+    // kFc: INT8 FullyConnected, f32 logits (Gemm transB = 1 keeps W as [N, K])
+    const QVal& xv = q.vals[stp.in];
+    const OnnxTensor& wt = m.inits.at(n->in[1]);
+    const bool trans_b = n->op == "Gemm" && n->attr_i("transB", 0) != 0;
+    const int64_t kdim = trans_b ? wt.dims[1] : wt.dims[0], ndim = trans_b ? wt.dims[0] : wt.dims[1];
+    if (kdim != xv.c) return fail(set_error(LSC_ERROR_SHAPE_MISMATCH, "INT8 session: classifier K mismatch"));
+    std::vector<float> wnk;
+    const float* wdata = wt.f.data();
+    if (!trans_b) {
+      wnk.resize(static_cast<size_t>(kdim * ndim));
+      for (int64_t a = 0; a < kdim; ++a)
+        for (int64_t b = 0; b < ndim; ++b) wnk[static_cast<size_t>(b * kdim + a)] = wt.f[static_cast<size_t>(a * ndim + b)];
+      wdata = wnk.data();
+    }
+    std::vector<float> zero_bias(static_cast<size_t>(ndim), 0.0f);
+    const float* bdata = zero_bias.data();
+    if (n->in.size() > 2 && !n->in[2].empty()) bdata = m.inits.at(n->in[2]).f.data();
+    lsc_op_desc d = base_desc(LSC_OP_FULLY_CONNECTED);
+    d.rounding = q.rounding;
+    QVal xin = xv;
+    xin.c_store = xv.c;  // the FC reads [N, K]: K = the pooled channels (multiple of 16 here)
+    if (xv.c_store != xv.c) return fail(set_error(LSC_ERROR_UNSUPPORTED_LAYOUT, "INT8 session: classifier input channels must be a multiple of 16"));
+    lsc_tensor cin[3] = {q_tensor(xin, q.ptr(stp.in), &sc_a), host_f32("fc.w", {ndim, kdim}, wdata),
+                         host_f32("fc.b", {ndim}, bdata)};
+    lsc_tensor yo = f32_dev("logits", {xv.n, ndim}, q.out_buf);
+    if ((s = lsc_compile_operator(be, &d, cin, 3, &yo, 1, &stp.op))) return fail(s);
+    if ((s = lsc_execute(be, stp.op, cin, 1, &yo, 1, st))) return fail(s);
+    q.out_classes = ndim;
+  }
+  lsc_deallocate(be, &sb);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return lsc::cuda_error(e, "INT8 session calibration");
+  return LSC_SUCCESS;
+}
+
+// Launches every step on `main` (and the side stream) reading the input from `in`.  A side
+// step forks from `main` before the step it runs beside, so both start from the same point,
+// and the next step joins it.
+lsc_status enqueue_int8(QSession& q, const float* in, cudaStream_t main) {
+  float sc_a = 0.0f, sc_b = 0.0f, sc_c = 0.0f;
+  size_t fork_i = 0, join_i = 0;
+  bool side_open = false;
+  for (size_t i = 0; i < q.steps.size(); ++i) {
+    QStep& stp = q.steps[i];
+    lsc_status s;
+    if (side_open && !stp.side) {
+      LSC_CUDA_TRY(cudaEventRecord(q.join_ev[join_i], q.side_stream));
+      LSC_CUDA_TRY(cudaStreamWaitEvent(main, q.join_ev[join_i], 0));
+      ++join_i;
+      side_open = false;
+    }
+    if (i + 1 < q.steps.size() && q.steps[i + 1].side) {
+      LSC_CUDA_TRY(cudaEventRecord(q.fork_ev[fork_i], main));
+      LSC_CUDA_TRY(cudaStreamWaitEvent(q.side_stream, q.fork_ev[fork_i], 0));
+      ++fork_i;
+    }
+    cudaStream_t st = stp.side ? q.side_stream : main;
+    side_open |= stp.side;
+    if (stp.kind == QStep::kInput) {
+      lsc_tensor xi = f32_dev("input", {q.in_shape[0], q.in_shape[1], q.in_shape[2], q.in_shape[3]}, const_cast<float*>(in));
+      lsc_tensor xo = q_tensor(q.vals[stp.out], q.ptr(stp.out), &sc_b);
+      if ((s = lsc_execute(q.be, stp.op, &xi, 1, &xo, 1, st))) return s;
+      continue;
+    }
+    lsc_tensor xi = q_tensor(q.vals[stp.in], q.ptr(stp.in), &sc_a);
+    if (stp.kind == QStep::kFc) {
+      lsc_tensor yo = f32_dev("logits", {q.vals[stp.in].n, q.out_classes}, q.out_buf);
+      if ((s = lsc_execute(q.be, stp.op, &xi, 1, &yo, 1, st))) return s;
+      continue;
+    }
+    lsc_tensor yo = q_tensor(q.vals[stp.out], q.ptr(stp.out), &sc_b);
+    if (stp.kind == QStep::kConv && stp.res >= 0) {
+      lsc_tensor ins[2] = {xi, q_tensor(q.vals[stp.res], q.ptr(stp.res), &sc_c)};
+      if ((s = lsc_execute(q.be, stp.op, ins, 2, &yo, 1, st))) return s;
+    } else {
+      if ((s = lsc_execute(q.be, stp.op, &xi, 1, &yo, 1, st))) return s;
+    }
+  }
+  if (side_open) {
+    LSC_CUDA_TRY(cudaEventRecord(q.join_ev[join_i], q.side_stream));
+    LSC_CUDA_TRY(cudaStreamWaitEvent(main, q.join_ev[join_i], 0));
+  }
+  return LSC_SUCCESS;
+}
+
+lsc_status capture_int8(QSession& q) {
+  size_t sides = 0;
+  for (const auto& s : q.steps) sides += s.side ? 1 : 0;
+  q.fork_ev.resize(sides);
+  q.join_ev.resize(sides + 1);
+  for (auto& e : q.fork_ev) LSC_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  for (auto& e : q.join_ev) LSC_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  for (int k = 0; k < 2; ++k) {
+    LSC_CUDA_TRY(cudaStreamBeginCapture(q.cap_stream, cudaStreamCaptureModeThreadLocal));
+    lsc_status s = enqueue_int8(q, static_cast<const float*>(q.in_slot[k]), q.cap_stream);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(q.cap_stream, &g);
+    if (s) {
+      if (g) cudaGraphDestroy(g);
+      return s;
+    }
+    if (e != cudaSuccess) return lsc::cuda_error(e, "INT8 session graph capture");
+    e = cudaGraphInstantiate(&q.exec[k], g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return lsc::cuda_error(e, "INT8 session graph instantiation");
+  }
+  return LSC_SUCCESS;
+}
+
+lsc_status build_int8(QSession& q, const lsc_model& m, const lsc_tensor* calib) {
+  lsc_status s = lower_int8(q, m);
+  if (s) return s;
+  schedule_int8(q);
+  uint64_t separate = 0;
+  for (const auto& v : q.vals) separate += static_cast<uint64_t>(round_up(v.bytes(), 256));
+  q.unplanned_bytes = separate;
+  if (q.plan_memory) {
+    q.planned_bytes = plan_offsets(q);
+    q.act_block = q.be->arena.alloc(q.planned_bytes, 256);
+    if (!q.act_block) return set_error(LSC_ERROR_OUT_OF_MEMORY, "INT8 session: no arena room for %llu activation bytes",
+                                       (unsigned long long)q.planned_bytes);
+  } else {
+    q.planned_bytes = separate;
+    for (const auto& v : q.vals) {
+      void* p = q.be->arena.alloc(static_cast<size_t>(round_up(v.bytes(), 256)), 256);
+      if (!p) return set_error(LSC_ERROR_OUT_OF_MEMORY, "INT8 session: no arena room for '%s'", v.name.c_str());
+      q.act_blocks.push_back(p);
+    }
+  }
+  const uint64_t in_bytes = static_cast<uint64_t>(count_of(q.in_shape)) * 4;
+  for (int k = 0; k < 2; ++k)
+    if (!(q.in_slot[k] = q.be->arena.alloc(in_bytes, 256)))
+      return set_error(LSC_ERROR_OUT_OF_MEMORY, "INT8 session: no arena room for the input");
+  // the classifier's width is known once it is compiled; room for up to 64 Ki classes
+  const uint64_t out_bytes = static_cast<uint64_t>(q.in_shape[0]) * 65536 * 4;
+  const Node& fc = m.nodes[q.steps.back().node];
+  const OnnxTensor& fw = m.inits.at(fc.in[1]);
+  const bool trans_b = fc.op == "Gemm" && fc.attr_i("transB", 0) != 0;
+  const int64_t classes = trans_b ? fw.dims[0] : fw.dims[1];
+  if (classes > 65536) return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "INT8 session: more than 65536 classes");
+  (void)out_bytes;
+  if (!(q.out_buf = q.be->arena.alloc(static_cast<size_t>(q.in_shape[0] * classes * 4), 256)))
+    return set_error(LSC_ERROR_OUT_OF_MEMORY, "INT8 session: no arena room for the output");
+  LSC_CUDA_TRY(cudaStreamCreateWithFlags(&q.cap_stream, cudaStreamNonBlocking));
+  LSC_CUDA_TRY(cudaStreamCreateWithFlags(&q.side_stream, cudaStreamNonBlocking));
+  LSC_CUDA_TRY(cudaStreamCreateWithFlags(&q.copy_stream, cudaStreamNonBlocking));
+  for (int k = 0; k < 2; ++k) {
+    LSC_CUDA_TRY(cudaEventCreateWithFlags(&q.slot_loaded[k], cudaEventDisableTiming));
+    LSC_CUDA_TRY(cudaEventCreateWithFlags(&q.slot_free[k], cudaEventDisableTiming));
+  }
+  // the calibration batch, staged into input slot 0 (host or device f32 of the input's shape)
+  const lsc_tensor& c = *calib;
+  bool ok = c.dtype == LSC_DTYPE_F32 && c.ndim == 4 && c.data;
+  for (int i = 0; ok && i < 4; ++i) ok = c.shape[i] == q.in_shape[static_cast<size_t>(i)];
+  if (!ok) return set_error(LSC_ERROR_SHAPE_MISMATCH, "INT8 session: the calibration batch must be f32 of the input's shape");
+  LSC_CUDA_TRY(cudaMemcpyAsync(q.in_slot[0], c.data, in_bytes,
+                               c.location == LSC_MEM_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                               q.cap_stream));
+  if ((s = calibrate_int8(q, m, static_cast<const float*>(q.in_slot[0]), q.cap_stream))) return s;
+  return capture_int8(q);
+}
+
+// Copies the input into slot k on `st` (nothing when it already lives there).
+lsc_status stage_input(QSession& q, const lsc_tensor& t, int k, cudaStream_t st) {
+  const uint64_t bytes = static_cast<uint64_t>(count_of(q.in_shape)) * 4;
+  bool ok = t.dtype == LSC_DTYPE_F32 && t.ndim == 4 && t.data && (!t.nbytes || t.nbytes >= bytes);
+  for (int i = 0; ok && i < 4; ++i) ok = t.shape[i] == q.in_shape[static_cast<size_t>(i)];
+  if (!ok) return set_error(LSC_ERROR_SHAPE_MISMATCH, "lsc_session_run: the input must be f32 of the model's input shape");
+  if (t.data == q.in_slot[k]) return LSC_SUCCESS;
+  LSC_CUDA_TRY(cudaMemcpyAsync(q.in_slot[k], t.data, bytes,
+                               t.location == LSC_MEM_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+  return LSC_SUCCESS;
+}
+
+lsc_status fetch_output(QSession& q, lsc_tensor& t, cudaStream_t st) {
+  const uint64_t bytes = static_cast<uint64_t>(q.in_shape[0] * q.out_classes) * 4;
+  if (!t.data || (t.nbytes && t.nbytes < bytes))
+    return set_error(LSC_ERROR_SHAPE_MISMATCH, "lsc_session_run: the output needs %llu bytes", (unsigned long long)bytes);
+  t.ndim = 2;
+  t.shape[0] = q.in_shape[0];
+  t.shape[1] = q.out_classes;
+  t.dtype = LSC_DTYPE_F32;
+  if (t.data == q.out_buf) return LSC_SUCCESS;
+  LSC_CUDA_TRY(cudaMemcpyAsync(t.data, q.out_buf, bytes,
+                               t.location == LSC_MEM_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
+  return LSC_SUCCESS;
+}
+
+}  // namespace
+
+void destroy_qsession(QSession* q) { delete q; }
+
 // ------------------------------------------------------------------------------ C ABI
 extern "C" {
 
@@ -866,6 +1601,22 @@ void lsc_session_destroy(lsc_session* session) { delete session; }
 lsc_status lsc_session_run(lsc_session* s, const lsc_tensor* inputs, uint32_t n_inputs, lsc_tensor* outputs,
                            uint32_t n_outputs, lsc_stream stream) {
   if (!s) return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_run: null session");
+  if (s->q) {
+    // INT8: input slot 0, the captured graph, the output; host buffers complete on return
+    if (n_inputs != 1 || n_outputs != 1 || !inputs || !outputs)
+      return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_run: one input and one output");
+    QSession& q = *s->q;
+    lsc::DeviceGuard guard(s->be->device);
+    if (!guard.ok()) return LSC_ERROR_DEVICE_ERROR;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    lsc_status r = stage_input(q, inputs[0], 0, st);
+    if (r) return r;
+    LSC_CUDA_TRY(cudaGraphLaunch(q.exec[0], st));
+    if ((r = fetch_output(q, outputs[0], st))) return r;
+    if (inputs[0].location == LSC_MEM_HOST || outputs[0].location == LSC_MEM_HOST)
+      LSC_CUDA_TRY(cudaStreamSynchronize(st));
+    return LSC_SUCCESS;
+  }
   const lsc_model& m = *s->model;
   if (n_inputs != m.inputs.size() || n_outputs != m.outputs.size() || (n_inputs && !inputs) || (n_outputs && !outputs))
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_run: the model takes %zu inputs and %zu outputs",
@@ -929,6 +1680,104 @@ lsc_status lsc_session_run(lsc_session* s, const lsc_tensor* inputs, uint32_t n_
       o.ndim = out[0].ndim;
       for (int i = 0; i < o.ndim; ++i) o.shape[i] = out[0].shape[i];
     }
+  }
+  return LSC_SUCCESS;
+}
+
+
+lsc_status lsc_session_create_ex(lsc_backend* backend, const lsc_model* model, const lsc_session_options* options,
+                                 lsc_session** out) {
+  if (!options || options->precision == LSC_PRECISION_F32) return lsc_session_create(backend, model, out);
+  if (!backend || !model || !out) return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_create_ex: null argument");
+  *out = nullptr;
+  if (options->precision != LSC_PRECISION_INT8)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_create_ex: unknown precision %d", options->precision);
+  if (!options->calibration)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_create_ex: an INT8 session needs a calibration batch");
+  lsc::DeviceGuard guard(backend->device);
+  if (!guard.ok()) return LSC_ERROR_DEVICE_ERROR;
+  std::unique_ptr<lsc_session> s(new (std::nothrow) lsc_session());
+  if (!s) return set_error(LSC_ERROR_OUT_OF_MEMORY, "lsc_session_create_ex: out of host memory");
+  backend->retain();
+  s->be = backend;
+  s->model = model;
+  s->q = new (std::nothrow) QSession();
+  if (!s->q) return set_error(LSC_ERROR_OUT_OF_MEMORY, "lsc_session_create_ex: out of host memory");
+  QSession& q = *s->q;
+  q.be = backend;
+  q.rounding = options->rounding >= 0 ? options->rounding : backend->cfg.rounding;
+  q.concurrent = options->concurrent != 0;
+  q.plan_memory = options->plan_memory != 0;
+  lsc_status st = build_int8(q, *model, options->calibration);
+  if (st) return st;
+  *out = s.release();
+  return LSC_SUCCESS;
+}
+
+lsc_status lsc_session_run_async(lsc_session* s, const lsc_tensor* inputs, uint32_t n_inputs, lsc_tensor* outputs,
+                                 uint32_t n_outputs, lsc_stream stream) {
+  if (!s) return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_run_async: null session");
+  if (!s->q) return set_error(LSC_ERROR_NOT_IMPLEMENTED, "lsc_session_run_async: INT8 sessions only");
+  if (n_inputs != 1 || n_outputs != 1 || !inputs || !outputs)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_run_async: one input and one output");
+  QSession& q = *s->q;
+  lsc::DeviceGuard guard(s->be->device);
+  if (!guard.ok()) return LSC_ERROR_DEVICE_ERROR;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int k = q.next_slot;
+  q.next_slot ^= 1;
+  lsc_status r;
+  if (inputs[0].location == LSC_MEM_HOST) {
+    // host data is ready now: upload on the copy stream once slot k's last reader has finished
+    LSC_CUDA_TRY(cudaStreamWaitEvent(q.copy_stream, q.slot_free[k], 0));
+    if ((r = stage_input(q, inputs[0], k, q.copy_stream))) return r;
+    LSC_CUDA_TRY(cudaEventRecord(q.slot_loaded[k], q.copy_stream));
+    LSC_CUDA_TRY(cudaStreamWaitEvent(st, q.slot_loaded[k], 0));
+  } else if ((r = stage_input(q, inputs[0], k, st))) {
+    return r;
+  }
+  LSC_CUDA_TRY(cudaGraphLaunch(q.exec[k], st));
+  LSC_CUDA_TRY(cudaEventRecord(q.slot_free[k], st));
+  return fetch_output(q, outputs[0], st);
+}
+
+lsc_status lsc_session_io_buffer(lsc_session* s, int32_t is_output, uint32_t index, void** device_ptr,
+                                 uint64_t* bytes) {
+  if (!s || !device_ptr || index != 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_io_buffer: bad arguments");
+  if (!s->q) return set_error(LSC_ERROR_NOT_IMPLEMENTED, "lsc_session_io_buffer: INT8 sessions only");
+  QSession& q = *s->q;
+  *device_ptr = is_output ? q.out_buf : q.in_slot[0];
+  if (bytes)
+    *bytes = static_cast<uint64_t>(is_output ? q.in_shape[0] * q.out_classes : count_of(q.in_shape)) * 4;
+  return LSC_SUCCESS;
+}
+
+lsc_status lsc_session_memory_plan(const lsc_session* s, uint64_t* planned_bytes, uint64_t* unplanned_bytes,
+                                   uint32_t* values) {
+  if (!s) return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_memory_plan: null session");
+  if (!s->q) return set_error(LSC_ERROR_NOT_IMPLEMENTED, "lsc_session_memory_plan: INT8 sessions only");
+  if (planned_bytes) *planned_bytes = s->q->planned_bytes;
+  if (unplanned_bytes) *unplanned_bytes = s->q->unplanned_bytes;
+  if (values) *values = static_cast<uint32_t>(s->q->vals.size());
+  return LSC_SUCCESS;
+}
+
+lsc_status lsc_session_value(const lsc_session* s, const char* tensor_name, float* scale, void** device_ptr,
+                             lsc_tensor* desc) {
+  if (!s || !tensor_name) return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_value: null argument");
+  if (!s->q) return set_error(LSC_ERROR_NOT_IMPLEMENTED, "lsc_session_value: INT8 sessions only");
+  const QSession& q = *s->q;
+  auto it = q.val_of.find(tensor_name);
+  if (it == q.val_of.end())
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "lsc_session_value: no int8 tensor '%s'", tensor_name);
+  const QVal& v = q.vals[it->second];
+  if (scale) *scale = v.scale;
+  if (device_ptr) *device_ptr = q.ptr(it->second);
+  if (desc) {
+    float dummy = 0.0f;
+    *desc = q_tensor(v, q.ptr(it->second), &dummy);
+    desc->name = nullptr;
+    desc->quant = lsc_quant{};
   }
   return LSC_SUCCESS;
 }

@@ -1,94 +1,13 @@
 """Writes ONNX models (ModelProto protobuf bytes) for the model-loader and session tests.
 
-The `onnx` package is not available here, so this encodes the protobuf wire format directly
-(the fields are those of onnx.proto: ModelProto.ir_version = 1, opset_import = 8, graph = 7;
-GraphProto node = 1, name = 2, initializer = 5, input = 11, output = 12; NodeProto input = 1,
-output = 2, name = 3, op_type = 4, attribute = 5; AttributeProto name = 1, f = 2, i = 3,
-s = 4, ints = 8, type = 20; TensorProto dims = 1, data_type = 2, name = 8, raw_data = 9;
-ValueInfoProto name = 1, type = 2).  Models are built from seeded numpy parameters, which the
-tests reuse to compute the expected outputs with the oracle.
+The protobuf encoding is lightship_b200.onnx_writer's.  Models are built from seeded numpy
+parameters, which the tests reuse to compute the expected outputs with the oracle.
 """
 from __future__ import annotations
 
-import struct
-
 import numpy as np
 
-FLOAT, INT64 = 1, 7
-A_FLOAT, A_INT, A_STRING, A_INTS = 1, 2, 3, 7
-
-
-def _varint(v: int) -> bytes:
-    v &= (1 << 64) - 1
-    out = bytearray()
-    while True:
-        b = v & 0x7F
-        v >>= 7
-        if v:
-            out.append(b | 0x80)
-        else:
-            out.append(b)
-            return bytes(out)
-
-
-def _key(field: int, wire: int) -> bytes:
-    return _varint((field << 3) | wire)
-
-
-def _len(field: int, payload: bytes) -> bytes:
-    return _key(field, 2) + _varint(len(payload)) + payload
-
-
-def _int(field: int, v: int) -> bytes:
-    return _key(field, 0) + _varint(v)
-
-
-def _str(field: int, s: str) -> bytes:
-    return _len(field, s.encode())
-
-
-def attr(name: str, value) -> bytes:
-    """AttributeProto for an int, float, string or list of ints."""
-    b = _str(1, name)
-    if isinstance(value, float):
-        b += _key(2, 5) + struct.pack("<f", value) + _int(20, A_FLOAT)
-    elif isinstance(value, int):
-        b += _int(3, value) + _int(20, A_INT)
-    elif isinstance(value, str):
-        b += _len(4, value.encode()) + _int(20, A_STRING)
-    else:  # list of ints, packed
-        b += _len(8, b"".join(_varint(int(v)) for v in value)) + _int(20, A_INTS)
-    return b
-
-
-def node(op: str, inputs, outputs, name: str = "", **attrs) -> bytes:
-    b = b"".join(_str(1, i) for i in inputs) + b"".join(_str(2, o) for o in outputs)
-    b += _str(3, name or outputs[0]) + _str(4, op)
-    for k, v in attrs.items():
-        b += _len(5, attr(k, v))
-    return b
-
-
-def tensor(name: str, arr: np.ndarray) -> bytes:
-    arr = np.ascontiguousarray(arr)
-    dt = FLOAT if arr.dtype == np.float32 else INT64
-    b = b"".join(_int(1, int(d)) for d in arr.shape) + _int(2, dt) + _str(8, name)
-    return b + _len(9, arr.astype("<f4" if dt == FLOAT else "<i8").tobytes())
-
-
-def value_info(name: str, shape) -> bytes:
-    dims = b"".join(_len(1, _int(1, int(d))) for d in shape)
-    tensor_type = _int(1, FLOAT) + _len(2, dims)
-    return _str(1, name) + _len(2, _len(1, tensor_type))
-
-
-def model(nodes, inits: dict, inputs: dict, outputs: dict, name: str = "graph") -> bytes:
-    g = b"".join(_len(1, n) for n in nodes) + _str(2, name)
-    g += b"".join(_len(5, tensor(k, v)) for k, v in inits.items())
-    g += b"".join(_len(11, value_info(k, s)) for k, s in inputs.items())
-    g += b"".join(_len(12, value_info(k, s)) for k, s in outputs.items())
-    opset = _str(1, "") + _int(2, 13)
-    return _int(1, 8) + _len(8, opset) + _len(7, g)
+from lightship_b200.onnx_writer import model, node  # noqa: F401  (the wire-format encoder)
 
 
 # ---------------------------------------------------------------------------- test models

@@ -5,9 +5,8 @@ f32 weights.  Compared with the reference KATs and the oracle.
 Tolerances (contractions): every output element must satisfy
     |y - y_oracle| <= tol * (sum_k |a_k * b_k| + |bias|)
 with tol = 2e-5 for split-TF32 (the default, three tensor-core products) and 2e-3 for
-single-pass TF32.  Elementwise operators (BatchNorm, ReLU, ReLU6, add) are bit-exact; SiLU
-is within 2 ulp (its exp is evaluated in double, glibc's expf is not always correctly
-rounded)."""
+single-pass TF32.  Elementwise operators (BatchNorm, ReLU, ReLU6, SiLU, add) are bit-exact:
+SiLU's exp restates the host libm's expf."""
 import numpy as np
 import pytest
 
@@ -303,13 +302,35 @@ def test_activation_kats_and_bits(be):
         got, ref = y.numpy(), orc.act(big, kind)
         if kat is not None:
             assert got[:len(kat)].tolist() == kat
-            np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
         else:
-            fin = np.isfinite(ref)
-            ulps = np.abs(got[fin].view(np.int32).astype(np.int64) - ref[fin].view(np.int32).astype(np.int64))
-            assert ulps.max() <= 2
             for xv, want, tol in K.SILU_POINTS:
                 assert abs(orc.act(np.float32([xv]), kind)[0] - want) < tol
+        np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_silu_bit_exact_over_its_exp_range(cuda):
+    """SiLU on every 7th float of [-20.5, 20.5] (the range where it evaluates exp, and past the
+    cut-offs), on the device, against the oracle's x / (1 + expf(-x)) bit for bit."""
+    import torch
+    B = _B()
+    be = B.CudaBackend(B.GpuBackendConfig(device_id=0, arena_bytes=64 << 20))
+    try:
+        op = None
+        for lo, hi in ((0x00000000, 0x41A40000), (0x80000000, 0xC1A40000)):
+            bits = np.arange(lo, hi, 7, dtype=np.uint64).astype(np.uint32)
+            x = bits.view(np.float32)
+            xt = B.Tensor("x", [x.size], B.DataType.F32, torch.from_numpy(x).to(cuda))
+            yd = torch.empty(x.size, dtype=torch.float32, device=cuda)
+            yt = B.Tensor("y", [x.size], B.DataType.F32, yd)
+            if op is None:
+                op = be.compile_operator(B.OperatorDef("silu", B.OperatorType.SiLU), None, [xt], [yt])
+            be.execute(op, [xt], [yt])
+            got = yd.cpu().numpy()
+            ref = orc.act(x, orc.ACT_SILU)
+            np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+        del op
+    finally:
+        be.close()
 
 
 # ------------------------------------------------------------------------------ INT8 Conv2d via the Backend

@@ -31,10 +31,8 @@ def _case(rng, m, n, k, bias=True):
 
 
 def _compare(got, want, f32_ulps=0):
-    """Bit-exact comparison.  f32_ulps > 0 only for SiLU: the oracle's exp is glibc's expf
-    (error < 0.502 ulp, so not always correctly rounded) while the kernel's is the
-    correctly rounded exp; the f32 outputs may then differ by a couple of ulps, and an int8
-    output may differ only where its f32 input differs."""
+    """Bit-exact comparison (f32_ulps = 0), SiLU included: the kernel's exp restates the
+    host libm's expf that the oracle calls."""
     q, y, acc = got
     wq, wy, wacc = want
     np.testing.assert_array_equal(acc, wacc)
@@ -70,7 +68,7 @@ def test_gemm_i8_activations(cuda, act):
     for rounding in (orc.ROUND_HALF_AWAY, orc.ROUND_HALF_EVEN):
         want = orc.gemm_i8_chain(a, w, b, scale, act, 0.05, rounding)
         got = _run(cuda, a, w, b, scale, act, 0.05, rounding)
-        _compare(got, want, f32_ulps=2 if act == orc.ACT_SILU else 0)
+        _compare(got, want)
 
 
 def test_gemm_i8_rounding_ties(cuda):
