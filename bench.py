@@ -143,15 +143,6 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(loaded)}
 
 
-def network_conv_ops(model):
-    """{conv name: ops per image} from the model's activation shapes."""
-    ops = {}
-    for spec in model.convs:
-        _, oh, ow, _ = model.shapes[spec.name]
-        ops[spec.name] = 2 * spec.cout * oh * ow * spec.k * spec.k * spec.cin
-    return ops
-
-
 # --------------------------------------------------------------------------- CPU side
 def host_threads():
     """Every host core this process may run on.  Passed explicitly to the CPU legs so that a
@@ -548,13 +539,6 @@ def conv_measure(torch, dev, batch, steps, warmup, only=()):
     return out
 
 
-def auto_branches(per_gpu_batch):
-    """Concurrent image groups for a per-GPU ResNet batch.  Measured on B200 (graph step time,
-    batch 32 / 64 / 128 / 256): two groups 322 / 450 / 676 / 1132 us against one chain's
-    299 / 411 / 666 / 1151 us, four groups at batch 32 362 us; one chain is kept."""
-    return 1
-
-
 def shard_bounds(batch, world, rank):
     """The contiguous slice [lo, hi) of the global batch that rank owns (batch % world == 0)."""
     if batch % world:
@@ -571,6 +555,241 @@ def reduce_max(v, world, device=None):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def load_profile_value(profile, key):
+    """A `key: value` number from a committed ncu summary under profiles/ (None if absent)."""
+    p = os.path.join(ROOT, "profiles", profile)
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            if line.startswith(key + ":"):
+                try:
+                    return float(line.split(":", 1)[1].strip())
+                except ValueError:
+                    return None
+    return None
+
+
+def resnet_conv_ops_per_image():
+    """Algorithmic ops (2 per MAC) of ResNet-18's 20 convolutions for one 224x224 image
+    (outputs 112 for conv1, then 56 / 28 / 14 / 7 for the four stages)."""
+    from lightship_b200.resnet18 import build_params
+    convs, _, _, _ = build_params(NET_SEED)
+    total = 0
+    for spec in convs:
+        o = 112 if spec.name == "conv1" else 56 >> (int(spec.name[5]) - 1)
+        total += 2 * spec.cout * o * o * spec.k * spec.k * spec.cin
+    return total
+
+
+RESNET_GOPS_PER_IMAGE = 3.628  # 2 x MACs incl. the classifier, standard stem max pool
+RESNET_KERNELS = 24  # input quantize, 20 convolutions, max pool, average pool, classifier
+
+
+def session_scales(sess):
+    """The INT8 session's calibrated scales under the layer names of lightship_b200.resnet18."""
+    from lightship_b200.resnet18 import build_params
+    convs, _, _, _ = build_params(NET_SEED)
+    sc = {"input": sess.value("X:q")["scale"], "pool": sess.value("pool")["scale"],
+          "pooled": sess.value("pooled")["scale"]}
+    for spec in convs:
+        sc[spec.name] = sess.value(spec.name)["scale"]
+    return sc
+
+
+def gemm_line(torch, dev, int8_peak, steps, cpu_leg):
+    """The 4096^3 INT8 per-channel GEMM: device TOPS per output variant with the library
+    yardsticks, the e2e figure (host A and W uploaded, the GEMM, the int8 output downloaded,
+    through lsc_memcpy_h2d / lsc_gemm_i8 / lsc_memcpy_d2h) and, on the CPU leg, the reference
+    chain on a row sample."""
+    from lightship_b200 import _lib
+    variants, s_out = gemm_measure(torch, dev, steps, 10)
+    tops, gms = variants["i8"]
+    vendor = vendor_gemm_measure(torch, dev, steps, 10)
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sptr = C.c_void_p(stream.cuda_stream)
+    a, w, scale, bias = gemm_inputs()
+    ha, hw = torch.from_numpy(a).pin_memory(), torch.from_numpy(w).pin_memory()
+    hq = torch.empty((GEMM_M, GEMM_N), dtype=torch.int8).pin_memory()
+    ta, tw = torch.empty_like(ha, device=dev), torch.empty_like(hw, device=dev)
+    ts, tb = torch.from_numpy(scale).to(dev), torch.from_numpy(bias).to(dev)
+    tq = torch.empty((GEMM_M, GEMM_N), dtype=torch.int8, device=dev)
+    P = lambda t: C.c_void_p(t.data_ptr())
+
+    def e2e_step():
+        _lib.check(lib.lsc_memcpy_h2d(P(ta), P(ha), a.nbytes, sptr))
+        _lib.check(lib.lsc_memcpy_h2d(P(tw), P(hw), w.nbytes, sptr))
+        _lib.check(lib.lsc_gemm_i8(P(ta), P(tw), GEMM_M, GEMM_N, GEMM_K, P(tb), P(ts), s_out, 0, 1, P(tq), None, None,
+                                   sptr))
+        _lib.check(lib.lsc_memcpy_d2h(P(hq), P(tq), hq.numel(), sptr))
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    n_e2e = 20
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record(stream)
+    for _ in range(n_e2e):
+        e2e_step()
+    ee.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = es.elapsed_time(ee) / n_e2e
+    leg = {"value": tops, "unit": "TOPS", "ms_per_launch": gms, "workload": GEMM_WORKLOAD,
+           "roofline_frac": tops / int8_peak, "traffic": load_traffic("contraction_i8_gemm_4096.md"),
+           "variants": {k: {"TOPS": v[0], "ms_per_launch": v[1], "roofline_frac": v[0] / int8_peak}
+                        for k, v in variants.items()},
+           "vendor": {k: {"TOPS": v[0], "ms_per_launch": v[1]} for k, v in vendor.items()},
+           "e2e": {"value": GEMM_OPS / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
+                   "h2d_bytes_per_step": a.nbytes + w.nbytes, "d2h_bytes_per_step": hq.numel(),
+                   "api": "lsc_memcpy_h2d (A, W) + lsc_gemm_i8 + lsc_memcpy_d2h (int8 C)"}}
+    if cpu_leg:
+        w_kn = np.ascontiguousarray(w.T)
+        rows = 64
+        dt = cpu_gemm_rows(rows, a, w_kn, bias, scale, s_out)
+        leg["cpu_baseline"] = {"value": 2 * rows * GEMM_N * GEMM_K / dt / 1e12, "unit": "TOPS",
+                               "cores": host_threads(), "kind": "port",
+                               "sample": f"rows 0..{rows - 1} of A through the reference chain (NN triple loop, "
+                                         f"OpenMP over M, half-even requantize), {dt:.2f} s"}
+    return leg
+
+
+def bert_line(torch, dev, be, world, rank, int8_peak, steps, max_over_ranks, barrier, cpu_leg):
+    """The BERT-base encoder block, batch 32 x seq 384 split over the ranks (each rank its
+    32/N sequences, the step time the max over ranks)."""
+    if BERT_BATCH % world:
+        return {"skipped": f"batch {BERT_BATCH} does not split over {world} GPUs"}
+    per = BERT_BATCH // world
+    barrier()
+    r = bert_measure(torch, dev, per, steps, 5, be)
+    ms = max_over_ranks(r["ms"])
+    e2e_ms = max_over_ranks(r["e2e_ms"])
+    leg = {"value": BERT_BATCH / (ms * 1e-3), "unit": "sequences/s", "ms_per_block": ms, "per_gpu_batch": per,
+           "workload": BERT_WORKLOAD, "projection_tops": r["gemm_tops"],
+           "projection_roofline_frac": r["gemm_tops"] / int8_peak, "attention_tflops": r["attention_tflops"],
+           "stage_ms": r["stage_ms"], "e2e_sequences_per_s": BERT_BATCH / (e2e_ms * 1e-3),
+           "e2e_matches_device_run": r["e2e_ok"]}
+    if cpu_leg:
+        seqs = 4
+        dt, _ = cpu_bert_sample(seqs, r["scales"])
+        leg["cpu_baseline"] = {"value": seqs / dt, "unit": "sequences/s", "cores": host_threads(), "kind": "port",
+                               "sample": f"{seqs} sequences of 384 tokens through the oracle's quantized encoder "
+                                         f"block, {dt:.2f} s"}
+    return leg
+
+
+def fp32_legs(torch, dev, be, bf16_peak, steps, cpu_leg):
+    """The two FP32 configurations through FP32 ONNX sessions (lsc_session_run on device
+    buffers, split-TF32 tensor-core kernels): the 512^3 MatMul of two runtime inputs, and the
+    1x64x56x56 3x3 convolution with bias, folded BatchNorm and ReLU.  Both are latency-bound at
+    their size; the peak is the three-product split-TF32 rate (bf16 burst / 2 for TF32, / 3)."""
+    from lightship_b200 import _lib
+    from lightship_b200.backend import DataType, OnnxModel, Session, StorageLayout, Tensor
+    from lightship_b200.onnx_writer import model as onnx_model, node as onnx_node
+    peak = bf16_peak / 2 / 3
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    rng = np.random.default_rng(DATA_SEED)
+    out = {}
+
+    def timed(run):
+        for _ in range(5):
+            flush.zero_()
+            run()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        torch.cuda.synchronize(dev)
+        for s_, e_ in ev:
+            flush.zero_()
+            s_.record(stream)
+            run()
+            e_.record(stream)
+        torch.cuda.synchronize(dev)
+        return float(np.mean([s_.elapsed_time(e_) for s_, e_ in ev]))
+
+    # config 1: C = A B, 512^3, entries U[-1, 1]
+    a = rng.uniform(-1, 1, (512, 512)).astype(np.float32)
+    b = rng.uniform(-1, 1, (512, 512)).astype(np.float32)
+    m1 = OnnxModel(onnx_model([onnx_node("MatMul", ["A", "B"], ["C"])], {}, {"A": [512, 512], "B": [512, 512]},
+                              {"C": [512, 512]}, name="gemm512"))
+    s1 = Session(be, m1)
+    ta, tb = torch.from_numpy(a).to(dev), torch.from_numpy(b).to(dev)
+    tc = torch.empty((512, 512), dtype=torch.float32, device=dev)
+    ins = [Tensor("A", [512, 512], DataType.F32, ta), Tensor("B", [512, 512], DataType.F32, tb)]
+    outs = [Tensor("C", [512, 512], DataType.F32, tc)]
+    ms = timed(lambda: s1.run(ins, outs, stream=stream.cuda_stream))
+    hc = np.zeros((512, 512), np.float32)
+    h_ins = [Tensor("A", [512, 512], DataType.F32, a), Tensor("B", [512, 512], DataType.F32, b)]
+    h_outs = [Tensor("C", [512, 512], DataType.F32, hc)]
+    e2e = timed(lambda: s1.run(h_ins, h_outs, stream=stream.cuda_stream))
+    flops = 2 * 512 ** 3
+    leg = {"workload": "FP32 GEMM via Session: A[512x512] B[512x512] (ONNX MatMul of two inputs), U[-1,1]",
+           "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+           "roofline": {"bound": "latency (tensor split-TF32)", "achieved": flops / (ms * 1e-3) / 1e12,
+                        "peak": peak, "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / peak},
+           "e2e": {"value": flops / (e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": a.nbytes + b.nbytes,
+                   "d2h_bytes_per_step": hc.nbytes, "api": "lsc_session_run (host A, B, C)"}}
+    if cpu_leg:
+        from oracle import oracle as orc
+        t0 = time.perf_counter()
+        reps = 5
+        for _ in range(reps):
+            want = orc.matmul(a, b, host_threads())
+        dt = (time.perf_counter() - t0) / reps
+        leg["cpu_baseline"] = {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": host_threads(), "kind": "port",
+                               "sample": "the whole 512^3 product, NEON-order blocked GEMM restated, row blocks over "
+                                         "all host threads"}
+        got = tc.cpu().numpy()
+        leg["max_rel_err_vs_oracle"] = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
+    out["gemm_512"] = leg
+    del s1, m1
+
+    # config 2: Conv2d 3x3 s1 p1, 1x64x56x56 -> 64, bias, BN folded, ReLU
+    x = rng.normal(size=(1, 64, 56, 56)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2.0 / 576), (64, 64, 3, 3)).astype(np.float32)
+    bias = rng.normal(0, 0.1, 64).astype(np.float32)
+    g, beta = rng.uniform(0.5, 1.5, 64).astype(np.float32), rng.normal(0, 0.1, 64).astype(np.float32)
+    mu, var = rng.normal(0, 0.1, 64).astype(np.float32), rng.uniform(0.5, 1.5, 64).astype(np.float32)
+    nodes = [onnx_node("Conv", ["X", "W", "Bc"], ["t"], kernel_shape=[3, 3], pads=[1, 1, 1, 1]),
+             onnx_node("BatchNormalization", ["t", "g", "beta", "mu", "var"], ["u"], epsilon=1e-5),
+             onnx_node("Relu", ["u"], ["Y"])]
+    m2 = OnnxModel(onnx_model(nodes, {"W": w, "Bc": bias, "g": g, "beta": beta, "mu": mu, "var": var},
+                              {"X": [1, 64, 56, 56]}, {"Y": [1, 64, 56, 56]}, name="conv_bn_relu"))
+    s2 = Session(be, m2)
+    tx = torch.from_numpy(x).to(dev)
+    ty = torch.empty((1, 64, 56, 56), dtype=torch.float32, device=dev)
+    ins = [Tensor("X", [1, 64, 56, 56], DataType.F32, tx, layout=StorageLayout.NCHW)]
+    outs = [Tensor("Y", [1, 64, 56, 56], DataType.F32, ty, layout=StorageLayout.NCHW)]
+    ms = timed(lambda: s2.run(ins, outs, stream=stream.cuda_stream))
+    hy = np.zeros((1, 64, 56, 56), np.float32)
+    h_ins = [Tensor("X", [1, 64, 56, 56], DataType.F32, x, layout=StorageLayout.NCHW)]
+    h_outs = [Tensor("Y", [1, 64, 56, 56], DataType.F32, hy, layout=StorageLayout.NCHW)]
+    e2e = timed(lambda: s2.run(h_ins, h_outs, stream=stream.cuda_stream))
+    flops = 2 * 3136 * 64 * 576
+    leg = {"workload": "FP32 Conv2d 3x3 s1 p1, 1x64x56x56 -> 64, bias, BatchNorm folded, ReLU (ONNX Conv+BN+Relu)",
+           "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+           "roofline": {"bound": "latency (tensor split-TF32)", "achieved": flops / (ms * 1e-3) / 1e12,
+                        "peak": peak, "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / peak},
+           "e2e": {"value": flops / (e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": x.nbytes,
+                   "d2h_bytes_per_step": hy.nbytes, "api": "lsc_session_run (host X, Y)"}}
+    if cpu_leg:
+        from oracle import oracle as orc
+        reps = 5
+        for threads, key in ((1, "cpu_baseline"), (host_threads(), "cpu_baseline_all_cores")):
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                want = orc.act(orc.batchnorm_inference(orc.conv2d_nchw(x, w, bias, pad=(1, 1), threads=threads),
+                                                       g, beta, mu, var), orc.ACT_RELU)
+            dt = (time.perf_counter() - t0) / reps
+            leg[key] = {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                        "sample": "the whole convolution (im2col + GEMM, BatchNorm, ReLU)" +
+                                  (", one thread per image as the reference runs it" if threads == 1 else "")}
+        got = ty.cpu().numpy()
+        leg["max_rel_err_vs_oracle"] = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
+    out["conv_bn_relu_64x56x56"] = leg
+    del s2, m2
+    return out
 
 
 def run_gpu(args):
@@ -694,8 +913,9 @@ def run_gpu(args):
         return 0
 
     # ------------------------------------------------------------------ ResNet-18 INT8
-    from lightship_b200.backend import CudaBackend, GpuBackendConfig
-    from lightship_b200.resnet18 import ResNet18Int8
+    # through the C ABI: the ONNX model compiled by lsc_session_create_ex into an INT8 session
+    from lightship_b200.backend import CudaBackend, GpuBackendConfig, DataType, OnnxModel, Session, StorageLayout, Tensor
+    from lightship_b200.onnx_writer import resnet18_onnx
     batch = args.batch
     if batch % world:
         raise SystemExit(f"batch {batch} does not split over {world} GPUs")
@@ -704,47 +924,42 @@ def run_gpu(args):
     # the global batch is seeded; each rank takes its contiguous shard
     rng = np.random.default_rng(DATA_SEED)
     x_all = rng.normal(size=(batch, 3, IMAGE, IMAGE)).astype(np.float32)
-    x_host = torch.from_numpy(x_all[lo:hi]).pin_memory()
+    x_np = np.ascontiguousarray(x_all[lo:hi])
     del x_all
-    be = CudaBackend(GpuBackendConfig(device_id=local, arena_bytes=256 << 20))
-    model = ResNet18Int8(be, per, dev, image=IMAGE, seed=NET_SEED)
-    x_dev = x_host.to(dev, non_blocking=False)
-    model.calibrate(x_dev)
+    x_host = torch.from_numpy(x_np).pin_memory()
+    arena = max(1 << 30, per * (12 << 20))  # calibration scratch + two input slots + the activation block
+    be = CudaBackend(GpuBackendConfig(device_id=local, arena_bytes=arena))
+    model = OnnxModel(resnet18_onnx(per, NET_SEED, IMAGE))
+    cal = Tensor("X", list(x_np.shape), DataType.F32, x_np, layout=StorageLayout.NCHW)
+    sess = Session(be, model, precision="int8", calibration=cal, concurrent=bool(args.ds_side))
+    lib = _lib.lib()
     stream = torch.cuda.current_stream(dev)
+    sptr = C.c_void_p(stream.cuda_stream)
+    in_ptr, in_bytes = sess.io_buffer(False)
+    out_ptr, out_bytes = sess.io_buffer(True)
+    _lib.check(lib.lsc_memcpy_h2d(C.c_void_p(in_ptr), C.c_void_p(x_host.data_ptr()), in_bytes, sptr))
+    dev_in, dev_out = _lib.lsc_tensor(), _lib.lsc_tensor()
+    dev_in.ndim = 4
+    for i, d in enumerate(x_np.shape):
+        dev_in.shape[i] = d
+    dev_in.dtype, dev_in.location, dev_in.data, dev_in.nbytes = 0, _lib.MEM_DEVICE, in_ptr, in_bytes
+    dev_out.dtype, dev_out.location, dev_out.data, dev_out.nbytes = 0, _lib.MEM_DEVICE, out_ptr, out_bytes
 
-    # eager pass with events around every conv launch: the conv kernel's share and TOPS
-    conv_ops = network_conv_ops(model)
-    fc_ops = 2 * 512 * model.num_classes
-    img_ops = sum(conv_ops.values()) + fc_ops
-    evs = {}
-    orig_run_conv = model._run_conv
+    def step():  # one forward pass on the session's own device buffers (nothing copied)
+        _lib.check(lib.lsc_session_run(sess._h, C.byref(dev_in), 1, C.byref(dev_out), 1, sptr))
 
-    def timed_conv(spec, *a, **k):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        orig_run_conv(spec, *a, **k)
-        e.record(stream)
-        evs.setdefault(spec.name, []).append((s, e))
-
-    model._run_conv = timed_conv
-    for _ in range(3):
-        # queue the pass behind a device sleep so the events time the kernels, not host launches
-        torch.cuda.synchronize(dev)
-        torch.cuda._sleep(20_000_000)
-        model.forward(x_dev)
-    torch.cuda.synchronize(dev)
-    model._run_conv = orig_run_conv
-    conv_ms = sum(np.mean([s.elapsed_time(e) for s, e in v]) for v in evs.values())
-    conv_tops = sum(conv_ops.values()) * per / (conv_ms * 1e-3) / 1e12
-
-    branches = args.branches if args.branches > 0 else auto_branches(per)
-    graph = model.capture(x_dev, branches=branches, concurrent_downsample=bool(args.ds_side))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for _ in range(args.warmup):
         flush.zero_()
-        graph.replay()
+        step()
     torch.cuda.synchronize(dev)
     ops.check_device()
+    # parity: the logits of the timed configuration against the oracle's quantized network on
+    # the same images with the session's calibrated scales (first and last two of the shard)
+    logits_dev = np.empty((per, 1000), np.float32)
+    _lib.check(lib.lsc_memcpy_d2h(C.c_void_p(logits_dev.ctypes.data), C.c_void_p(out_ptr), out_bytes, sptr))
+    torch.cuda.synchronize(dev)
+    scales = session_scales(sess)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     sampler = ClockSampler(uuid)
     sampler.start()
@@ -753,7 +968,7 @@ def run_gpu(args):
     for s, e in ev:
         flush.zero_()
         s.record(stream)
-        graph.replay()
+        step()
         e.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
@@ -763,122 +978,95 @@ def run_gpu(args):
     ms_max = max_over_ranks(ms)
     value = batch / (ms_max * 1e-3)
 
-    # end to end: pinned host input -> device, the network, logits -> host
-    lib = _lib.lib()
-    logits_host = torch.empty((per, model.num_classes), dtype=torch.float32).pin_memory()
-    in_bytes = x_host.numel() * 4
-    out_bytes = logits_host.numel() * 4
-    sptr = C.c_void_p(stream.cuda_stream)
+    # end to end through the session's public API: pinned host input in, host logits out,
+    # sequential (lsc_session_run, complete on return) and pipelined (lsc_session_run_async:
+    # step i+1's upload on the session's copy stream overlaps step i's network)
+    logits_host = torch.empty((per, 1000), dtype=torch.float32).pin_memory()
+    host_in = Tensor("X", list(x_np.shape), DataType.F32, x_host, layout=StorageLayout.NCHW)
+    host_out = Tensor("logits", [1], DataType.F32, logits_host)
     e2e_steps = max(3, min(args.steps, 20))
-
-    def e2e_step():
-        _lib.check(lib.lsc_memcpy_h2d(C.c_void_p(x_dev.data_ptr()), C.c_void_p(x_host.data_ptr()), in_bytes, sptr))
-        graph.replay()
-        _lib.check(lib.lsc_memcpy_d2h(C.c_void_p(logits_host.data_ptr()), C.c_void_p(model.logits.data_ptr()),
-                                      out_bytes, sptr))
-
     for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize(dev)
+        sess.run([host_in], [host_out], stream=stream.cuda_stream)
     barrier()
     es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     es.record(stream)
     for _ in range(e2e_steps):
-        e2e_step()
+        sess.run([host_in], [host_out], stream=stream.cuda_stream)
     ee.record(stream)
     torch.cuda.synchronize(dev)
     e2e_seq_ms = max_over_ranks(es.elapsed_time(ee) / e2e_steps)
-    e2e_ok = bool(torch.equal(logits_host, model.logits.cpu()))
-
-    # the same, pipelined as a server runs it: step i+1's input upload (copy stream) overlaps
-    # step i's network (compute stream); two input buffers, one graph captured on each; the
-    # logits download follows each graph on the compute stream
-    x_dev2 = torch.empty_like(x_dev)
-    graph2 = model.capture(x_dev2, branches=branches, concurrent_downsample=bool(args.ds_side))
-    copy_stream = torch.cuda.Stream(dev)
-    cptr = C.c_void_p(copy_stream.cuda_stream)
-    bufs, graphs = (x_dev, x_dev2), (graph, graph2)
-    loaded = [torch.cuda.Event() for _ in range(2)]
-    freed = [torch.cuda.Event() for _ in range(2)]
-    for ev_ in freed:
-        ev_.record(stream)
-
-    def e2e_pipelined(n_steps):
-        for i in range(n_steps):
-            b = i & 1
-            copy_stream.wait_event(freed[b])
-            _lib.check(lib.lsc_memcpy_h2d(C.c_void_p(bufs[b].data_ptr()), C.c_void_p(x_host.data_ptr()), in_bytes,
-                                          cptr))
-            loaded[b].record(copy_stream)
-            stream.wait_event(loaded[b])
-            graphs[b].replay()
-            _lib.check(lib.lsc_memcpy_d2h(C.c_void_p(logits_host.data_ptr()), C.c_void_p(model.logits.data_ptr()),
-                                          out_bytes, sptr))
-            freed[b].record(stream)
-
-    e2e_pipelined(4)
+    e2e_ok = bool(np.array_equal(logits_host.numpy().view(np.uint32), logits_dev.view(np.uint32)))
+    for _ in range(4):
+        sess.run_async([host_in], [host_out], stream=stream.cuda_stream)
     torch.cuda.synchronize(dev)
     barrier()
     ps, pe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ps.record(stream)
-    copy_stream.wait_event(ps)
-    e2e_pipelined(e2e_steps)
+    for _ in range(e2e_steps):
+        sess.run_async([host_in], [host_out], stream=stream.cuda_stream)
     pe.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(ps.elapsed_time(pe) / e2e_steps)
     e2e_value = batch / (e2e_ms * 1e-3)
-    e2e_ok = e2e_ok and bool(torch.equal(logits_host, model.logits.cpu()))
-    del graph2
+    e2e_ok = e2e_ok and bool(np.array_equal(logits_host.numpy().view(np.uint32), logits_dev.view(np.uint32)))
 
+    plan = sess.memory_plan()
+    conv_ops_img = resnet_conv_ops_per_image()
+    share = load_profile_value("resnet18_int8_b256_launches.md", "conv_kernel_share")
+    conv_tops = conv_ops_img * batch / (ms_max * 1e-3 * share) / 1e12 if share else None
     line = {
         "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": RESNET_WORKLOAD, "global_batch": batch, "per_gpu_batch": per,
                    "image": IMAGE, "parallelism": f"batch split x{world} (no collective)",
-                   "graph_branches": branches, "downsample_side_stream": bool(args.ds_side),
+                   "api": "ONNX model -> lsc_session_create_ex (INT8) -> lsc_session_run",
                    "l2": "flushed (256 MiB write) before every timed step", "seed": NET_SEED},
-        "network_tops": img_ops * batch / (ms_max * 1e-3) / 1e12,
+        "parity": None,
+        "network_tops": RESNET_GOPS_PER_IMAGE * batch / (ms_max * 1e-3) / 1e3,
         "roofline": {"bound": "tensor", "kernel": "contraction_i8_kernel + contraction_i8_swap_kernel (INT8 implicit-GEMM conv)",
-                     "achieved": conv_tops, "peak": int8_peak, "unit": "TOPS", "frac": conv_tops / int8_peak,
-                     "traffic": load_traffic("contraction_i8_conv_layer1_b256.md"), "peak_source": peak_source,
-                     "conv_share_of_step": conv_ms / ms if ms > 0 else None},
-        "conv_us": {k: round(1e3 * float(np.mean([s.elapsed_time(e) for s, e in v])), 2) for k, v in evs.items()},
+                     "achieved": conv_tops, "peak": int8_peak, "unit": "TOPS",
+                     "frac": conv_tops / int8_peak if conv_tops else None,
+                     "traffic": load_profile_value("contraction_i8_conv_layer1_b256.md", "traffic_bytes_per_launch"),
+                     "peak_source": peak_source,
+                     "conv_share_of_step": share,
+                     "method": "achieved = algorithmic conv ops / (graph step time x the conv kernels' share of the "
+                               "step's device time in the committed launch list)"},
+        "memory_plan": plan,
         "e2e": {"value": e2e_value, "unit": "img/s", "h2d_bytes_per_step": in_bytes * world,
-                "d2h_bytes_per_step": out_bytes * world, "api": "lsc_memcpy_h2d + network + lsc_memcpy_d2h",
-                "pipelined": "step i+1's upload (copy stream) overlaps step i's network; every step's "
+                "d2h_bytes_per_step": out_bytes * world,
+                "api": "lsc_session_run_async (pinned host input and logits, two input slots)",
+                "pipelined": "step i+1's upload (the session's copy stream) overlaps step i's network; every step's "
                              "upload and logits download are inside the timed region",
                 "sequential_value": batch / (e2e_seq_ms * 1e-3), "matches_device_run": e2e_ok},
-        "gpu_launches": model.kernel_launches() * args.steps,
+        "gpu_launches": RESNET_KERNELS * args.steps,
         "clocks": clocks,
     }
-    if rank == 0 and not args.no_gemm:
-        variants, _ = gemm_measure(torch, dev, max(50, min(args.steps, 200)), 10)
-        tops, gms = variants["i8"]
-        vendor = vendor_gemm_measure(torch, dev, max(50, min(args.steps, 200)), 10)
-        line["tensor_rate_probe"] = tensor_rate_probe()
-        line["int8_gemm_4096"] = {"value": tops, "unit": "TOPS", "ms_per_launch": gms, "workload": GEMM_WORKLOAD,
-                                  "vendor": {k: {"TOPS": v[0], "ms_per_launch": v[1]} for k, v in vendor.items()},
-                                  "roofline_frac": tops / int8_peak,
-                                  "traffic": load_traffic("contraction_i8_gemm_4096.md"),
-                                  "variants": {k: {"TOPS": v[0], "ms_per_launch": v[1],
-                                                   "roofline_frac": v[0] / int8_peak} for k, v in variants.items()}}
-    if rank == 0 and not args.no_bert:
-        r = bert_measure(torch, dev, BERT_BATCH, max(20, min(args.steps, 100)), 5, be)
-        line["bert_block"] = {"value": BERT_BATCH / (r["ms"] * 1e-3), "unit": "sequences/s", "ms_per_block": r["ms"],
-                              "workload": BERT_WORKLOAD, "projection_tops": r["gemm_tops"],
-                              "projection_roofline_frac": r["gemm_tops"] / int8_peak,
-                              "attention_tflops": r["attention_tflops"], "stage_ms": r["stage_ms"],
-                              "e2e_sequences_per_s": BERT_BATCH / (r["e2e_ms"] * 1e-3)}
-    if rank == 0:
-        if world == 1 and not args.no_cpu_baseline:
-            imgs = 24
-            dt, _, _ = cpu_resnet_sample(imgs, dict(model.scales))
-            line["cpu_baseline"] = {"value": imgs / dt, "unit": "img/s", "cores": host_threads(), "kind": "port",
-                                    "sample": f"{imgs} images through the oracle's quantized ResNet-18 "
-                                              f"(direct int8 convolutions, OpenMP), {dt:.2f} s"}
-    del graph
-    model.graph = None
+    del sess, model
+    if not args.no_gemm:
+        gemm_leg = gemm_line(torch, dev, int8_peak, max(50, min(args.steps, 200)), rank == 0 and world == 1 and
+                             not args.no_cpu_baseline)
+        if rank == 0:
+            line["int8_gemm_4096"] = gemm_leg
+    if not args.no_bert:
+        bert_leg = bert_line(torch, dev, be, world, rank, int8_peak, max(20, min(args.steps, 100)), max_over_ranks,
+                             barrier, rank == 0 and world == 1 and not args.no_cpu_baseline)
+        if rank == 0:
+            line["bert_block"] = bert_leg
+    if not args.no_fp32 and rank == 0:
+        line["fp32_configs"] = fp32_legs(torch, dev, be, bf16_peak, max(20, min(args.steps, 100)),
+                                         world == 1 and not args.no_cpu_baseline)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # the CPU leg: the oracle's quantized ResNet-18 on the first images of the batch with the
+        # session's calibrated scales -- timed as the baseline, and its logits compared with the
+        # timed configuration's (parity)
+        imgs = 24
+        dt, cpu_logits, _ = cpu_resnet_sample(imgs, scales)
+        line["cpu_baseline"] = {"value": imgs / dt, "unit": "img/s", "cores": host_threads(), "kind": "port",
+                                "sample": f"{imgs} images through the oracle's quantized ResNet-18 "
+                                          f"(direct int8 convolutions, OpenMP), {dt:.2f} s"}
+        line["parity"] = {"images": imgs, "bit_exact_logits": bool(np.array_equal(
+            cpu_logits.view(np.uint32), logits_dev[:imgs].view(np.uint32)))}
     be.close()
     if world > 1:
         dist.barrier()
@@ -896,14 +1084,13 @@ def main():
     ap.add_argument("--impl", choices=["lightship", "reference"], default="lightship")
     ap.add_argument("--workload", choices=["resnet18", "gemm", "bert", "probe", "conv"], default="resnet18")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--branches", type=int, default=0,
-                    help="image groups run concurrently inside the ResNet graph (0 = chosen by the per-GPU batch)")
     ap.add_argument("--ds-side", type=int, default=1,
-                    help="1 = run each stage's downsample conv on a side stream beside its first conv")
+                    help="1 = the session runs each stage's downsample conv on a second stream beside its first conv")
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH,
                     help="global ResNet batch (default 256, the benchmark's; smaller only for profiling)")
     ap.add_argument("--no-gemm", action="store_true", help="skip the 4096^3 GEMM sub-measurement")
     ap.add_argument("--no-bert", action="store_true", help="skip the encoder-block sub-measurement")
+    ap.add_argument("--no-fp32", action="store_true", help="skip the FP32 configurations")
     ap.add_argument("--only", default="", help="--workload conv: comma-separated shape names to run")
     args = ap.parse_args()
     if args.warmup < 3:
