@@ -56,3 +56,37 @@ def test_shard_bounds_rejects_uneven_split():
     assert bench.shard_bounds(256, 8, 7) == (224, 256)
     with pytest.raises(ValueError):
         bench.shard_bounds(10, 4, 0)
+
+
+def _leaving_rank_main(rank, world, port, out_dir):
+    """Rank 1 runs one step and leaves between steps (no collective of its in flight); rank 0
+    finds out at its next collective, which the short process-group timeout bounds."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    import bench
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    bench.reduce_max(1.0 + rank, world)  # step 0: both ranks
+    if rank == 1:
+        os._exit(0)  # leaves between steps
+    t0 = time.monotonic()
+    err = ""
+    try:
+        bench.reduce_max(1.0, world)  # step 1: the peer is gone
+    except Exception as e:  # noqa: BLE001 -- any error is the detection
+        err = type(e).__name__ + ": " + str(e)[:200]
+    with open(os.path.join(out_dir, "detect0.txt"), "w") as f:
+        f.write(f"{time.monotonic() - t0:.3f}\n{err}")
+    os._exit(0)
+
+
+def test_rank_that_leaves_is_detected_at_the_next_collective(tmp_path):
+    import torch.multiprocessing as mp
+    mp.start_processes(_leaving_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    elapsed, err = (tmp_path / "detect0.txt").read_text().split("\n", 1)
+    assert err, "rank 0's collective returned although its peer had left"
+    assert float(elapsed) < 30.0
