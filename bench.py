@@ -789,7 +789,43 @@ def fp32_legs(torch, dev, be, bf16_peak, steps, cpu_leg):
         leg["max_rel_err_vs_oracle"] = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
     out["conv_bn_relu_64x56x56"] = leg
     del s2, m2
+    out["conv3x3_algorithms"] = fp32_conv_algorithms(torch, dev, be, timed)
     return out
+
+
+def fp32_conv_algorithms(torch, dev, be, timed):
+    """The FP32 3x3 stride-1 convolution by the direct split-TF32 kernel and by Winograd
+    F(2x2, 3x3) (fp32_mode LSC_FP32_WINOGRAD), Backend operator on device tensors, at the
+    config-2 shape and at a layer1-sized batch of 32: device time per launch sequence and the
+    direct convolution's algorithmic TFLOP/s."""
+    from lightship_b200 import _lib
+    from lightship_b200.backend import DataType, OperatorDef, OperatorType, Tensor
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+    for n in (1, 32):
+        rng = np.random.default_rng(DATA_SEED + n)
+        x = torch.from_numpy(rng.normal(size=(n, 64, 56, 56)).astype(np.float32)).to(dev)
+        w = rng.normal(0, np.sqrt(2.0 / 576), (64, 64, 3, 3)).astype(np.float32)
+        bias = rng.normal(0, 0.1, 64).astype(np.float32)
+        y = torch.empty((n, 64, 56, 56), dtype=torch.float32, device=dev)
+        xt = Tensor("x", [n, 64, 56, 56], DataType.F32, x)
+        yt = Tensor("y", [n, 64, 56, 56], DataType.F32, y)
+        flops = 2.0 * n * 3136 * 64 * 576
+        row = {}
+        outs = {}
+        for name, mode in (("direct_3xtf32", _lib.FP32_3XTF32), ("winograd_f2x2_3x3", _lib.FP32_WINOGRAD)):
+            op = be.compile_operator(OperatorDef("conv", OperatorType.Conv2d, padding=(1, 1), fp32_mode=mode), None,
+                                     [xt, Tensor("w", list(w.shape), DataType.F32, w),
+                                      Tensor("b", [64], DataType.F32, bias)], [yt])
+            ms = timed(lambda: be.execute(op, [xt], [yt], stream=stream.cuda_stream))
+            row[name] = {"us": round(ms * 1e3, 2), "TFLOP_s_algorithmic": round(flops / (ms * 1e-3) / 1e12, 1)}
+            outs[name] = y.clone()
+            del op
+        d = outs["direct_3xtf32"].double()
+        row["max_abs_diff_winograd_vs_direct"] = float((outs["winograd_f2x2_3x3"].double() - d).abs().max())
+        row["winograd_speedup"] = round(row["direct_3xtf32"]["us"] / row["winograd_f2x2_3x3"]["us"], 3)
+        res[f"n{n}_64x56x56_to_64"] = row
+    return res
 
 
 def run_gpu(args):

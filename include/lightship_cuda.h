@@ -125,6 +125,8 @@ typedef enum lsc_fusion_type {
 /* FP32 contraction mode */
 #define LSC_FP32_3XTF32 0 /* split-TF32, three tensor-core products: ~fp32 accuracy */
 #define LSC_FP32_TF32 1   /* single TF32 product: 10-bit mantissa inputs */
+#define LSC_FP32_WINOGRAD 2 /* as LSC_FP32_3XTF32, with 3x3 stride-1 dilation-1 FP32 convolutions
+                               run as Winograd F(2x2, 3x3) (cpu/winograd_conv2d.rs:50-397) */
 
 /* tensor memory location */
 #define LSC_MEM_HOST 0

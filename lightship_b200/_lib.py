@@ -30,7 +30,7 @@ ERROR_TIMEOUT = 15
 ACT_NONE, ACT_RELU, ACT_RELU6, ACT_SILU, ACT_GELU = 0, 1, 2, 3, 4
 DTYPE_F32, DTYPE_F16 = 0, 1  # lsc_dtype
 ROUND_HALF_AWAY, ROUND_HALF_EVEN = 0, 1
-FP32_3XTF32, FP32_TF32 = 0, 1
+FP32_3XTF32, FP32_TF32, FP32_WINOGRAD = 0, 1, 2
 MEM_HOST, MEM_DEVICE = 0, 1
 PRECISION_F32, PRECISION_INT8 = 0, 1
 MAX_DIMS = 8

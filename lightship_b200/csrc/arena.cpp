@@ -49,19 +49,28 @@ void* Arena::alloc(size_t size, size_t align) {
   std::lock_guard<std::mutex> lock(mu_);
   if (!base_) return nullptr;
   if (!pending_.empty()) reap_locked();
-  for (auto it = free_.begin(); it != free_.end(); ++it) {
-    const size_t off = it->first, len = it->second;
-    const size_t aligned = (off + align - 1) & ~(align - 1);
-    if (aligned + size > off + len) continue;
-    free_.erase(it);
-    if (aligned > off) free_[off] = aligned - off;
-    if (aligned + size < off + len) free_[aligned + size] = off + len - (aligned + size);
-    used_[aligned] = size;
-    current_ += size;
-    if (current_ > peak_) peak_ = current_;
-    return base_ + aligned;
+  for (;;) {
+    for (auto it = free_.begin(); it != free_.end(); ++it) {
+      const size_t off = it->first, len = it->second;
+      const size_t aligned = (off + align - 1) & ~(align - 1);
+      if (aligned + size > off + len) continue;
+      free_.erase(it);
+      if (aligned > off) free_[off] = aligned - off;
+      if (aligned + size < off + len) free_[aligned + size] = off + len - (aligned + size);
+      used_[aligned] = size;
+      current_ += size;
+      if (current_ > peak_) peak_ = current_;
+      return base_ + aligned;
+    }
+    // no room: wait for the oldest stream-deferred free (launches queued ahead of this one
+    // still own their scratch) and try again
+    if (pending_.empty()) return nullptr;
+    cudaEventSynchronize(pending_.front().ev);
+    cudaEventDestroy(pending_.front().ev);
+    free_locked(pending_.front().off);
+    pending_.erase(pending_.begin());
+    cudaGetLastError();
   }
-  return nullptr;
 }
 
 bool Arena::free_locked(size_t off) {

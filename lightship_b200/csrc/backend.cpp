@@ -208,7 +208,7 @@ lsc_status lsc_backend_create(const lsc_config* config, lsc_backend** out) {
   if (config) cfg = *config;
   if (cfg.rounding != LSC_ROUND_HALF_AWAY && cfg.rounding != LSC_ROUND_HALF_EVEN)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "backend_create: bad rounding %d", cfg.rounding);
-  if (cfg.fp32_mode != LSC_FP32_3XTF32 && cfg.fp32_mode != LSC_FP32_TF32)
+  if (cfg.fp32_mode != LSC_FP32_3XTF32 && cfg.fp32_mode != LSC_FP32_TF32 && cfg.fp32_mode != LSC_FP32_WINOGRAD)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "backend_create: bad fp32_mode %d", cfg.fp32_mode);
   const int ndev = lsc_device_count();
   if (cfg.device_id < 0 || cfg.device_id >= ndev)
@@ -271,6 +271,8 @@ lsc_status lsc_compile_operator(lsc_backend* be, const lsc_op_desc* def, const l
   op->fp32_mode = def->fp32_mode >= 0 ? def->fp32_mode : be->cfg.fp32_mode;
   if (op->rounding != LSC_ROUND_HALF_AWAY && op->rounding != LSC_ROUND_HALF_EVEN)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "compile_operator: bad rounding %d", op->rounding);
+  if (op->fp32_mode != LSC_FP32_3XTF32 && op->fp32_mode != LSC_FP32_TF32 && op->fp32_mode != LSC_FP32_WINOGRAD)
+    return set_error(LSC_ERROR_INVALID_ARGUMENT, "compile_operator: bad fp32_mode %d", op->fp32_mode);
   lsc_status st = compile_op(be, op.get(), inputs, n_inputs, outputs, n_outputs);
   if (st != LSC_SUCCESS) return st == LSC_ERROR_UNSUPPORTED_OPERATOR ? st : st;
   *out = op.release();

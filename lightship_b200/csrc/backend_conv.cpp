@@ -252,6 +252,35 @@ lsc_status compile_conv(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_te
                        (long long)x.shape[1], (long long)ci);
     op->kind = OpKind::kConvF32;
     op->kp = (ci + 3) / 4 * 4;
+    op->winograd = op->fp32_mode == LSC_FP32_WINOGRAD && op->kh == 3 && op->kw == 3 && op->sh == 1 &&
+                   op->sw == 1 && op->dh == 1 && op->dw == 1;
+    if (op->winograd) {
+      // U_xi[o][c] = (G g G^T)[i][j], xi = 4 i + j, G = [1 0 0; 1/2 1/2 1/2; 1/2 -1/2 1/2; 0 0 1]
+      // (evaluated in double, rounded once to f32), then split into TF32 halves
+      static const double G[4][3] = {{1, 0, 0}, {0.5, 0.5, 0.5}, {0.5, -0.5, 0.5}, {0, 0, 1}};
+      const size_t plane = static_cast<size_t>(co * op->kp);
+      std::vector<float> hi(16 * plane, 0.0f), lo(16 * plane, 0.0f);
+      for (int64_t o = 0; o < co; ++o)
+        for (int64_t c = 0; c < ci; ++c) {
+          const float* g = &w[static_cast<size_t>((o * ci + c) * 9)];
+          double gg[4][3];  // G g
+          for (int i = 0; i < 4; ++i)
+            for (int j = 0; j < 3; ++j) gg[i][j] = G[i][0] * g[j] + G[i][1] * g[3 + j] + G[i][2] * g[6 + j];
+          for (int i = 0; i < 4; ++i)
+            for (int j = 0; j < 4; ++j) {
+              const float u = static_cast<float>(gg[i][0] * G[j][0] + gg[i][1] * G[j][1] + gg[i][2] * G[j][2]);
+              const size_t at = static_cast<size_t>(4 * i + j) * plane + static_cast<size_t>(o * op->kp + c);
+              split_host(u, hi[at], lo[at]);
+            }
+        }
+      if ((st = own_upload(op, hi.data(), static_cast<int64_t>(hi.size()) * 4, &op->w))) return st;
+      if ((st = own_upload(op, lo.data(), static_cast<int64_t>(lo.size()) * 4, &op->w_lo))) return st;
+      if (has_bias) {
+        if ((st = own_upload(op, b.data(), co * 4, &p))) return st;
+        op->bias_f32 = static_cast<float*>(p);
+      }
+      return LSC_SUCCESS;
+    }
     std::vector<float> wl = oihw_to_ohwi(w.data(), co, ci, op->kh, op->kw, op->kp);
     std::vector<float> hi(wl.size()), lo(wl.size());
     for (size_t i = 0; i < wl.size(); ++i) split_host(wl[i], hi[i], lo[i]);
@@ -372,6 +401,20 @@ lsc_status execute_conv(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_te
     const int64_t hw = g.h * g.w;
     const void* xd = nullptr;
     if ((st = s.input(x, g.n * op->c_in * hw * 4, &xd))) return st;
+    if (op->winograd) {
+      lsc_tensor& y = out[0];
+      if (y.dtype != LSC_DTYPE_F32) return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "Conv2d output must be F32");
+      void* yd = nullptr;
+      if ((st = s.output(y, g.n * g.c_out * g.oh * g.ow * 4, &yd))) return st;
+      set_shape(y, {g.n, g.c_out, g.oh, g.ow});
+      ConvGeometry gw = g;
+      gw.c = op->c_in;
+      float* scratch = static_cast<float*>(s.scratch(winograd_f32_scratch_floats(gw, op->kp, true) * 4));
+      if (!scratch) return LSC_ERROR_OUT_OF_MEMORY;
+      return launch_conv_winograd_f32(static_cast<const float*>(xd), static_cast<const float*>(op->w),
+                                      static_cast<const float*>(op->w_lo), gw, op->kp, op->bias_f32, op->act,
+                                      static_cast<float*>(yd), scratch, true, s.st);
+    }
     const bool split = op->fp32_mode != LSC_FP32_TF32;
     const int64_t nbytes = g.n * hw * g.c * 4;
     float* hi = static_cast<float*>(s.scratch(nbytes));

@@ -63,6 +63,10 @@ struct lsc_op {
   int64_t c_in = 0, kh = 1, kw = 1;
   int32_t sh = 1, sw = 1, ph = 0, pw = 0, dh = 1, dw = 1, groups = 1;
   int32_t ph_end = 0, pw_end = 0;  // bottom / right padding
+  // FP32 Winograd F(2x2, 3x3) form (fp32_mode LSC_FP32_WINOGRAD on a 3x3 stride-1 dilation-1
+  // convolution with symmetric padding): w / w_lo then hold the transformed filter
+  // U = G g G^T as [16][Cout][kp] split-TF32 halves.
+  bool winograd = false;
 
   // pixel-grouped form of a stride-1 INT8 convolution (group_px > 1): the NHWC input viewed
   // as [N, H, W/G, G*C] and the filter expanded to [G*Cout, KH, kw_g, G*C], so that each

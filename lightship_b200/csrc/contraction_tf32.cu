@@ -28,6 +28,12 @@ struct Tf32Params {
   uint32_t* err;
   int32_t ow, ohw, sw, sh, pw, ph, dw, dh, kw;
   int32_t chunks_per_tap, total_chunks, chunk_elems;
+  // batched GEMM (GEMM mode only): `batches` independent products; batch b's A rows start at
+  // b * a_batch_rows of A's tensor map, its B rows at b * b_batch_rows, its output at
+  // out + b * out_batch_stride.  Rows or columns a tile reads past its batch's m / n belong
+  // to the next batch (or lie past the map, zero-filled) and are never stored.
+  int32_t batches, a_batch_rows, b_batch_rows;
+  int64_t out_batch_stride;
 };
 
 template <int BN_, bool SPLIT_>
@@ -135,7 +141,8 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
 
   const int m_tiles = (p.m + C::BM - 1) / C::BM;
   const int n_tiles = (p.n + C::BN - 1) / C::BN;
-  const int num_tiles = m_tiles * n_tiles;
+  const int batch_tiles = m_tiles * n_tiles;
+  const int num_tiles = batch_tiles * p.batches;
   const int kblocks = (p.k + C::BK - 1) / C::BK;
 
   if (warp == 0) {
@@ -144,7 +151,9 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
       int issued = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int mb = tile % m_tiles, nb = tile / m_tiles;
+        const int bz = tile / batch_tiles;
+        const int mb = (tile - bz * batch_tiles) % m_tiles, nb = (tile - bz * batch_tiles) / m_tiles;
+        const int a_row0 = bz * p.a_batch_rows + mb * C::BM, b_row0 = bz * p.b_batch_rows + nb * C::BN;
         int32_t cw = 0, chh = 0, cn = 0;
         if constexpr (ACB > 0) {
           const int m0 = mb * C::BM;
@@ -166,7 +175,7 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
             const CUtensorMap* ta = part == 0 ? &tmAh : &tmAl;
             const CUtensorMap* tb = part == 0 ? &tmBh : &tmBl;
             if constexpr (ACB == 0) {
-              tma_load_2d(ta, &full[stage], a_part(stage, part), kb * C::BK, mb * C::BM);
+              tma_load_2d(ta, &full[stage], a_part(stage, part), kb * C::BK, a_row0);
             } else {
               constexpr int SUB = 128 / ACB;
 #pragma unroll
@@ -182,7 +191,7 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
                                    static_cast<uint16_t>(ky * p.dh));
               }
             }
-            tma_load_2d(tb, &full[stage], b_part(stage, part), kb * C::BK, nb * C::BN);
+            tma_load_2d(tb, &full[stage], b_part(stage, part), kb * C::BK, b_row0);
           }
           ++issued;
           if (++stage == C::STAGES) {
@@ -257,7 +266,9 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
     const int row_in_tile = quarter * 32 + lane;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int mb = tile % m_tiles, nb = tile / m_tiles;
+      const int bz = tile / batch_tiles;
+      const int mb = (tile - bz * batch_tiles) % m_tiles, nb = (tile - bz * batch_tiles) / m_tiles;
+      float* const out_b = p.out + bz * p.out_batch_stride;
       const int buf = local & 1;
       const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
       if (!mbar_wait(&tfull[buf], buf_phase, abort_flag, p.err)) break;
@@ -290,12 +301,12 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
         if (p.out_nchw) {
           const int img = row / p.ohw;
           const int pix = row - img * p.ohw;
-          float* o = p.out + (static_cast<int64_t>(img) * p.n + col0) * p.ohw + pix;
+          float* o = out_b + (static_cast<int64_t>(img) * p.n + col0) * p.ohw + pix;
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (col0 + j < p.n) o[static_cast<int64_t>(j) * p.ohw] = y[j];
         } else {
-          float* o = p.out + static_cast<int64_t>(row) * p.ldo + col0;
+          float* o = out_b + static_cast<int64_t>(row) * p.ldo + col0;
           if (p.vec_ok && col0 + 32 <= p.n) {
 #pragma unroll
             for (int j = 0; j < 8; ++j)
@@ -328,8 +339,8 @@ lsc_status launch_cfg(const CUtensorMap (&tm)[4], const Tf32Params& p, int sm_co
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(contraction_tf32)");
-  const int tiles = ((p.m + C::BM - 1) / C::BM) * ((p.n + C::BN - 1) / C::BN);
-  const int grid = tiles < sm_count ? tiles : sm_count;
+  const int64_t tiles = static_cast<int64_t>((p.m + C::BM - 1) / C::BM) * ((p.n + C::BN - 1) / C::BN) * p.batches;
+  const int grid = tiles < sm_count ? static_cast<int>(tiles) : sm_count;
   contraction_tf32_kernel<BN, ACB, SPLIT>
       <<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3], p);
   LSC_CUDA_TRY(cudaGetLastError());
@@ -354,17 +365,17 @@ lsc_status check_ptr16(const void* p, const char* what) {
 
 }  // namespace
 
-lsc_status launch_gemm_tf32(const float* a_hi, const float* a_lo, const float* b_hi,
-                            const float* b_lo, int64_t m, int64_t n, int64_t k,
-                            const float* bias, int act, float* out, int64_t ldo, bool split,
-                            cudaStream_t stream) {
-  if (m < 0 || n < 0 || k < 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_tf32: negative size");
-  if (m == 0 || n == 0) return LSC_SUCCESS;
+lsc_status launch_gemm_tf32_batched(const float* a_hi, const float* a_lo, const float* b_hi,
+                                    const float* b_lo, int64_t batches, int64_t m, int64_t n, int64_t k,
+                                    const float* bias, int act, float* out, int64_t ldo,
+                                    int64_t out_batch_stride, bool split, cudaStream_t stream) {
+  if (m < 0 || n < 0 || k < 0 || batches < 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_tf32: negative size");
+  if (m == 0 || n == 0 || batches == 0) return LSC_SUCCESS;
   if (!a_hi || !b_hi || !out || (split && (!a_lo || !b_lo)))
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_tf32: null operand");
   if (k == 0 || k % 4 != 0)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_tf32: K must be a positive multiple of 4");
-  if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2)
+  if (batches * m > INT32_MAX / 2 || batches * n > INT32_MAX / 2 || k > INT32_MAX / 2)
     return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_tf32: size too large");
   if (act < LSC_ACT_NONE || act > LSC_ACT_GELU) return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_tf32: bad activation");
   lsc_status st;
@@ -379,7 +390,7 @@ lsc_status launch_gemm_tf32(const float* a_hi, const float* a_lo, const float* b
   const float* srcs[4] = {a_hi, split ? a_lo : a_hi, b_hi, split ? b_lo : b_hi};
   for (int i = 0; i < 4; ++i) {
     const bool is_a = i < 2;
-    st = encode_tmap_2d(&tm[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, srcs[i], k, is_a ? m : n, k * 4, 32,
+    st = encode_tmap_2d(&tm[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, srcs[i], k, batches * (is_a ? m : n), k * 4, 32,
                         is_a ? 128 : bn, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
   }
@@ -392,9 +403,20 @@ lsc_status launch_gemm_tf32(const float* a_hi, const float* a_lo, const float* b
   p.out = out;
   p.ldo = ldo;
   p.out_nchw = 0;
-  p.vec_ok = ((reinterpret_cast<uintptr_t>(out) & 15) == 0 && ldo % 4 == 0) ? 1 : 0;
+  p.vec_ok = ((reinterpret_cast<uintptr_t>(out) & 15) == 0 && ldo % 4 == 0 && out_batch_stride % 4 == 0) ? 1 : 0;
   p.err = ds->err_word;
+  p.batches = static_cast<int32_t>(batches);
+  p.a_batch_rows = static_cast<int32_t>(m);
+  p.b_batch_rows = static_cast<int32_t>(n);
+  p.out_batch_stride = out_batch_stride;
   return launch_acb<0>(bn, split, tm, p, ds->sm_count, stream);
+}
+
+lsc_status launch_gemm_tf32(const float* a_hi, const float* a_lo, const float* b_hi,
+                            const float* b_lo, int64_t m, int64_t n, int64_t k,
+                            const float* bias, int act, float* out, int64_t ldo, bool split,
+                            cudaStream_t stream) {
+  return launch_gemm_tf32_batched(a_hi, a_lo, b_hi, b_lo, 1, m, n, k, bias, act, out, ldo, 0, split, stream);
 }
 
 lsc_status launch_conv_tf32(const float* x_hi, const float* x_lo, const float* w_hi,
@@ -478,6 +500,7 @@ lsc_status launch_conv_tf32(const float* x_hi, const float* x_lo, const float* w
   p.chunks_per_tap = static_cast<int32_t>(chunks_per_tap);
   p.total_chunks = static_cast<int32_t>(total_chunks);
   p.chunk_elems = acb / 4;
+  p.batches = 1;
   switch (acb) {
     case 128: return launch_acb<128>(bn, split, tm, p, ds->sm_count, stream);
     case 64: return launch_acb<64>(bn, split, tm, p, ds->sm_count, stream);

@@ -128,6 +128,19 @@ lsc_status launch_gemm_tf32(const float* a_hi, const float* a_lo, const float* b
 lsc_status launch_conv_tf32(const float* x_hi, const float* x_lo, const float* w_hi,
                             const float* w_lo, const ConvGeometry& g, const float* bias, int act,
                             float* out_nchw, bool split, cudaStream_t stream);
+// `batches` GEMMs in one launch: batch b's A is rows [b*m, (b+1)*m) of a_hi/a_lo, its B rows
+// [b*n, (b+1)*n) of b_hi/b_lo, its output out + b * out_batch_stride.
+lsc_status launch_gemm_tf32_batched(const float* a_hi, const float* a_lo, const float* b_hi,
+                                    const float* b_lo, int64_t batches, int64_t m, int64_t n, int64_t k,
+                                    const float* bias, int act, float* out, int64_t ldo,
+                                    int64_t out_batch_stride, bool split, cudaStream_t stream);
+// FP32 3x3 stride-1 convolution as Winograd F(2x2, 3x3) (winograd_f32.cu): NCHW input with
+// g.c channels, transformed filter u [16][Cout][cp] (hi/lo), NCHW output; `scratch` holds
+// winograd_f32_scratch_floats(g, cp, split) floats.
+int64_t winograd_f32_scratch_floats(const ConvGeometry& g, int64_t cp, bool split);
+lsc_status launch_conv_winograd_f32(const float* x_nchw, const float* u_hi, const float* u_lo,
+                                    const ConvGeometry& g, int64_t cp, const float* bias, int act,
+                                    float* out_nchw, float* scratch, bool split, cudaStream_t stream);
 // Operand preparation (tf32_prep.cu): split into hi/lo parts with padding / transposition.
 lsc_status prep_split_rows(const float* x, int64_t rows, int64_t cols, int64_t ld, float* hi,
                            float* lo, cudaStream_t st);

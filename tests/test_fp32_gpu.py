@@ -403,3 +403,77 @@ def test_conv_int8_groups(be, ci, co, groups, stride):
     assert q.shape == list(want[0].shape)
     np.testing.assert_array_equal(acc.numpy().reshape(want[2].shape), want[2])
     np.testing.assert_array_equal(q.numpy().reshape(want[0].shape), want[0])
+
+
+# ------------------------------------------------------------------------------ Winograd
+TOL_WINOGRAD = 1e-4  # |y - y_oracle| <= tol * (sum |x * w| + |bias|): transforms + split-TF32
+
+
+@pytest.mark.parametrize("n,ci,co,h,wd,p", [(1, 64, 64, 56, 56, 1), (2, 5, 7, 9, 11, 1), (1, 16, 8, 10, 10, 0),
+                                            (1, 8, 70, 7, 7, 2), (3, 3, 4, 6, 5, 1), (2, 130, 96, 15, 13, 1)])
+def test_conv_winograd_matches_oracle(be, n, ci, co, h, wd, p):
+    """fp32_mode LSC_FP32_WINOGRAD: the 3x3 stride-1 convolution as Winograd F(2x2, 3x3)
+    (input transform, 16-batch split-TF32 GEMM, output transform) against the oracle's direct
+    convolution; odd output sizes, channel counts off the 4 / 32 / 64 grids, padding 0-2."""
+    B = _B()
+    rng = np.random.default_rng(n * 1000 + ci * 7 + co + p)
+    x = rng.normal(size=(n, ci, h, wd)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2 / (9 * ci)), size=(co, ci, 3, 3)).astype(np.float32)
+    bias = rng.normal(size=co).astype(np.float32)
+    xt = B.Tensor("x", list(x.shape), B.DataType.F32, x)
+    oh, ow = h + 2 * p - 2, wd + 2 * p - 2
+    y = B.Tensor("y", [1], B.DataType.F32, np.full(n * co * oh * ow, np.nan, np.float32))
+    _run(be, B.OperatorDef("conv", B.OperatorType.Conv2d, padding=(p, p), fp32_mode=_lib().FP32_WINOGRAD),
+         [xt, B.Tensor("w", list(w.shape), B.DataType.F32, w), B.Tensor("b", [co], B.DataType.F32, bias)], [y],
+         runtime_inputs=[xt])
+    ref = orc.conv2d_nchw(x, w, bias, (1, 1), (p, p))
+    mag = orc.conv2d_nchw(np.abs(x), np.abs(w), None, (1, 1), (p, p)).astype(np.float64) + np.abs(bias)[None, :, None, None]
+    assert y.shape == list(ref.shape)
+    assert _rel_err(y.numpy().reshape(ref.shape), ref, mag) <= TOL_WINOGRAD
+
+
+def test_conv_winograd_bn_relu_config(be):
+    """The FP32 Conv2d workload (1x64x56x56, 3x3 s1 p1, bias, folded BatchNorm, ReLU) on the
+    Winograd path."""
+    B = _B()
+    rng = np.random.default_rng(56)
+    x = rng.normal(size=(1, 64, 56, 56)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2 / 576), size=(64, 64, 3, 3)).astype(np.float32)
+    bias = rng.normal(0, 0.1, 64).astype(np.float32)
+    g, beta, mu, var = _bn_params(rng, 64)
+    T = lambda n, a: B.Tensor(n, list(a.shape), B.DataType.F32, a)
+    xt = T("x", x)
+    y = B.Tensor("y", [1], B.DataType.F32, np.zeros(64 * 56 * 56, np.float32))
+    opdef = B.OperatorDef("conv", B.OperatorType.Conv2d, padding=(1, 1), activation=B.Activation.ReLU,
+                          fp32_mode=_lib().FP32_WINOGRAD)
+    _run(be, opdef, [xt, T("w", w), T("b", bias), T("g", g), T("beta", beta), T("mu", mu), T("var", var)],
+         [y], fusion=B.FusionInfo.conv_batch_norm(), runtime_inputs=[xt])
+    ref = orc.act(orc.batchnorm_inference(orc.conv2d_nchw(x, w, bias, pad=(1, 1)), g, beta, mu, var),
+                  orc.ACT_RELU)
+    f = (g / np.sqrt(var + np.float32(1e-5))).astype(np.float64)
+    mag = orc.conv2d_nchw(np.abs(x), np.abs(w), pad=(1, 1)).astype(np.float64) * f[None, :, None, None] \
+        + np.abs(f * (bias - mu) + beta)[None, :, None, None]
+    assert _rel_err(y.numpy().reshape(ref.shape), ref, mag) <= TOL_WINOGRAD
+
+
+def test_conv_winograd_mode_leaves_other_convolutions_direct(be):
+    """Under fp32_mode LSC_FP32_WINOGRAD a 5x5 or strided convolution runs the direct kernel."""
+    B = _B()
+    rng = np.random.default_rng(9)
+    x = rng.normal(size=(1, 8, 12, 12)).astype(np.float32)
+    for k, s in ((5, 1), (3, 2)):
+        w = rng.normal(0, 0.2, size=(8, 8, k, k)).astype(np.float32)
+        xt = B.Tensor("x", list(x.shape), B.DataType.F32, x)
+        oh = (12 + 2 - k) // s + 1
+        y = B.Tensor("y", [1], B.DataType.F32, np.zeros(8 * oh * oh, np.float32))
+        _run(be, B.OperatorDef("conv", B.OperatorType.Conv2d, stride=(s, s), padding=(1, 1),
+                               fp32_mode=_lib().FP32_WINOGRAD),
+             [xt, B.Tensor("w", list(w.shape), B.DataType.F32, w)], [y], runtime_inputs=[xt])
+        ref = orc.conv2d_nchw(x, w, None, (s, s), (1, 1))
+        mag = orc.conv2d_nchw(np.abs(x), np.abs(w), None, (s, s), (1, 1)).astype(np.float64)
+        assert _rel_err(y.numpy().reshape(ref.shape), ref, mag) <= TOL_3XTF32
+
+
+def _lib():
+    from lightship_b200 import _lib as L
+    return L
