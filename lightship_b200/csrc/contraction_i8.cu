@@ -86,11 +86,22 @@ constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per block (2
 // to producer (it * L + j) % kProducers, L = loads per k-block, and the producer of load 0
 // posts the stage's byte count.  Another producer's bytes may land first; the mbarrier's
 // tx-count then goes negative for a while, and the phase still completes only after that
-// arrive.  The ring needs at least kProducers stages (so a producer's parity wait on `empty`
-// cannot alias a phase two rounds back).  The producers are lanes 0-1 of warps 0-1: separate
-// threads are what matters (measured: two lanes of one warp deliver 44 B/clk, two warps 49),
-// and 19 warps keep the 96 registers per thread that a fifth warp on one SM sub-partition
-// (21 warps) would cut to 80.
+// arrive.  A producer waits only on the slots it loads into, and the ring needs at least
+// kProducers stages: a producer's loads are then less than a ring round apart, so its parity
+// wait on `empty` cannot alias a phase two rounds back.  (Waiting on every slot does not lift
+// that limit: a producer behind the others can then meet a slot two phases ahead and wait for
+// a phase that needs its own load; measured on B200 as a bounded-wait timeout.)  The producers
+// are lanes 0-1 of warps 0-1: separate threads are what matters (measured: two lanes of one
+// warp deliver 44 B/clk, two warps 49), and 19 warps keep the 96 registers per thread that a
+// fifth warp on one SM sub-partition (21 warps) would cut to 80.  Measured and not kept on
+// B200: eight producers as lanes 0-3 of the same two warps (ResNet-18 step 1.087 -> 1.120 ms
+// at batch 256, 0.275 -> 0.336 ms at batch 32: four lanes of one warp spinning on different
+// barriers and issuing copies serialise each other), dealing the A loads round-robin over
+// all four producers instead of two (4096^3 GEMM 2554 -> 2468 TOPS), and the producer count
+// as a runtime value (its modulo in every iteration cost 3 % at batch 256, 12 % at batch 32:
+// the producers set the pace of small-batch convolutions, which is also why the im2col tap
+// coordinates come from a stepped cursor, TapCursor, instead of two divisions per load:
+// 1.096 -> 1.083 ms at batch 256, 0.278 -> 0.268 ms at batch 32).
 constexpr int kProducerWarps = 2;
 constexpr int kProducerLanes = 2;
 constexpr int kProducers = kProducerWarps * kProducerLanes;
@@ -138,6 +149,33 @@ __device__ __noinline__ void drain_in_flight(uint64_t* full, int stages, int it_
 // Index, among this producer's loads of iteration `it`, of its first load (>= L: none).
 __device__ __forceinline__ int first_load_of(int pr, int it, int L) {
   return (pr - (it * L) % kProducers + kProducers) % kProducers;
+}
+
+// Channel chunk jc of a convolution's K dimension, in (kh, kw, c) order, as (chunk within its
+// tap, kx, ky), advanced one chunk at a time.  The producers keep one per tile and step it by
+// the k-block's chunk count every iteration instead of dividing jc by the chunks per tap and
+// the tap by KW: the producer threads set the pace of small-batch convolutions, and two
+// integer divisions per load are a visible share of their time.
+struct TapCursor {
+  int ci = 0, kx = 0, ky = 0, jc = 0;
+  __device__ __forceinline__ void step(int chunks_per_tap, int kw) {
+    ++jc;
+    if (++ci == chunks_per_tap) {
+      ci = 0;
+      if (++kx == kw) {
+        kx = 0;
+        ++ky;
+      }
+    }
+  }
+};
+
+// The cursor `n` chunks past `c` (n < 8), or chunk 0 once past the filter (its weights are
+// zero there, so any in-bounds load serves).
+__device__ __forceinline__ TapCursor tap_at(TapCursor c, int n, const I8Params& p) {
+  for (int t = 0; t < n; ++t) c.step(p.chunks_per_tap, p.kw);
+  if (c.jc >= p.total_chunks) c = TapCursor{};
+  return c;
 }
 
 template <int BN_>
@@ -485,12 +523,18 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
           cw = ox * p.sw - p.pw;
           chh = oy * p.sh - p.ph;
         }
+        TapCursor cur;  // chunk kb * SUB (convolution only)
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int stage = ring_stage;
           const uint32_t phase = ring_phase;
           if (++ring_stage == stages) {
             ring_stage = 0;
             ring_phase ^= 1u;
+          }
+          const TapCursor base = cur;
+          if constexpr (ACB > 0) {
+#pragma unroll
+            for (int t = 0; t < SUB; ++t) cur.step(p.chunks_per_tap, p.kw);
           }
           const int j0 = first_load_of(pr, it, L);
           if (j0 >= L) continue;
@@ -508,14 +552,9 @@ __global__ void __launch_bounds__(I8Cfg<BN>::THREADS, 1)
             } else if constexpr (ACB == 0) {
               tma_load_2d(&tmA, &full[stage], a_dst, kb * C::BK, mb * C::BM);
             } else {
-              int jc = kb * SUB + j;  // channel chunk index in (kh, kw, c) order
-              if (jc >= p.total_chunks) jc = 0;  // past the filter: weights are zero there
-              const int tap = jc / p.chunks_per_tap;
-              const int c0 = (jc - tap * p.chunks_per_tap) * ACB;
-              const int ky = tap / p.kw;
-              const int kx = tap - ky * p.kw;
-              tma_load_im2col_4d(&tmA, &full[stage], a_dst + j * (C::BM * ACB), c0, cw, chh, cn,
-                                 static_cast<uint16_t>(kx * p.dw), static_cast<uint16_t>(ky * p.dh));
+              const TapCursor c = tap_at(base, j, p);  // chunk kb * SUB + j
+              tma_load_im2col_4d(&tmA, &full[stage], a_dst + j * (C::BM * ACB), c.ci * ACB, cw, chh, cn,
+                                 static_cast<uint16_t>(c.kx * p.dw), static_cast<uint16_t>(c.ky * p.dh));
             }
           }
           if (j0 == 0) plog->slot_it[stage] = it;
@@ -1123,6 +1162,7 @@ __global__ void __launch_bounds__(SwapCfg::THREADS, 1)
           cw[h] = ox * p.sw - p.pw;
           chh[h] = oy * p.sh - p.ph;
         }
+        TapCursor cur;  // chunk kb * SUB
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int stage = ring_stage;
           const uint32_t phase = ring_phase;
@@ -1130,6 +1170,9 @@ __global__ void __launch_bounds__(SwapCfg::THREADS, 1)
             ring_stage = 0;
             ring_phase ^= 1u;
           }
+          const TapCursor base = cur;
+#pragma unroll
+          for (int t = 0; t < SUB; ++t) cur.step(p.chunks_per_tap, p.kw);
           const int j0 = first_load_of(pr, it, L);
           if (j0 >= L) continue;
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
@@ -1143,14 +1186,9 @@ __global__ void __launch_bounds__(SwapCfg::THREADS, 1)
               tma_load_2d(&tmW, &full[stage], sW + stage * S::W_BYTES, kb * S::BK, 0);
             } else {
               const int i = (j - 1) >> 1, h = (j - 1) & 1;
-              int jc = kb * SUB + i;             // channel chunk index in (kh, kw, c) order
-              if (jc >= p.total_chunks) jc = 0;  // past the filter: weights are zero there
-              const int tap = jc / p.chunks_per_tap;
-              const int c0 = (jc - tap * p.chunks_per_tap) * ACB;
-              const int ky = tap / p.kw;
-              const int kx = tap - ky * p.kw;
-              tma_load_im2col_4d(&tmX, &full[stage], x_dst + i * (S::BP * ACB) + h * (128 * ACB), c0, cw[h], chh[h],
-                                 cn[h], static_cast<uint16_t>(kx * p.dw), static_cast<uint16_t>(ky * p.dh));
+              const TapCursor c = tap_at(base, i, p);  // chunk kb * SUB + i
+              tma_load_im2col_4d(&tmX, &full[stage], x_dst + i * (S::BP * ACB) + h * (128 * ACB), c.ci * ACB, cw[h],
+                                 chh[h], cn[h], static_cast<uint16_t>(c.kx * p.dw), static_cast<uint16_t>(c.ky * p.dh));
             }
           }
           if (j0 == 0) plog->slot_it[stage] = it;

@@ -104,40 +104,53 @@ __global__ void quantize_nchw_to_s2d_kernel(const float* __restrict__ x, int8_t*
       make_uint4(wd[0], wd[1], wd[2], wd[3]);
 }
 
-// The same for the CNN stem's case, C = 3 input channels, 2x2 blocks, 16 stored channels:
-// everything but the pixel position is a compile-time constant.
+// The same for the CNN stem's case, C = 3 input channels, 2x2 blocks, 16 stored channels,
+// image width a multiple of 4.  grid (1, output row, image), 128 threads, 24 * w bytes of
+// dynamic shared memory: the block first stages its two input rows of the three channels
+// with 16-byte loads (rows outside the image as zeros), then each thread builds whole 16-byte
+// output pixels from shared memory (channel j = (dy * 2 + dx) * 3 + c, bytes 12-15 zero; a
+// padding tap quantizes 0, which is code 0).  Reading the rows whole, instead of each thread
+// gathering its twelve pixels with scalar loads, keeps the kernel at HBM speed.
 template <int RND>
-__global__ void quantize_nchw_to_s2d_c3b2_kernel(const float* __restrict__ x, int8_t* __restrict__ y,
-                                                 int h, int w, int ph, int pw, int hs, int ws,
-                                                 float scale, float inv_s) {
+__global__ void __launch_bounds__(128) quantize_nchw_to_s2d_c3b2_kernel(const float* __restrict__ x,
+                                                                        int8_t* __restrict__ y, int h, int w,
+                                                                        int ph, int pw, int hs, int ws,
+                                                                        float scale, float inv_s) {
+  extern __shared__ float srow[];  // [dy * 3 + c][w]
   griddep_wait();  // launched as a dependent kernel: inputs and outputs are settled from here on
   griddep_launch_dependents();
   const int ys = blockIdx.y, img = blockIdx.z;
-  const int xs = blockIdx.x * blockDim.x + threadIdx.x;
-  if (xs >= ws) return;
   const int plane = h * w;
   const float* xi = x + static_cast<size_t>(img) * 3 * plane;
-  uint32_t wd[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int dy = 0; dy < 2; ++dy) {
+  const int w4 = w >> 2;
+  for (int i = threadIdx.x; i < 6 * w4; i += blockDim.x) {
+    const int r = i / w4, q = i - r * w4;
+    const int dy = r / 3, cc = r - dy * 3;
     const int iy = ys * 2 + dy - ph;
-    const bool row_ok = iy >= 0 && iy < h;
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (iy >= 0 && iy < h) v = __ldg(reinterpret_cast<const float4*>(xi + cc * plane + iy * w) + q);
+    reinterpret_cast<float4*>(srow + r * w)[q] = v;
+  }
+  __syncthreads();
+  for (int xs = threadIdx.x; xs < ws; xs += blockDim.x) {
+    uint32_t wd[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int dx = 0; dx < 2; ++dx) {
-      const int ix = xs * 2 + dx - pw;
-      if (row_ok && ix >= 0 && ix < w) {
-        const float* px = xi + iy * w + ix;
+    for (int dy = 0; dy < 2; ++dy) {
+#pragma unroll
+      for (int dx = 0; dx < 2; ++dx) {
+        const int ix = xs * 2 + dx - pw;
+        if (ix < 0 || ix >= w) continue;
 #pragma unroll
         for (int cc = 0; cc < 3; ++cc) {
           const int j = (dy * 2 + dx) * 3 + cc;
-          const int32_t q = requant_one<RND>(__ldg(px + cc * plane), scale, inv_s);
+          const int32_t q = requant_one<RND>(srow[(dy * 3 + cc) * w + ix], scale, inv_s);
           wd[j >> 2] |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * (j & 3));
         }
       }
     }
+    reinterpret_cast<uint4*>(y + ((static_cast<size_t>(img) * hs + ys) * ws + xs) * 16)[0] =
+        make_uint4(wd[0], wd[1], wd[2], wd[3]);
   }
-  reinterpret_cast<uint4*>(y + ((static_cast<size_t>(img) * hs + ys) * ws + xs) * 16)[0] =
-      make_uint4(wd[0], wd[1], wd[2], wd[3]);
 }
 
 __device__ __forceinline__ uint32_t vmax_s8x4(uint32_t a, uint32_t b) { return __vmaxs4(a, b); }
@@ -338,15 +351,17 @@ lsc_status launch_quantize_nchw_to_s2d_i8(const float* x, int8_t* y, int64_t n, 
   const dim3 grid(static_cast<unsigned>((per_row + 127) / 128), static_cast<unsigned>(hs), static_cast<unsigned>(n));
   const int ic = static_cast<int>(c), ih = static_cast<int>(h), iw = static_cast<int>(w);
   const float inv_s = reciprocal_or_zero(scale);
-  if (c == 3 && blk == 2 && cp == 16) {
-    const dim3 g2(static_cast<unsigned>((ws + 127) / 128), static_cast<unsigned>(hs), static_cast<unsigned>(n));
+  if (c == 3 && blk == 2 && cp == 16 && w % 4 == 0 && w <= 2048 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const dim3 g2(1u, static_cast<unsigned>(hs), static_cast<unsigned>(n));
+    const size_t smem = static_cast<size_t>(24 * w);
     if (rounding == LSC_ROUND_HALF_EVEN)
       LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, quantize_nchw_to_s2d_c3b2_kernel<LSC_ROUND_HALF_EVEN>, g2,
-                                    dim3(128), 0, st, x, y, ih, iw, static_cast<int>(ph), static_cast<int>(pw),
+                                    dim3(128), smem, st, x, y, ih, iw, static_cast<int>(ph), static_cast<int>(pw),
                                     static_cast<int>(hs), static_cast<int>(ws), scale, inv_s));
     else
       LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, quantize_nchw_to_s2d_c3b2_kernel<LSC_ROUND_HALF_AWAY>, g2,
-                                    dim3(128), 0, st, x, y, ih, iw, static_cast<int>(ph), static_cast<int>(pw),
+                                    dim3(128), smem, st, x, y, ih, iw, static_cast<int>(ph), static_cast<int>(pw),
                                     static_cast<int>(hs), static_cast<int>(ws), scale, inv_s));
     LSC_CUDA_TRY(cudaGetLastError());
     return LSC_SUCCESS;
