@@ -101,7 +101,10 @@ constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per block (2
 // as a runtime value (its modulo in every iteration cost 3 % at batch 256, 12 % at batch 32:
 // the producers set the pace of small-batch convolutions, which is also why the im2col tap
 // coordinates come from a stepped cursor, TapCursor, instead of two divisions per load:
-// 1.096 -> 1.083 ms at batch 256, 0.278 -> 0.268 ms at batch 32).
+// 1.096 -> 1.083 ms at batch 256, 0.278 -> 0.268 ms at batch 32), and six producers as lanes
+// 0-1 of three warps (20 warps, still 96 registers; loads dealt without divisions: 1.082 ->
+// 1.094 ms at batch 256, 0.268 -> 0.276 ms at batch 32 -- the extra spinning warp takes issue
+// slots from the MMA and epilogue warps of its sub-partition).
 constexpr int kProducerWarps = 2;
 constexpr int kProducerLanes = 2;
 constexpr int kProducers = kProducerWarps * kProducerLanes;
