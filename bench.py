@@ -1063,7 +1063,7 @@ def run_gpu(args):
         "roofline": {"bound": "tensor", "kernel": "contraction_i8_kernel + contraction_i8_swap_kernel (INT8 implicit-GEMM conv)",
                      "achieved": conv_tops, "peak": int8_peak, "unit": "TOPS",
                      "frac": conv_tops / int8_peak if conv_tops else None,
-                     "traffic": load_profile_value("contraction_i8_conv_layer1_b256.md", "traffic_bytes_per_launch"),
+                     "traffic": load_profile_value("contraction_i8_swap_conv_layer1.md", "traffic_bytes_per_launch"),
                      "peak_source": peak_source,
                      "conv_share_of_step": share,
                      "method": "achieved = algorithmic conv ops / (graph step time x the conv kernels' share of the "
