@@ -588,6 +588,13 @@ RESNET_GOPS_PER_IMAGE = 3.628  # 2 x MACs incl. the classifier, standard stem ma
 RESNET_KERNELS = 24  # input quantize, 20 convolutions, max pool, average pool, classifier
 
 
+def resnet_kernels(per_gpu_batch, sm_count):
+    """Kernel launches of one INT8-session pass: the session runs the stem's convolution and max
+    pool as one launch when there are at least 16 four-row bands of the 112-row stem output per
+    SM (28 per image)."""
+    return RESNET_KERNELS - (1 if per_gpu_batch * 28 >= 16 * sm_count else 0)
+
+
 def session_scales(sess):
     """The INT8 session's calibrated scales under the layer names of lightship_b200.resnet18."""
     from lightship_b200.resnet18 import build_params
@@ -1075,7 +1082,7 @@ def run_gpu(args):
                 "pipelined": "step i+1's upload (the session's copy stream) overlaps step i's network; every step's "
                              "upload and logits download are inside the timed region",
                 "sequential_value": batch / (e2e_seq_ms * 1e-3), "matches_device_run": e2e_ok},
-        "gpu_launches": RESNET_KERNELS * args.steps,
+        "gpu_launches": resnet_kernels(per, torch.cuda.get_device_properties(local).multi_processor_count) * args.steps,
         "clocks": clocks,
     }
     del sess, model

@@ -477,6 +477,29 @@ lsc_status execute_conv(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_te
                         static_cast<const int8_t*>(rd), r_scale, s.st);
 }
 
+lsc_status execute_conv_pool(const lsc_op* op, const lsc_tensor& x, lsc_tensor& y, cudaStream_t st) {
+  if (op->kind != OpKind::kConvI8 || op->act != LSC_ACT_RELU || !op->w_grouped)
+    return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "conv + max pool: a pixel-grouped INT8 ReLU convolution only");
+  if (!is_int8(x.dtype) || x.ndim != 4 || x.shape[3] != op->kp || x.location != LSC_MEM_DEVICE ||
+      y.location != LSC_MEM_DEVICE || !is_int8(y.dtype))
+    return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "conv + max pool: device int8 NHWC tensors only");
+  ConvGeometry g{};
+  lsc_status s = geometry_from(op, x, true, g);
+  if (s) return s;
+  ConvGeometry gg{};
+  if (!grouped_geometry(op, g, gg))
+    return set_error(LSC_ERROR_UNSUPPORTED_OPERATOR, "conv + max pool: the convolution does not run pixel-grouped here");
+  const int64_t bytes = g.n * (g.oh / 2) * (g.ow / 2) * g.c_out;
+  if (y.nbytes && y.nbytes < static_cast<uint64_t>(bytes))
+    return set_error(LSC_ERROR_SHAPE_MISMATCH, "conv + max pool: output '%s' needs %lld bytes", tname(y), (long long)bytes);
+  const float s_out = y.quant.count > 0 && y.quant.scale && y.quant.scale[0] > 0.0f ? y.quant.scale[0] : op->s_out;
+  s = launch_conv_pool_i8(static_cast<const int8_t*>(x.data), static_cast<const int8_t*>(op->w_grouped), gg,
+                          op->group_px, op->bias_grouped, op->scale_grouped, s_out, op->act, op->rounding,
+                          static_cast<int8_t*>(y.data), st);
+  if (s == LSC_SUCCESS) set_shape(y, {g.n, g.oh / 2, g.ow / 2, g.c_out});
+  return s;
+}
+
 // ------------------------------------------------------------------------------ pooling (INT8 NHWC)
 lsc_status compile_pool(lsc_op* op, const lsc_tensor* in, int n_in, int n_out, bool global) {
   if (n_in < 1 || n_out < 1) return set_error(LSC_ERROR_INVALID_ARGUMENT, "Missing input or output");

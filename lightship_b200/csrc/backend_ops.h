@@ -134,6 +134,10 @@ struct Staging {
 lsc_status compile_conv(lsc_op* op, const lsc_tensor* in, int n_in, const lsc_tensor* out, int n_out);
 lsc_status execute_conv(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out, int n_out,
                         Staging& s);
+// The INT8 session's fused stem: compiled pixel-grouped ReLU convolution `op` and the 3x3 / 2
+// max pool of padding 1 after it, in one launch, into the pooled int8 NHWC y (device tensors).
+// LSC_ERROR_UNSUPPORTED_OPERATOR (nothing launched) when the convolution does not qualify.
+lsc_status execute_conv_pool(const lsc_op* op, const lsc_tensor& x, lsc_tensor& y, cudaStream_t st);
 lsc_status compile_matmul_f32(lsc_op* op, const lsc_tensor* in, int n_in, int n_out);
 lsc_status execute_matmul_f32(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_tensor* out,
                               int n_out, Staging& s);

@@ -103,6 +103,13 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
                           const int32_t* bias, const float* scale, float s_out, int act,
                           int rounding, int8_t* out_i8, float* out_f32, int32_t* out_i32,
                           const int8_t* residual, float res_scale, cudaStream_t stream);
+// A pixel-grouped ReLU convolution (grouped geometry g: the NHWC input viewed with `group`
+// pixels per row group, filter [256 = group * Cout, KH, KWg, C]) with the 3x3 / 2 max pool of
+// padding 1 over its ungrouped output fused in: out_pool is [N, OH / 2, OW * group / 2, Cout]
+// int8 (the CNN stem's convolution and max pool in one launch; contraction_i8.cu).
+lsc_status launch_conv_pool_i8(const int8_t* x, const int8_t* w, const ConvGeometry& g, int group,
+                               const int32_t* bias, const float* scale, float s_out, int act, int rounding,
+                               int8_t* out_pool, cudaStream_t stream);
 
 // INT8 GEMM + requant/dequant epilogue (contraction_i8.cu).  ldo = row stride of the outputs in
 // elements.  Validates its arguments.

@@ -849,6 +849,8 @@ struct QStep {
   bool side = false;       // runs on the second stream beside the step before it
   int pos = 0;             // schedule position (liveness)
   lsc_op* op = nullptr;
+  // max pool window (kernel, stride, padding), square
+  int pool_k = 0, pool_s = 0, pool_p = 0;
   // stem (space-to-depth) geometry
   bool s2d = false;
   int64_t s2d_pad = 0, s2d_extra = 0;
@@ -1115,6 +1117,11 @@ lsc_status lower_int8(QSession& q, const lsc_model& m) {
       const QVal& x = q.vals[in];
       st.kind = QStep::kMaxPool;
       st.in = in;
+      if (d.kernel_h == d.kernel_w && d.stride_h == d.stride_w && d.pad_h == d.pad_w) {
+        st.pool_k = d.kernel_h;
+        st.pool_s = d.stride_h;
+        st.pool_p = d.pad_h;
+      }
       st.out = add_val(n.out[0], (x.h + 2 * d.pad_h - d.kernel_h) / d.stride_h + 1,
                        (x.w + 2 * d.pad_w - d.kernel_w) / d.stride_w + 1, x.c);
       q.steps.push_back(st);
@@ -1149,6 +1156,21 @@ lsc_status lower_int8(QSession& q, const lsc_model& m) {
 }
 
 // Schedule positions, second-stream steps and each value's live range.
+// Step i is a ReLU convolution whose output only the 3x3 / 2 max pool (padding 1) of step i + 1
+// reads, both on the main stream: they can run as one launch (lsc::execute_conv_pool decides
+// whether the compiled convolution qualifies).
+bool pool_fusable(const QSession& q, size_t i) {
+  if (i + 1 >= q.steps.size()) return false;
+  const QStep& c = q.steps[i];
+  const QStep& m = q.steps[i + 1];
+  if (c.kind != QStep::kConv || m.kind != QStep::kMaxPool || c.side || m.side || c.res >= 0 || m.in != c.out ||
+      c.act != LSC_ACT_RELU || m.pool_k != 3 || m.pool_s != 2 || m.pool_p != 1)
+    return false;
+  for (size_t j = 0; j < q.steps.size(); ++j)
+    if (j != i + 1 && (q.steps[j].in == c.out || q.steps[j].res == c.out)) return false;
+  return true;
+}
+
 void schedule_int8(QSession& q) {
   int pos = 0;
   int prev_conv_in = -1;
@@ -1171,6 +1193,10 @@ void schedule_int8(QSession& q) {
     for (int r : {s.in, s.res})
       if (r >= 0) q.vals[r].last = std::max(q.vals[r].last, s.pos);
   }
+  // a max pool fused into the convolution before it is written while that convolution still
+  // reads its input: its output lives from the convolution on
+  for (size_t i = 0; i + 1 < q.steps.size(); ++i)
+    if (pool_fusable(q, i)) q.vals[q.steps[i + 1].out].def = q.steps[i].pos;
   for (auto& v : q.vals)
     if (v.last < v.def) v.last = v.def;
 }
@@ -1375,6 +1401,7 @@ lsc_status calibrate_int8(QSession& q, const lsc_model& m, const float* x, cudaS
 // and the next step joins it.
 lsc_status enqueue_int8(QSession& q, const float* in, cudaStream_t main) {
   float sc_a = 0.0f, sc_b = 0.0f, sc_c = 0.0f;
+  bool pool_done = false;
   size_t fork_i = 0, join_i = 0;
   bool side_open = false;
   for (size_t i = 0; i < q.steps.size(); ++i) {
@@ -1393,6 +1420,10 @@ lsc_status enqueue_int8(QSession& q, const float* in, cudaStream_t main) {
     }
     cudaStream_t st = stp.side ? q.side_stream : main;
     side_open |= stp.side;
+    if (pool_done) {
+      pool_done = false;
+      continue;
+    }
     if (stp.kind == QStep::kInput) {
       lsc_tensor xi = f32_dev("input", {q.in_shape[0], q.in_shape[1], q.in_shape[2], q.in_shape[3]}, const_cast<float*>(in));
       lsc_tensor xo = q_tensor(q.vals[stp.out], q.ptr(stp.out), &sc_b);
@@ -1406,6 +1437,18 @@ lsc_status enqueue_int8(QSession& q, const float* in, cudaStream_t main) {
       continue;
     }
     lsc_tensor yo = q_tensor(q.vals[stp.out], q.ptr(stp.out), &sc_b);
+    if (pool_fusable(q, i)) {
+      // the stem's convolution and the 3x3 / 2 max pool after it in one launch; the conv
+      // output (only the pool reads it) is not written
+      const QStep& pool = q.steps[i + 1];
+      lsc_tensor po = q_tensor(q.vals[pool.out], q.ptr(pool.out), &sc_c);
+      s = lsc::execute_conv_pool(stp.op, xi, po, st);
+      if (s == LSC_SUCCESS) {
+        pool_done = true;  // the next step (the pool) has run
+        continue;
+      }
+      if (s != LSC_ERROR_UNSUPPORTED_OPERATOR) return s;
+    }
     if (stp.kind == QStep::kConv && stp.res >= 0) {
       lsc_tensor ins[2] = {xi, q_tensor(q.vals[stp.res], q.ptr(stp.res), &sc_c)};
       if ((s = lsc_execute(q.be, stp.op, ins, 2, &yo, 1, st))) return s;

@@ -75,7 +75,8 @@ def test_int8_session_matches_oracle_with_intermediates(be, cuda, rounding):
     logits = _run(sess, x)
     net = _Net(sess)
     want, acts = oracle_resnet18(x, net, rounding)
-    for name in ["conv1", "pool"] + [s.name for s in net.convs[1:]]:
+    # the stem's convolution and max pool run as one launch: the conv output is not written
+    for name in ["pool"] + [s.name for s in net.convs[1:]]:
         v = sess.value(name)
         got = _device_bytes(v["ptr"], v["nbytes"], np.int8).reshape(v["shape"])
         np.testing.assert_array_equal(got, acts[name], err_msg=name)
@@ -83,12 +84,14 @@ def test_int8_session_matches_oracle_with_intermediates(be, cuda, rounding):
     assert not np.array_equal(logits[0], logits[1])
 
 
-@pytest.mark.parametrize("batch", [32, 256])
+@pytest.mark.parametrize("batch", [32, 128, 256])
 def test_int8_session_at_benchmark_batches(be, cuda, batch):
     """The benchmark's per-GPU batches with the memory plan and the captured graph: the first
     and last four images against the oracle; the session against the Backend-operator
-    composition (resnet18.ResNet18Int8, same parameters and calibration batch) on all images;
-    the planned activation block smaller than one buffer per activation."""
+    composition (resnet18.ResNet18Int8, same parameters and calibration batch, the stem's
+    convolution and max pool as separate launches) on all images; the planned activation
+    block smaller than one buffer per activation.  From batch 128 the session runs the stem's
+    convolution and max pool as one launch (enough 4-row bands per CTA)."""
     import torch
     from lightship_b200.resnet18 import ResNet18Int8
     x = np.random.default_rng(batch).normal(size=(batch, 3, 224, 224)).astype(np.float32)
