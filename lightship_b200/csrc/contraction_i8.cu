@@ -1446,20 +1446,14 @@ __global__ void __launch_bounds__(SwapCfg::THREADS, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(buf * S::BP + part * 64);
-      // the next chunk's accumulator load is in flight while a chunk is processed
-      uint32_t r_next[16];
-      tmem_ld_cols(t_row, r_next);
-      tmem_ld_wait();
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         const int col = part * 64 + c * 16;
         const int pix0 = tile * S::BP + col;
         uint32_t r[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) r[j] = r_next[j];
-        if (c < 3) {
-          tmem_ld_cols(t_row + static_cast<uint32_t>((c + 1) * 16), r_next);
-        } else {
+        tmem_ld_cols(t_row + static_cast<uint32_t>(c * 16), r);
+        tmem_ld_wait();
+        if (c == 3) {
           // every accumulator column of the tile has been read
           tc_fence_before();
           __syncwarp();
@@ -1476,10 +1470,7 @@ __global__ void __launch_bounds__(SwapCfg::THREADS, 1)
           for (int j = 0; j < 16; ++j)
             if (pix0 + j < p.m) p.out_i32[static_cast<int64_t>(pix0 + j) * p.ldo + ch] = acc[j];
         }
-        if (!p.out_f32 && !p.out_i8) {
-          if (c < 3) tmem_ld_wait();
-          continue;
-        }
+        if (!p.out_f32 && !p.out_i8) continue;
         float y[16];
         const uint64_t sc2 = f2pack(scale, scale);
 #pragma unroll
@@ -1529,7 +1520,6 @@ __global__ void __launch_bounds__(SwapCfg::THREADS, 1)
                 make_uint4(o[0], o[1], o[2], o[3]);
           named_bar_sync(bar_id, 128);
         }
-        if (c < 3) tmem_ld_wait();
       }
     }
   }
