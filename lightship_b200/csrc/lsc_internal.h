@@ -110,6 +110,18 @@ lsc_status launch_conv_i8(const int8_t* x, const int8_t* w, const ConvGeometry& 
 lsc_status launch_conv_pool_i8(const int8_t* x, const int8_t* w, const ConvGeometry& g, int group,
                                const int32_t* bias, const float* scale, float s_out, int act, int rounding,
                                int8_t* out_pool, cudaStream_t stream);
+// The ResNet stem in one launch (stem_i8.cu): f32 NCHW x [n, 3, 224, 224] quantized with s_in
+// (rounding_in), the 7x7 / 2 convolution of padding 3 to 64 channels with the INT8 chain's
+// epilogue (bias, per-channel scale, ReLU, requantization by s_out), then the 3x3 / 2 max pool
+// of padding 1: out [n, 56, 56, 64] int8 NHWC.  The filter is w_img, kStemFilterBytes made by
+// stem_filter_image.  Bit-exact with the separate launches when every scale[c] > 0 and
+// |bias[c]| < 2^30 (the caller checks).
+constexpr int64_t kStemFilterBytes = 12288;
+lsc_status launch_stem_conv_pool_i8(const float* x, int64_t n, const int8_t* w_img, const int32_t* bias,
+                                    const float* scale, float s_in, int rounding_in, float s_out, int rounding,
+                                    int8_t* out, cudaStream_t stream);
+// The stem kernel's filter image from the space-to-depth filter [64][4][4][16] (host bytes).
+void stem_filter_image(const int8_t* w_s2d, int8_t* img);
 
 // INT8 GEMM + requant/dequant epilogue (contraction_i8.cu).  ldo = row stride of the outputs in
 // elements.  Validates its arguments.

@@ -879,6 +879,10 @@ struct QSession {
   cudaEvent_t slot_loaded[2] = {nullptr, nullptr}, slot_free[2] = {nullptr, nullptr};
   cudaGraphExec_t exec[2] = {nullptr, nullptr};
   int next_slot = 0;
+  // the stem (input quantize, 7x7 / 2 convolution, 3x3 / 2 max pool) as one launch
+  // (lsc::launch_stem_conv_pool_i8) with its filter image
+  bool stem_fused = false;
+  void* stem_w = nullptr;
   ~QSession() {
     for (auto& e : exec)
       if (e) cudaGraphExecDestroy(e);
@@ -894,7 +898,7 @@ struct QSession {
     for (auto& s : steps)
       if (s.op) lsc_op_destroy(s.op);
     if (be) {
-      for (void* p : {in_slot[0], in_slot[1], out_buf, act_block})
+      for (void* p : {in_slot[0], in_slot[1], out_buf, act_block, stem_w})
         if (p) be->arena.free(p);
       for (void* p : act_blocks) be->arena.free(p);
     }
@@ -1171,6 +1175,28 @@ bool pool_fusable(const QSession& q, size_t i) {
   return true;
 }
 
+// The graph starts with the ResNet stem: the input quantized to space-to-depth (padding 3), read
+// only by a ReLU convolution over 3 channels that yields 112 x 112 x 64 and whose output only a
+// fused-able 3x3 / 2 max pool reads.  Such a stem can run as one launch from the f32 input
+// (lsc::launch_stem_conv_pool_i8; prepare_stem checks the compiled parameters).
+bool stem_shape_fusable(const QSession& q) {
+  if (q.steps.size() < 3 || q.in_shape.size() != 4) return false;
+  const QStep& in = q.steps[0];
+  const QStep& cv = q.steps[1];
+  if (in.kind != QStep::kInput || !in.s2d || in.s2d_pad != 3 || cv.kind != QStep::kConv || !cv.s2d ||
+      cv.in != in.out || !pool_fusable(q, 1))
+    return false;
+  if (q.in_shape[1] != 3 || q.in_shape[2] != 224 || q.in_shape[3] != 224) return false;
+  const QVal& co = q.vals[cv.out];
+  const QVal& po = q.vals[q.steps[2].out];
+  if (co.h != 112 || co.w != 112 || co.c != 64 || co.c_store != 64 || co.w_store != 112 || po.h != 56 ||
+      po.w != 56 || po.c_store != 64 || po.w_store != 56 || po.flat)
+    return false;
+  for (size_t j = 2; j < q.steps.size(); ++j)
+    if (q.steps[j].in == in.out || q.steps[j].res == in.out) return false;
+  return true;
+}
+
 void schedule_int8(QSession& q) {
   int pos = 0;
   int prev_conv_in = -1;
@@ -1197,6 +1223,8 @@ void schedule_int8(QSession& q) {
   // reads its input: its output lives from the convolution on
   for (size_t i = 0; i + 1 < q.steps.size(); ++i)
     if (pool_fusable(q, i)) q.vals[q.steps[i + 1].out].def = q.steps[i].pos;
+  // ... and a stem run as one launch writes it while the input is being quantized
+  if (stem_shape_fusable(q)) q.vals[q.steps[2].out].def = q.steps[0].pos;
   for (auto& v : q.vals)
     if (v.last < v.def) v.last = v.def;
 }
@@ -1402,6 +1430,7 @@ lsc_status calibrate_int8(QSession& q, const lsc_model& m, const float* x, cudaS
 lsc_status enqueue_int8(QSession& q, const float* in, cudaStream_t main) {
   float sc_a = 0.0f, sc_b = 0.0f, sc_c = 0.0f;
   bool pool_done = false;
+  int stem_left = 0;  // steps the fused stem launch has done
   size_t fork_i = 0, join_i = 0;
   bool side_open = false;
   for (size_t i = 0; i < q.steps.size(); ++i) {
@@ -1422,6 +1451,22 @@ lsc_status enqueue_int8(QSession& q, const float* in, cudaStream_t main) {
     side_open |= stp.side;
     if (pool_done) {
       pool_done = false;
+      continue;
+    }
+    if (stem_left > 0) {
+      --stem_left;
+      continue;
+    }
+    if (stp.kind == QStep::kInput && q.stem_fused && i == 0) {
+      // input quantize, stem convolution and max pool in one launch: the space-to-depth input
+      // and the convolution output are not written
+      const QStep& cv = q.steps[1];
+      const QStep& pool = q.steps[2];
+      s = lsc::launch_stem_conv_pool_i8(in, q.in_shape[0], static_cast<const int8_t*>(q.stem_w), cv.op->bias_i32,
+                                        cv.op->scale, q.vals[stp.out].scale, stp.op->rounding,
+                                        q.vals[cv.out].scale, cv.op->rounding, static_cast<int8_t*>(q.ptr(pool.out)), st);
+      if (s) return s;
+      stem_left = 2;
       continue;
     }
     if (stp.kind == QStep::kInput) {
@@ -1460,6 +1505,39 @@ lsc_status enqueue_int8(QSession& q, const float* in, cudaStream_t main) {
     LSC_CUDA_TRY(cudaEventRecord(q.join_ev[join_i], q.side_stream));
     LSC_CUDA_TRY(cudaStreamWaitEvent(main, q.join_ev[join_i], 0));
   }
+  return LSC_SUCCESS;
+}
+
+// Decides whether the stem runs as one launch and builds that kernel's filter image from the
+// compiled space-to-depth convolution.  Besides the shapes (stem_shape_fusable), the fused form
+// pools the int32 accumulators before requantizing, which equals pooling the int8 codes when
+// every channel scale is positive and acc + bias cannot wrap (|acc| < 2^22 for 147 int8 taps);
+// otherwise, or with LSC_FUSED_STEM=0 in the environment, the stem keeps its separate launches.
+lsc_status prepare_stem(QSession& q) {
+  q.stem_fused = false;
+  const char* env = getenv("LSC_FUSED_STEM");
+  if ((env && env[0] == '0') || !stem_shape_fusable(q)) return LSC_SUCCESS;
+  const lsc_op* op = q.steps[1].op;
+  lsc::DeviceState* ds = lsc::current_device_state();
+  if (!op || !ds || ds->cc_major != 10 || op->kind != OpKind::kConvI8 || op->act != LSC_ACT_RELU || op->n != 64 ||
+      op->kh != 4 || op->kw != 4 || op->kp != 16 || !op->w || !op->scale)
+    return LSC_SUCCESS;
+  if (!(q.vals[q.steps[1].out].scale > 0.0f)) return LSC_SUCCESS;
+  std::vector<float> scale(64);
+  std::vector<int32_t> bias(64, 0);
+  std::vector<int8_t> w(64 * 4 * 4 * 16), img(static_cast<size_t>(lsc::kStemFilterBytes));
+  LSC_CUDA_TRY(cudaMemcpy(scale.data(), op->scale, 64 * 4, cudaMemcpyDeviceToHost));
+  if (op->bias_i32) LSC_CUDA_TRY(cudaMemcpy(bias.data(), op->bias_i32, 64 * 4, cudaMemcpyDeviceToHost));
+  LSC_CUDA_TRY(cudaMemcpy(w.data(), op->w, w.size(), cudaMemcpyDeviceToHost));
+  for (int c = 0; c < 64; ++c)
+    if (!(scale[static_cast<size_t>(c)] > 0.0f) || !std::isfinite(scale[static_cast<size_t>(c)]) ||
+        bias[static_cast<size_t>(c)] > (1 << 30) || bias[static_cast<size_t>(c)] < -(1 << 30))
+      return LSC_SUCCESS;
+  lsc::stem_filter_image(w.data(), img.data());
+  if (!(q.stem_w = q.be->arena.alloc(static_cast<size_t>(lsc::kStemFilterBytes), 256)))
+    return set_error(LSC_ERROR_OUT_OF_MEMORY, "INT8 session: no arena room for the stem filter");
+  LSC_CUDA_TRY(cudaMemcpy(q.stem_w, img.data(), img.size(), cudaMemcpyHostToDevice));
+  q.stem_fused = true;
   return LSC_SUCCESS;
 }
 
@@ -1537,6 +1615,7 @@ lsc_status build_int8(QSession& q, const lsc_model& m, const lsc_tensor* calib) 
                                c.location == LSC_MEM_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
                                q.cap_stream));
   if ((s = calibrate_int8(q, m, static_cast<const float*>(q.in_slot[0]), q.cap_stream))) return s;
+  if ((s = prepare_stem(q))) return s;
   return capture_int8(q);
 }
 

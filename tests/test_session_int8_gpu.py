@@ -161,3 +161,38 @@ def test_int8_session_rejects_unsupported_graphs(be, cuda):
         Session(be, OnnxModel(blob), precision="int8",
                 calibration=Tensor("X", [2, 3, 16, 16], DataType.F32, x, layout=StorageLayout.NCHW))
     assert e.value.code == _lib.ERROR_UNSUPPORTED_OPERATOR
+
+
+def _fill_device(ptr, nbytes, byte):
+    from lightship_b200 import _lib
+    buf = (C.c_byte * nbytes)(*([byte] * nbytes))
+    _lib.check(_lib.lib().lsc_memcpy_h2d(C.c_void_p(ptr), C.addressof(buf), nbytes, None))
+
+
+@pytest.mark.parametrize("batch,rounding", [(1, 0), (3, 1), (5, 0), (37, 1)])
+def test_int8_session_fused_stem_matches_separate_launches(be, cuda, batch, rounding, monkeypatch):
+    """The stem (input quantize, 7x7 / 2 convolution, 3x3 / 2 max pool) as one launch against
+    the same session built with LSC_FUSED_STEM=0 (three launches): the pooled activation and
+    the logits bit for bit, at batches whose pooled rows split unevenly over the CTAs (CTAs
+    that start inside an image, ranges that cross images).  The fused run never writes the
+    space-to-depth input, which the separate launches do."""
+    x = np.random.default_rng(100 + batch).normal(size=(batch, 3, 224, 224)).astype(np.float32)
+    x[0, :, :5, :] = 40.0  # saturating input codes along the top edge
+    monkeypatch.setenv("LSC_FUSED_STEM", "0")
+    sep = _session(be, batch, x, plan_memory=False, rounding=rounding)
+    monkeypatch.delenv("LSC_FUSED_STEM")
+    fused = _session(be, batch, x, plan_memory=False, rounding=rounding)
+    for sess in (sep, fused):
+        v = sess.value("X:q")
+        _fill_device(v["ptr"], v["nbytes"], 0)
+    want = _run(sep, x)
+    got = _run(fused, x)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    a, b = sep.value("pool"), fused.value("pool")
+    assert a["shape"] == b["shape"] == [batch, 56, 56, 64]
+    np.testing.assert_array_equal(_device_bytes(b["ptr"], b["nbytes"], np.int8),
+                                  _device_bytes(a["ptr"], a["nbytes"], np.int8))
+    xq_sep = sep.value("X:q")
+    xq_fused = fused.value("X:q")
+    assert np.any(_device_bytes(xq_sep["ptr"], xq_sep["nbytes"], np.int8) != 0)
+    assert not np.any(_device_bytes(xq_fused["ptr"], xq_fused["nbytes"], np.int8) != 0)
