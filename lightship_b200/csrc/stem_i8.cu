@@ -21,12 +21,15 @@
 // evenly over the grid).  A pooled row py reads conv rows 2py-1, 2py, 2py+1; consecutive pooled
 // rows share the odd conv row, so a CTA computes every conv row of its range once (plus the
 // row before its first pooled row).  Warp roles:
-//   builders (the 7 warps below 15 with warp % 4 in {2, 3}): fetch the two new f32 input rows of each
-//               conv row with cp.async three conv rows ahead; quantize them into a ring of
-//               int8 rows held as four copies shifted by 1, 3, 5 and 7 bytes, so that the
-//               eight taps (kw = 0..7) of every (channel, kh) pair of an output pixel are one
-//               aligned 8-byte load; write the conv row's im2col rows (pixel x at row x + 4)
-//               into a B stage (K-major, no swizzle).
+//   builders (the 7 warps below 15 with warp % 4 in {2, 3}): one TMA tensor load per conv
+//               row brings its two new f32 input rows of the three channels (rows outside the
+//               image arrive as zeros), three conv rows ahead; the rows are quantized into a
+//               ring of int8 rows held as four copies shifted by 1, 3, 5 and 7 bytes, so that
+//               the eight taps (kw = 0..7) of every (channel, kh) pair of an output pixel are
+//               one aligned 8-byte load; the conv row's im2col rows (pixel x at row x + 4) go
+//               into a B stage (K-major, no swizzle).  Software-pipelined: between two
+//               barriers the builders write conv row i's im2col rows and quantize the input
+//               rows of conv row i + 1.
 //   MMA (warp 15): 6 x tcgen05.mma.cta_group::1.kind::i8 per conv row, M = 128 (the 64 filter
 //               rows and 64 zero rows), N = 128 (pixels), K = 32, into one of four 128-column
 //               TMEM blocks: TMEM lane = output channel, column = pixel + 4.  Commits free the
@@ -60,10 +63,11 @@ constexpr int kStPH = 56, kStPW = 56;   // pool output
 constexpr int kStCout = 64;
 constexpr int kStK = 192;               // 21 (c, kh) groups x 8 taps = 168, padded to 6 x 32
 constexpr int kStKSteps = kStK / 32;
-constexpr int kStStages = 4;
+constexpr int kStStages = 3;
 constexpr int kStABytes = (kStK / 16) * 128 * 16;   // 12 chunks of [128 rows][16 B] (filter, im2col)
-constexpr int kStF32Slots = 16;                     // f32 input rows (3 channels each)
-constexpr int kStF32Row = kStC * kStW;              // floats per slot
+constexpr int kStF32Slots = 10;    // TMA loads of two f32 input rows x 3 channels
+constexpr int kStF32Load = 2 * kStC * kStW * 4;     // bytes per load: [c][2 rows][224]
+constexpr int kStRingRows = 16;     // quantized input rows, by a running row count
 constexpr int kStCopyPitch = 288;   // one shifted copy of a quantized row (bank-spread)
 constexpr int kStLead = 3;          // conv rows whose input is fetched ahead
 constexpr int kStBuilders = 224;  // 7 warps: two threads per im2col row of the 112 pixels
@@ -76,14 +80,13 @@ constexpr int kStTmemCols = 512;    // four 128-column accumulator blocks
 constexpr int kOffW = 0;
 constexpr int kOffA = kOffW + kStABytes;
 constexpr int kOffF32 = kOffA + kStStages * kStABytes;
-constexpr int kOffRing = kOffF32 + kStF32Slots * kStF32Row * 4;
-constexpr int kOffBar = kOffRing + 8 * kStC * 4 * kStCopyPitch;
+constexpr int kOffRing = kOffF32 + kStF32Slots * kStF32Load;
+constexpr int kOffBar = kOffRing + kStRingRows * kStC * 4 * kStCopyPitch;
 constexpr int kStSmem = kOffBar + 32 * 8 + 1024;  // + alignment of the dynamic base
-static_assert(kOffA % 1024 == 0 && kOffF32 % 16 == 0 && kOffRing % 16 == 0 && kOffBar % 8 == 0, "alignment");
+static_assert(kOffA % 1024 == 0 && kOffF32 % 128 == 0 && kStF32Load % 128 == 0 && kOffRing % 16 == 0 && kOffBar % 8 == 0, "alignment");
 static_assert(kStSmem <= 232448, "shared memory");
 
 struct StemParams {
-  const float* x;
   int8_t* out;
   const int8_t* w;  // the filter's shared-memory image (stem_filter_image)
   const int32_t* bias;
@@ -94,15 +97,6 @@ struct StemParams {
   int32_t n;
   uint32_t* err;
 };
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 // Conv row i of a CTA's sequence: image n, row r; `first` when no earlier row of the same
 // image precedes it in the sequence (all seven input rows of its window are new).  e = 1 when
@@ -125,17 +119,22 @@ __device__ __forceinline__ StemItem stem_item(int i, int g0, int e) {
   it.first = (i == 0 || it.r == 0) ? 1 : 0;
   return it;
 }
-// input rows conv row r needs that the previous row of the sequence did not: [lo, hi]
-__device__ __forceinline__ int stem_lo(const StemItem& it) { return it.first ? 2 * it.r - 3 : 2 * it.r + 2; }
+// TMA loads of two input rows that conv row `it` needs beyond the previous row of the
+// sequence: rows 2r-3 .. 2r+4 (four loads, the last row unused) for a first row, else rows
+// 2r+2, 2r+3; and the input rows it adds to the quantized ring (7 or 2)
+__device__ __forceinline__ int stem_loads(const StemItem& it) { return it.first ? 4 : 1; }
+__device__ __forceinline__ int stem_new_rows(const StemItem& it) { return it.first ? 7 : 2; }
+__device__ __forceinline__ int stem_first_row(const StemItem& it) { return it.first ? 2 * it.r - 3 : 2 * it.r + 2; }
 
 template <int RND_IN>
-__global__ void __launch_bounds__(kStThreads, 1) stem_conv_pool_kernel(const StemParams p) {
+__global__ void __launch_bounds__(kStThreads, 1)
+    stem_conv_pool_kernel(const __grid_constant__ CUtensorMap tmX, const StemParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sW = smem + kOffW;
   uint8_t* sA = smem + kOffA;
-  float* f32r = reinterpret_cast<float*>(smem + kOffF32);
+  uint8_t* f32r = smem + kOffF32;
   uint8_t* ring = smem + kOffRing;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* afull = bars;                  // [kStStages] B stage written (7 builder warps)
@@ -143,7 +142,8 @@ __global__ void __launch_bounds__(kStThreads, 1) stem_conv_pool_kernel(const Ste
   uint64_t* tfull = bars + 2 * kStStages;  // [4] TMEM block holds a finished conv row
   uint64_t* tempty = tfull + kStTmemBlocks;  // [4] TMEM block released (8 epilogue warps)
   uint64_t* drain = tempty + kStTmemBlocks;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* xfull = drain + 1;               // [kStF32Slots] input load landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + kStF32Slots);
   volatile uint32_t* abort_flag = tmem_slot + 1;
   volatile uint32_t* build_ok = tmem_slot + 2;  // the builders' shared verdict on a stage wait
 
@@ -165,6 +165,7 @@ __global__ void __launch_bounds__(kStThreads, 1) stem_conv_pool_kernel(const Ste
       mbar_init(&tempty[b], kStEpiWarps);
     }
     mbar_init(drain, 1);
+    for (int f = 0; f < kStF32Slots; ++f) mbar_init(&xfull[f], 1);
     *abort_flag = 0u;
     *build_ok = 1u;
     fence_barrier_init();
@@ -173,6 +174,7 @@ __global__ void __launch_bounds__(kStThreads, 1) stem_conv_pool_kernel(const Ste
     tmem_alloc(tmem_slot, kStTmemCols);
     tmem_relinquish();
   }
+  if (threadIdx.x == 0) tma_prefetch_desc(&tmX);
   // constant operands before the wait for the previous kernel: the filter as the A operand
   // (image rows 0-63, K chunks 1024 bytes apart, moved to 2048; rows 64-127 zero), and the B
   // stages' last K chunk (taps 176..191: zero weights; the builders never write it)
@@ -196,49 +198,47 @@ __global__ void __launch_bounds__(kStThreads, 1) stem_conv_pool_kernel(const Ste
     // ------------------------------------------------------------------ builders
     const int bwarp = (warp >> 2) * 2 + (warp & 1);  // 0..6
     const int t = bwarp * 32 + lane;
-    int ld_cnt = 0, use_cnt = 0;
-    auto prefetch = [&](int i) {
-      if (i < items) {
-        const StemItem it = stem_item(i, g0, e);
-        for (int iy = stem_lo(it); iy <= 2 * it.r + 3; ++iy) {
-          if (iy < 0 || iy >= kStH) continue;
-          float* dst = f32r + (ld_cnt & (kStF32Slots - 1)) * kStF32Row;
-          ++ld_cnt;
-          const float* src = p.x + (static_cast<int64_t>(it.n) * kStC * kStH + iy) * kStW;
-          for (int u = t; u < kStC * (kStW / 4); u += kStBuilders) {
-            const int c = u / (kStW / 4), v = u - c * (kStW / 4);
-            cp_async16(dst + c * kStW + 4 * v, src + static_cast<int64_t>(c) * kStH * kStW + 4 * v);
-          }
+    // input loads in sequence order: slot = count mod kStF32Slots.  Thread 0 issues the loads
+    // of conv row i + kStLead + 1 after the barrier of iteration i, when every builder has
+    // quantized row i's input; rows i+1 .. i+4 then hold at most 4 + 1 + 1 + 4 loads (first
+    // rows are at least three rows apart), within the ten slots.
+    int issued_item = 0, issued_loads = 0;  // thread 0
+    auto issue_upto = [&](int upto) {
+      for (; issued_item <= upto && issued_item < items; ++issued_item) {
+        const StemItem it = stem_item(issued_item, g0, e);
+        const int y0 = stem_first_row(it);
+        for (int j = 0; j < stem_loads(it); ++j, ++issued_loads) {
+          const int slot = issued_loads % kStF32Slots;
+          mbar_arrive_expect_tx(&xfull[slot], kStF32Load);
+          tma_load_4d(&tmX, &xfull[slot], f32r + slot * kStF32Load, 0, y0 + 2 * j, 0, it.n);
         }
       }
-      cp_async_commit();  // one group per conv row, empty past the end
     };
+    int used_loads = 0;  // loads consumed (all builders)
+    int qrows = 0;       // input rows quantized into the ring (all builders)
+    bool ok = true;
+    // quantize the new input rows of conv row k: one (row, channel) per warp; lane l quantizes
+    // words l and l + 32 of the row image P (word u = columns 4u-8 .. 4u-5, P[i] = q(x[i - 8]),
+    // zero outside the image), then writes words l and l + 32 (< 62) of the copies shifted by
+    // 1, 3, 5 and 7 bytes into ring row qrows mod 16, the next two words from lanes l+1, l+2
+    auto quantize = [&](int k) -> bool {
+      const StemItem it = stem_item(k, g0, e);
+      const int nl = stem_loads(it), nr = stem_new_rows(it);
+      for (int j = 0; j < nl; ++j) {
+        const int u = used_loads + j;
+        if (!mbar_wait(&xfull[u % kStF32Slots], (u / kStF32Slots) & 1, abort_flag, p.err)) return false;
+      }
 #pragma unroll 1
-    for (int i = 0; i < kStLead; ++i) prefetch(i);
-#pragma unroll 1
-    for (int i = 0; i < items; ++i) {
-      prefetch(i + kStLead);
-      cp_async_wait<kStLead>();  // this thread's copies of row i have landed
-      named_bar_sync(1, kStBuilders);
-      const StemItem it = stem_item(i, g0, e);
-      const int lo = stem_lo(it), hi = 2 * it.r + 3;
-      const int real_lo = lo < 0 ? 0 : lo;
-      // one (new input row, channel) per warp: lane l quantizes words l and l + 32 of the row
-      // image P (word u = columns 4u-8 .. 4u-5; P[i] = q(x[i - 8]), zero outside the image),
-      // then writes words l and l + 32 (< 62) of the copies shifted by 1, 3, 5 and 7 bytes
-      // into the ring (slot = input row mod 8), the next two words coming from lanes l+1, l+2
-#pragma unroll 1
-      for (int task = bwarp; task < (hi - lo + 1) * kStC; task += kStBuilders / 32) {
+      for (int task = bwarp; task < nr * kStC; task += kStBuilders / 32) {
         const int ri = task / kStC, c = task - ri * kStC;
-        const int iy = lo + ri;
-        const bool real = iy >= 0 && iy < kStH;
-        const float* row = f32r + ((use_cnt + iy - real_lo) & (kStF32Slots - 1)) * kStF32Row + c * kStW;
+        const float* row = reinterpret_cast<const float*>(
+            f32r + ((used_loads + (ri >> 1)) % kStF32Slots) * kStF32Load + (c * 2 + (ri & 1)) * (kStW * 4));
         uint32_t pw[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int u = lane + 32 * h;
           float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-          if (real && u >= 2 && u <= 57) {
+          if (u >= 2 && u <= 57) {
             const float4 f = *reinterpret_cast<const float4*>(row + 4 * u - 8);
             v[0] = f.x;
             v[1] = f.y;
@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(kStThreads, 1) stem_conv_pool_kernel(const Ste
         const int l1 = (lane + 1) & 31, l2 = (lane + 2) & 31;
         const uint32_t a1_0 = __shfl_sync(0xFFFFFFFFu, pw[0], l1), a1_1 = __shfl_sync(0xFFFFFFFFu, pw[1], l1);
         const uint32_t a2_0 = __shfl_sync(0xFFFFFFFFu, pw[0], l2), a2_1 = __shfl_sync(0xFFFFFFFFu, pw[1], l2);
-        uint8_t* dst = ring + (((iy + 8) & 7) * kStC + c) * 4 * kStCopyPitch + 4 * lane;
+        uint8_t* dst = ring + (((qrows + ri) & (kStRingRows - 1)) * kStC + c) * 4 * kStCopyPitch + 4 * lane;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           if (h == 1 && lane >= 30) break;  // words 62, 63 of the copies are never read
@@ -266,25 +266,34 @@ __global__ void __launch_bounds__(kStThreads, 1) stem_conv_pool_kernel(const Ste
           *reinterpret_cast<uint32_t*>(o + 3 * kStCopyPitch) = __funnelshift_r(b, d, 24);
         }
       }
-      {
-        const int real_hi = hi >= kStH ? kStH - 1 : hi;
-        use_cnt += real_hi >= real_lo ? real_hi - real_lo + 1 : 0;
+      used_loads += nl;
+      qrows += nr;
+      return true;
+    };
+    if (t == 0) issue_upto(kStLead);
+    ok = quantize(0);
+#pragma unroll 1
+    for (int i = 0; i < items; ++i) {
+      const int s = i % kStStages;
+      if (t == 0) {
+        if (!ok || !mbar_wait(&aempty[s], ((i / kStStages) & 1) ^ 1u, abort_flag, p.err)) *build_ok = 0u;
       }
-      const int s = i & (kStStages - 1);
-      if (t == 0 && !mbar_wait(&aempty[s], ((i / kStStages) & 1) ^ 1u, abort_flag, p.err)) *build_ok = 0u;
+      if (!ok) *build_ok = 0u;  // a builder whose input wait ran out
       named_bar_sync(1, kStBuilders);
       if (!*build_ok) break;
+      if (t == 0) issue_upto(i + kStLead + 1);
       // the im2col row of output pixel x at B row x + 4 (rows 0-3 and 116-127 are never read
-      // back); threads 0-111 write K chunks 0-5 ((c, kh) groups 0-11) of pixels 0-111,
-      // threads 112-223 chunks 6-10
-      const int nrow = 4 + (t < kStOW ? t : t - kStOW);
+      // back) from the last seven quantized rows (input rows 2r-3 .. 2r+3); threads 0-111 write
+      // K chunks 0-5 ((c, kh) groups 0-11) of pixels 0-111, threads 112-223 chunks 6-10
       {
+        const int nrow = 4 + (t < kStOW ? t : t - kStOW);
         const int o = 2 * (nrow - 4) + 5;  // P index of input column 2x - 3
         const uint8_t* rb = ring + ((o & 7) >> 1) * kStCopyPitch + (o & ~7);
         uint8_t* ab = sA + s * kStABytes + nrow * 16;
+        const int row0 = qrows - 7;  // ring rows of conv row i (row i + 1's come after the build)
         auto group = [&](int q) -> uint2 {
           const int c = q / 7, kh = q - 7 * (q / 7);
-          const int slot = (2 * it.r - 3 + kh + 8) & 7;
+          const int slot = (row0 + kh) & (kStRingRows - 1);
           return *reinterpret_cast<const uint2*>(rb + (slot * kStC + c) * 4 * kStCopyPitch);
         };
         if (t < kStOW) {
@@ -308,8 +317,13 @@ __global__ void __launch_bounds__(kStThreads, 1) stem_conv_pool_kernel(const Ste
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[s]);
+      if (i + 1 < items) ok = quantize(i + 1);
     }
-    cp_async_wait<0>();
+    if (t == 0) {  // loads still in flight land before the CTA exits
+      volatile uint32_t no_abort = 0u;
+      for (int u = used_loads; u < issued_loads; ++u)
+        mbar_wait(&xfull[u % kStF32Slots], (u / kStF32Slots) & 1, &no_abort, p.err);
+    }
   } else if (warp == kStMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = idesc_i8(128, 128);
@@ -322,7 +336,7 @@ __global__ void __launch_bounds__(kStThreads, 1) stem_conv_pool_kernel(const Ste
     bool ok = true, any = false;
 #pragma unroll 1
     for (int i = 0; i < items && ok; ++i) {
-      const int b = i & (kStTmemBlocks - 1), s = i & (kStStages - 1);
+      const int b = i & (kStTmemBlocks - 1), s = i % kStStages;
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&tempty[b], ((i / kStTmemBlocks) & 1) ^ 1u, abort_flag, p.err));
       if (!ok) break;
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&afull[s], (i / kStStages) & 1, abort_flag, p.err));
@@ -468,8 +482,17 @@ lsc_status launch_stem_conv_pool_i8(const float* x, int64_t n, const int8_t* w_i
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kStSmem);
   });
   if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(stem_conv_pool)");
+  CUtensorMap tmx;
+  const uint64_t dims[4] = {static_cast<uint64_t>(kStW), static_cast<uint64_t>(kStH), static_cast<uint64_t>(kStC),
+                            static_cast<uint64_t>(n)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(kStW) * 4, static_cast<uint64_t>(kStH) * kStW * 4,
+                               static_cast<uint64_t>(kStC) * kStH * kStW * 4};
+  const uint32_t box[4] = {static_cast<uint32_t>(kStW), 2u, static_cast<uint32_t>(kStC), 1u};
+  const uint32_t estr[4] = {1u, 1u, 1u, 1u};
+  lsc_status st = encode_tmap_4d(&tmx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, x, dims, strides, box, estr,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st) return st;
   StemParams p{};
-  p.x = x;
   p.out = out;
   p.w = w_img;
   p.bias = bias;
@@ -485,7 +508,7 @@ lsc_status launch_stem_conv_pool_i8(const float* x, int64_t n, const int8_t* w_i
   const int64_t rows = n * kStPH;
   const int grid = static_cast<int>(rows < ds->sm_count ? rows : ds->sm_count);
   LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, kernel, dim3(grid), dim3(kStThreads), static_cast<size_t>(kStSmem),
-                                stream, p));
+                                stream, tmx, p));
   return LSC_SUCCESS;
 }
 
