@@ -585,14 +585,14 @@ def resnet_conv_ops_per_image():
 
 
 RESNET_GOPS_PER_IMAGE = 3.628  # 2 x MACs incl. the classifier, standard stem max pool
-RESNET_KERNELS = 24  # input quantize, 20 convolutions, max pool, average pool, classifier
+RESNET_KERNELS = 22  # the stem (input quantize, conv1, max pool), 19 convolutions, average pool, classifier
 
 
 def resnet_kernels(per_gpu_batch, sm_count):
-    """Kernel launches of one INT8-session pass: the session runs the stem's convolution and max
-    pool as one launch when there are at least 16 four-row bands of the 112-row stem output per
-    SM (28 per image)."""
-    return RESNET_KERNELS - (1 if per_gpu_batch * 28 >= 16 * sm_count else 0)
+    """Kernel launches of one INT8-session pass: the session runs the stem (input quantize, 7x7/2
+    convolution, 3x3/2 max pool) as one launch at every batch."""
+    del per_gpu_batch, sm_count
+    return RESNET_KERNELS
 
 
 def session_scales(sess):
@@ -1067,7 +1067,7 @@ def run_gpu(args):
                    "l2": "flushed (256 MiB write) before every timed step", "seed": NET_SEED},
         "parity": None,
         "network_tops": RESNET_GOPS_PER_IMAGE * batch / (ms_max * 1e-3) / 1e3,
-        "roofline": {"bound": "tensor", "kernel": "contraction_i8_kernel + contraction_i8_swap_kernel (INT8 implicit-GEMM conv)",
+        "roofline": {"bound": "tensor", "kernel": "contraction_i8_kernel + contraction_i8_swap_kernel + stem_conv_pool_kernel (INT8 convolutions)",
                      "achieved": conv_tops, "peak": int8_peak, "unit": "TOPS",
                      "frac": conv_tops / int8_peak if conv_tops else None,
                      "traffic": load_profile_value("contraction_i8_swap_conv_layer1.md", "traffic_bytes_per_launch"),
