@@ -1110,6 +1110,14 @@ def run_gpu(args):
                                           f"(direct int8 convolutions, OpenMP), {dt:.2f} s"}
         line["parity"] = {"images": imgs, "bit_exact_logits": bool(np.array_equal(
             cpu_logits.view(np.uint32), logits_dev[:imgs].view(np.uint32)))}
+    elif rank == 0:
+        # without the timed CPU leg (several GPUs, or --no-cpu-baseline): the oracle on the first
+        # four images of this rank's shard (the first images of the batch) with its session's
+        # calibrated scales, against the timed configuration's logits
+        imgs = min(4, per)
+        _, cpu_logits, _ = cpu_resnet_sample(imgs, scales)
+        line["parity"] = {"images": imgs, "rank": 0, "bit_exact_logits": bool(np.array_equal(
+            cpu_logits.view(np.uint32), logits_dev[:imgs].view(np.uint32)))}
     be.close()
     if world > 1:
         dist.barrier()
