@@ -218,12 +218,14 @@ __device__ __forceinline__ float div_by_row(float a, float b, float y) {
 }
 
 template <typename T, int J, int RND>
-__global__ void __launch_bounds__(kRowWarps * 32) layernorm_rows_kernel(const T* x, T* y, int8_t* q, int64_t rows,
+__global__ void __launch_bounds__(kRowWarps * 32, 4) layernorm_rows_kernel(const T* x, T* y, int8_t* q, int64_t rows,
                                                                         int d, const float* __restrict__ gamma,
                                                                         const float* __restrict__ beta, float eps,
-                                                                        float s_out, float inv_s) {
+                                                                        float s_out, float inv_s, bool gb16) {
   const int lane = threadIdx.x & 31;
   const float fd = static_cast<float>(d);
+  griddep_wait();  // launched as a dependent kernel: inputs and outputs are settled from here on
+  griddep_launch_dependents();
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * kRowWarps + (threadIdx.x >> 5); r < rows;
        r += static_cast<int64_t>(gridDim.x) * kRowWarps) {
     const T* xr = x + r * d;
@@ -258,19 +260,36 @@ __global__ void __launch_bounds__(kRowWarps * 32) layernorm_rows_kernel(const T*
       const int i = 128 * j + 4 * lane;
       if (i >= d) continue;
       float o[4];
+      // gamma and beta as 16-byte vectors when they are 16-byte aligned (d is a multiple of 4)
+      float gv[4] = {0.f, 0.f, 0.f, 0.f}, bv[4] = {0.f, 0.f, 0.f, 0.f};
+      if (gb16) {
+        if (gamma) {
+          const float4 g4 = __ldg(reinterpret_cast<const float4*>(gamma + i));
+          gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+        }
+        if (beta) {
+          const float4 b4 = __ldg(reinterpret_cast<const float4*>(beta + i));
+          bv[0] = b4.x; bv[1] = b4.y; bv[2] = b4.z; bv[3] = b4.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (gamma) gv[e] = __ldg(gamma + i + e);
+          if (beta) bv[e] = __ldg(beta + i + e);
+        }
+      }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         float t = div_by_row(__fsub_rn(v[j][e], mean), sd, inv_sd);
-        if (gamma) t = __fmul_rn(__ldg(gamma + i + e), t);
-        if (beta) t = __fadd_rn(t, __ldg(beta + i + e));
+        if (gamma) t = __fmul_rn(gv[e], t);
+        if (beta) t = __fadd_rn(t, bv[e]);
         o[e] = t;
       }
       if (q) {
-        uint32_t pk = 0;
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          pk |= (static_cast<uint32_t>(requant_one<RND>(o[e], s_out, inv_s)) & 0xFFu) << (8 * e);
-        *reinterpret_cast<uint32_t*>(q + r * d + i) = pk;
+        // the four codes by the two-lane form of the same requantization (identical results)
+        uint32_t pk[1];
+        requant_pack_rnd<4, RND>(o, s_out, inv_s, false, pk);
+        *reinterpret_cast<uint32_t*>(q + r * d + i) = pk[0];
       } else {
         st4(y + r * d, i, o);
       }
@@ -280,12 +299,13 @@ __global__ void __launch_bounds__(kRowWarps * 32) layernorm_rows_kernel(const T*
 
 template <typename T, int RND>
 lsc_status layernorm_rows(const T* x, T* y, int8_t* q, int64_t rows, int d, const float* gamma, const float* beta,
-                          float eps, float s_out, float inv_s, int grid, cudaStream_t st) {
+                          float eps, float s_out, float inv_s, int grid, bool overlap, cudaStream_t st) {
   const int j = (d + 127) / 128;
+  const bool gb16 = ((reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15) == 0;
 #define LSC_LN_CASE(J)                                                                                          \
   case J:                                                                                                     \
-    layernorm_rows_kernel<T, J, RND><<<grid, kRowWarps * 32, 0, st>>>(x, y, q, rows, d, gamma, beta, eps, s_out, \
-                                                                      inv_s);                                 \
+    LSC_CUDA_TRY(launch_dependent(overlap, layernorm_rows_kernel<T, J, RND>, dim3(grid), dim3(kRowWarps * 32), 0, \
+                                  st, x, y, q, rows, d, gamma, beta, eps, s_out, inv_s, gb16));                 \
     break;
   switch (j) {
     LSC_LN_CASE(1) LSC_LN_CASE(2) LSC_LN_CASE(3) LSC_LN_CASE(4) LSC_LN_CASE(5) LSC_LN_CASE(6) LSC_LN_CASE(7)
@@ -351,13 +371,13 @@ lsc_status launch_layernorm(const void* x, void* y, int32_t dtype, int64_t rows,
     if (dtype == LSC_DTYPE_F32) {
       const float* xs = static_cast<const float*>(x);
       float* ys = static_cast<float*>(y);
-      return even ? layernorm_rows<float, LSC_ROUND_HALF_EVEN>(xs, ys, q, rows, di, gamma, beta, eps, q_scale, inv, grid, st)
-                  : layernorm_rows<float, LSC_ROUND_HALF_AWAY>(xs, ys, q, rows, di, gamma, beta, eps, q_scale, inv, grid, st);
+      return even ? layernorm_rows<float, LSC_ROUND_HALF_EVEN>(xs, ys, q, rows, di, gamma, beta, eps, q_scale, inv, grid, ds->overlap_launches, st)
+                  : layernorm_rows<float, LSC_ROUND_HALF_AWAY>(xs, ys, q, rows, di, gamma, beta, eps, q_scale, inv, grid, ds->overlap_launches, st);
     }
     const __half* xh = static_cast<const __half*>(x);
     __half* yh = static_cast<__half*>(y);
-    return even ? layernorm_rows<__half, LSC_ROUND_HALF_EVEN>(xh, yh, q, rows, di, gamma, beta, eps, q_scale, inv, grid, st)
-                : layernorm_rows<__half, LSC_ROUND_HALF_AWAY>(xh, yh, q, rows, di, gamma, beta, eps, q_scale, inv, grid, st);
+    return even ? layernorm_rows<__half, LSC_ROUND_HALF_EVEN>(xh, yh, q, rows, di, gamma, beta, eps, q_scale, inv, grid, ds->overlap_launches, st)
+                : layernorm_rows<__half, LSC_ROUND_HALF_AWAY>(xh, yh, q, rows, di, gamma, beta, eps, q_scale, inv, grid, ds->overlap_launches, st);
   }
   if (q)
     return set_error(LSC_ERROR_UNSUPPORTED_LAYOUT,
