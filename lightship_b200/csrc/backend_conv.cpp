@@ -426,8 +426,11 @@ lsc_status execute_conv(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_te
     void* yd = nullptr;
     if ((st = s.output(y, g.n * g.c_out * g.oh * g.ow * 4, &yd))) return st;
     set_shape(y, {g.n, g.c_out, g.oh, g.ow});
+    const int64_t ks_floats = tf32_conv_ksplit_floats(g);
+    float* ks_ws = ks_floats > 0 ? static_cast<float*>(s.scratch(ks_floats * 4)) : nullptr;
     return launch_conv_tf32(hi, lo, static_cast<const float*>(op->w), static_cast<const float*>(op->w_lo), g,
-                            op->bias_f32, op->act, static_cast<float*>(yd), split, s.st);
+                            op->bias_f32, op->act, static_cast<float*>(yd), split, s.st, ks_ws,
+                            ks_ws ? ks_floats : 0);
   }
   if (!is_int8(x.dtype)) return set_error(LSC_ERROR_UNSUPPORTED_DATATYPE, "INT8 Conv2d: input must be int8 NHWC");
   if (x.shape[3] != op->kp)
@@ -634,7 +637,10 @@ lsc_status execute_matmul_f32(const lsc_op* op, const lsc_tensor* in, int n_in, 
   if (!ah || !bh || (split && (!al || !bl))) return LSC_ERROR_OUT_OF_MEMORY;
   if ((st = prep_split_rows(static_cast<const float*>(ad), m, k, kp, ah, al, s.st))) return st;
   if ((st = prep_split_transpose(static_cast<const float*>(bd), k, n, kp, bh, bl, s.st))) return st;
-  return launch_gemm_tf32(ah, al, bh, bl, m, n, kp, nullptr, op->act, static_cast<float*>(cd), n, split, s.st);
+  const int64_t ks_floats = tf32_gemm_ksplit_floats(m, n, kp);
+  float* ks_ws = ks_floats > 0 ? static_cast<float*>(s.scratch(ks_floats * 4)) : nullptr;
+  return launch_gemm_tf32(ah, al, bh, bl, m, n, kp, nullptr, op->act, static_cast<float*>(cd), n, split, s.st, ks_ws,
+                          ks_ws ? ks_floats : 0);
 }
 
 lsc_status compile_fc_f32(lsc_op* op, const lsc_tensor* in, int n_in, int n_out) {
@@ -696,8 +702,11 @@ lsc_status execute_fc_f32(const lsc_op* op, const lsc_tensor* in, int n_in, lsc_
   float* xl = split ? static_cast<float*>(s.scratch(m * op->kp * 4)) : nullptr;
   if (!xh || (split && !xl)) return LSC_ERROR_OUT_OF_MEMORY;
   if ((st = prep_split_rows(static_cast<const float*>(xd), m, op->k, op->kp, xh, xl, s.st))) return st;
+  const int64_t ks_floats = tf32_gemm_ksplit_floats(m, op->n, op->kp);
+  float* ks_ws = ks_floats > 0 ? static_cast<float*>(s.scratch(ks_floats * 4)) : nullptr;
   return launch_gemm_tf32(xh, xl, static_cast<const float*>(op->w), static_cast<const float*>(op->w_lo), m,
-                          op->n, op->kp, op->bias_f32, op->act, static_cast<float*>(yd), op->n, split, s.st);
+                          op->n, op->kp, op->bias_f32, op->act, static_cast<float*>(yd), op->n, split, s.st, ks_ws,
+                          ks_ws ? ks_floats : 0);
 }
 
 // ------------------------------------------------------------------------------ BatchNorm / activations

@@ -34,6 +34,10 @@ struct Tf32Params {
   // to the next batch (or lie past the map, zero-filled) and are never stored.
   int32_t batches, a_batch_rows, b_batch_rows;
   int64_t out_batch_stride;
+  // split K (one batch only): ksplit CTAs share a tile, each over kb_per_split K blocks, and
+  // write their raw f32 sums to partial[split][m][n]; tf32_splitk_reduce adds them in order
+  int32_t ksplit, kb_per_split;
+  float* partial;
 };
 
 template <int BN_, bool SPLIT_>
@@ -142,7 +146,8 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
   const int m_tiles = (p.m + C::BM - 1) / C::BM;
   const int n_tiles = (p.n + C::BN - 1) / C::BN;
   const int batch_tiles = m_tiles * n_tiles;
-  const int num_tiles = batch_tiles * p.batches;
+  const int out_tiles = batch_tiles * p.batches;
+  const int num_tiles = out_tiles * p.ksplit;
   const int kblocks = (p.k + C::BK - 1) / C::BK;
 
   if (warp == 0) {
@@ -150,7 +155,10 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
       uint32_t stage = 0, phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile_k = blockIdx.x; tile_k < num_tiles && ok; tile_k += gridDim.x) {
+        const int ks = tile_k / out_tiles, tile = tile_k - ks * out_tiles;
+        const int kb0 = ks * p.kb_per_split;
+        const int kb1 = kb0 + p.kb_per_split < kblocks ? kb0 + p.kb_per_split : kblocks;
         const int bz = tile / batch_tiles;
         const int mb = (tile - bz * batch_tiles) % m_tiles, nb = (tile - bz * batch_tiles) / m_tiles;
         const int a_row0 = bz * p.a_batch_rows + mb * C::BM, b_row0 = bz * p.b_batch_rows + nb * C::BN;
@@ -164,7 +172,7 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
           cw = ox * p.sw - p.pw;
           chh = oy * p.sh - p.ph;
         }
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
             ok = false;
             break;
@@ -215,7 +223,9 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
       uint32_t stage = 0, phase = 0;
       int local = 0;
       bool ok = true, any_mma = false;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int tile_k = blockIdx.x; tile_k < num_tiles && ok; tile_k += gridDim.x, ++local) {
+        const int kb0 = (tile_k / out_tiles) * p.kb_per_split;
+        const int kb1 = kb0 + p.kb_per_split < kblocks ? kb0 + p.kb_per_split : kblocks;
         const int buf = local & 1;
         const uint32_t buf_phase = static_cast<uint32_t>((local >> 1) & 1);
         if (!mbar_wait(&tempty[buf], buf_phase ^ 1u, abort_flag, p.err)) {
@@ -224,7 +234,7 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * C::BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
             ok = false;
             break;
@@ -236,7 +246,7 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t adh = a_desc<ACB>(ah, kk);
             const uint64_t bdh = smem_desc_sw128_kmajor(bh + kk * 32);
-            mma_tf32(d_tmem, adh, bdh, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+            mma_tf32(d_tmem, adh, bdh, C::IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
             if constexpr (SPLIT) {
               const uint64_t adl = a_desc<ACB>(smem_u32(a_part(stage, 1)), kk);
               const uint64_t bdl = smem_desc_sw128_kmajor(smem_u32(b_part(stage, 1)) + kk * 32);
@@ -265,7 +275,8 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
     const int half = epi >> 2;
     const int row_in_tile = quarter * 32 + lane;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int tile_k = blockIdx.x; tile_k < num_tiles; tile_k += gridDim.x, ++local) {
+      const int ks = tile_k / out_tiles, tile = tile_k - ks * out_tiles;
       const int bz = tile / batch_tiles;
       const int mb = (tile - bz * batch_tiles) % m_tiles, nb = (tile - bz * batch_tiles) / m_tiles;
       float* const out_b = p.out + bz * p.out_batch_stride;
@@ -290,6 +301,20 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
         }
         if (row >= p.m) continue;
         const int col0 = nb * C::BN + tcol;
+        if (p.ksplit > 1) {  // raw sums of this K range; bias and activation after the reduction
+          float* o = p.partial + (static_cast<int64_t>(ks) * p.m + row) * p.n + col0;
+          if (p.n % 4 == 0 && col0 + 32 <= p.n) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              reinterpret_cast<float4*>(o)[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                            __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.n) o[j] = __uint_as_float(r[j]);
+          }
+          continue;
+        }
         float y[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -328,6 +353,34 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
   }
 }
 
+// out = act(sum over the K splits, in split order, + bias): row-major [m, ldo] or, for a
+// convolution, NCHW (element i walks the NCHW output so that the stores coalesce).
+__global__ void tf32_splitk_reduce_kernel(const float* __restrict__ partial, int32_t ksplit, int32_t m, int32_t n,
+                                          const float* __restrict__ bias, int32_t act, float* __restrict__ out,
+                                          int64_t ldo, int32_t out_nchw, int32_t ohw) {
+  const int64_t total = static_cast<int64_t>(m) * n;
+  const int64_t mn = total;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t row, col;
+    if (out_nchw) {
+      const int64_t img = i / (static_cast<int64_t>(n) * ohw);
+      const int64_t rem = i - img * n * ohw;
+      col = rem / ohw;
+      row = img * ohw + (rem - col * ohw);
+    } else {
+      row = i / n;
+      col = i - row * n;
+    }
+    float v = partial[row * n + col];
+    for (int s = 1; s < ksplit; ++s) v = __fadd_rn(v, partial[s * mn + row * n + col]);
+    if (bias) v = __fadd_rn(v, __ldg(bias + col));
+    v = act_rt(v, act);
+    if (out_nchw) out[i] = v;
+    else out[row * ldo + col] = v;
+  }
+}
+
 template <int BN, int ACB, bool SPLIT>
 lsc_status launch_cfg(const CUtensorMap (&tm)[4], const Tf32Params& p, int sm_count,
                       cudaStream_t stream) {
@@ -339,11 +392,20 @@ lsc_status launch_cfg(const CUtensorMap (&tm)[4], const Tf32Params& p, int sm_co
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(contraction_tf32)");
-  const int64_t tiles = static_cast<int64_t>((p.m + C::BM - 1) / C::BM) * ((p.n + C::BN - 1) / C::BN) * p.batches;
+  const int64_t tiles =
+      static_cast<int64_t>((p.m + C::BM - 1) / C::BM) * ((p.n + C::BN - 1) / C::BN) * p.batches * p.ksplit;
   const int grid = tiles < sm_count ? static_cast<int>(tiles) : sm_count;
   contraction_tf32_kernel<BN, ACB, SPLIT>
       <<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3], p);
   LSC_CUDA_TRY(cudaGetLastError());
+  if (p.ksplit > 1) {
+    const int64_t total = static_cast<int64_t>(p.m) * p.n;
+    const int64_t blocks = (total + 255) / 256;
+    const int rgrid = static_cast<int>(blocks < 8 * sm_count ? blocks : 8 * sm_count);
+    tf32_splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(p.partial, p.ksplit, p.m, p.n, p.bias, p.act, p.out, p.ldo,
+                                                         p.out_nchw, p.ohw);
+    LSC_CUDA_TRY(cudaGetLastError());
+  }
   return LSC_SUCCESS;
 }
 
@@ -363,12 +425,61 @@ lsc_status check_ptr16(const void* p, const char* what) {
   return LSC_SUCCESS;
 }
 
+// K splits for a product of `tiles` output tiles and `kblocks` K blocks: none while the tiles
+// fill half the SMs; else up to one CTA per SM, at least two K blocks each, at most 16 splits.
+// A single producer thread issues each CTA's tensor loads one after another, so a small
+// product with a long K runs at the pace of its few CTAs' load streams (the 512^3 GEMM on 16
+// CTAs, a batch-1 56x56 convolution on 25) unless K is spread over more CTAs.
+void choose_ksplit(int64_t tiles, int64_t kblocks, int sm_count, int32_t& ksplit, int32_t& kb_per_split) {
+  ksplit = 1;
+  kb_per_split = static_cast<int32_t>(kblocks);
+  if (tiles <= 0 || 2 * tiles > sm_count || kblocks < 4) return;
+  int64_t s = sm_count / tiles;
+  if (s > kblocks / 2) s = kblocks / 2;
+  if (s > 16) s = 16;
+  if (s < 2) return;
+  const int64_t per = (kblocks + s - 1) / s;
+  ksplit = static_cast<int32_t>((kblocks + per - 1) / per);
+  kb_per_split = static_cast<int32_t>(per);
+}
+
+int64_t gemm_tiles(int64_t m, int64_t n, int64_t batches) {
+  const int64_t bn = n <= 64 ? 64 : 128;
+  return ((m + 127) / 128) * ((n + bn - 1) / bn) * batches;
+}
+
+int64_t conv_kblocks(const ConvGeometry& g) {
+  const int64_t cbytes = g.c * 4;
+  const int64_t acb = cbytes % 128 == 0 ? 128 : (cbytes % 64 == 0 ? 64 : (cbytes % 32 == 0 ? 32 : 16));
+  const int64_t total_chunks = g.kh * g.kw * (cbytes / acb);
+  const int64_t sub = 128 / acb;
+  return (total_chunks + sub - 1) / sub;
+}
+
 }  // namespace
+
+int64_t tf32_gemm_ksplit_floats(int64_t m, int64_t n, int64_t k) {
+  DeviceState* ds = current_device_state();
+  if (!ds || m <= 0 || n <= 0 || k <= 0) return 0;
+  int32_t ks = 1, per = 0;
+  choose_ksplit(gemm_tiles(m, n, 1), (k + 31) / 32, ds->sm_count, ks, per);
+  return ks > 1 ? ks * m * n : 0;
+}
+
+int64_t tf32_conv_ksplit_floats(const ConvGeometry& g) {
+  DeviceState* ds = current_device_state();
+  const int64_t m = g.n * g.oh * g.ow;
+  if (!ds || m <= 0 || g.c_out <= 0 || g.c <= 0) return 0;
+  int32_t ks = 1, per = 0;
+  choose_ksplit(gemm_tiles(m, g.c_out, 1), conv_kblocks(g), ds->sm_count, ks, per);
+  return ks > 1 ? ks * m * g.c_out : 0;
+}
 
 lsc_status launch_gemm_tf32_batched(const float* a_hi, const float* a_lo, const float* b_hi,
                                     const float* b_lo, int64_t batches, int64_t m, int64_t n, int64_t k,
                                     const float* bias, int act, float* out, int64_t ldo,
-                                    int64_t out_batch_stride, bool split, cudaStream_t stream) {
+                                    int64_t out_batch_stride, bool split, cudaStream_t stream,
+                                    float* ksplit_ws, int64_t ksplit_ws_floats) {
   if (m < 0 || n < 0 || k < 0 || batches < 0) return set_error(LSC_ERROR_INVALID_ARGUMENT, "gemm_tf32: negative size");
   if (m == 0 || n == 0 || batches == 0) return LSC_SUCCESS;
   if (!a_hi || !b_hi || !out || (split && (!a_lo || !b_lo)))
@@ -409,19 +520,32 @@ lsc_status launch_gemm_tf32_batched(const float* a_hi, const float* a_lo, const 
   p.a_batch_rows = static_cast<int32_t>(m);
   p.b_batch_rows = static_cast<int32_t>(n);
   p.out_batch_stride = out_batch_stride;
+  p.ksplit = 1;
+  p.kb_per_split = static_cast<int32_t>((k + 31) / 32);
+  if (ksplit_ws && batches == 1) {
+    int32_t ks = 1, per = 0;
+    choose_ksplit(gemm_tiles(m, n, 1), (k + 31) / 32, ds->sm_count, ks, per);
+    if (ks > 1 && ks * m * n <= ksplit_ws_floats) {
+      p.ksplit = ks;
+      p.kb_per_split = per;
+      p.partial = ksplit_ws;
+    }
+  }
   return launch_acb<0>(bn, split, tm, p, ds->sm_count, stream);
 }
 
 lsc_status launch_gemm_tf32(const float* a_hi, const float* a_lo, const float* b_hi,
                             const float* b_lo, int64_t m, int64_t n, int64_t k,
                             const float* bias, int act, float* out, int64_t ldo, bool split,
-                            cudaStream_t stream) {
-  return launch_gemm_tf32_batched(a_hi, a_lo, b_hi, b_lo, 1, m, n, k, bias, act, out, ldo, 0, split, stream);
+                            cudaStream_t stream, float* ksplit_ws, int64_t ksplit_ws_floats) {
+  return launch_gemm_tf32_batched(a_hi, a_lo, b_hi, b_lo, 1, m, n, k, bias, act, out, ldo, 0, split, stream,
+                                  ksplit_ws, ksplit_ws_floats);
 }
 
 lsc_status launch_conv_tf32(const float* x_hi, const float* x_lo, const float* w_hi,
                             const float* w_lo, const ConvGeometry& g, const float* bias, int act,
-                            float* out_nchw, bool split, cudaStream_t stream) {
+                            float* out_nchw, bool split, cudaStream_t stream, float* ksplit_ws,
+                            int64_t ksplit_ws_floats) {
   const int64_t m = g.n * g.oh * g.ow;
   if (g.n < 0 || g.h <= 0 || g.w <= 0 || g.c <= 0 || g.kh <= 0 || g.kw <= 0 || g.sh <= 0 ||
       g.sw <= 0 || g.dh <= 0 || g.dw <= 0 || g.ph < 0 || g.pw < 0 || g.c_out < 0)
@@ -501,6 +625,17 @@ lsc_status launch_conv_tf32(const float* x_hi, const float* x_lo, const float* w
   p.total_chunks = static_cast<int32_t>(total_chunks);
   p.chunk_elems = acb / 4;
   p.batches = 1;
+  p.ksplit = 1;
+  p.kb_per_split = static_cast<int32_t>(conv_kblocks(g));
+  if (ksplit_ws) {
+    int32_t ks = 1, per = 0;
+    choose_ksplit(gemm_tiles(m, g.c_out, 1), conv_kblocks(g), ds->sm_count, ks, per);
+    if (ks > 1 && ks * m * g.c_out <= ksplit_ws_floats) {
+      p.ksplit = ks;
+      p.kb_per_split = per;
+      p.partial = ksplit_ws;
+    }
+  }
   switch (acb) {
     case 128: return launch_acb<128>(bn, split, tm, p, ds->sm_count, stream);
     case 64: return launch_acb<64>(bn, split, tm, p, ds->sm_count, stream);

@@ -140,19 +140,27 @@ lsc_status launch_gemm_i8(const int8_t* a, const int8_t* w, int64_t m, int64_t n
 // (hi and lo parts; lo unused when split == false), K a multiple of 4, output row-major with
 // stride ldo.  Convolution: NHWC hi/lo input with g.c stored channels (multiple of 4),
 // weights [Cout, KH*KW*C], output NCHW.
+// Small products with a long K (fewer output tiles than half the SMs) split K over more CTAs
+// when the caller passes `ksplit_ws`, device scratch of the floats tf32_gemm_ksplit_floats /
+// tf32_conv_ksplit_floats return (0: no split for that shape); the partial sums are added in a
+// fixed order by a second launch.
+int64_t tf32_gemm_ksplit_floats(int64_t m, int64_t n, int64_t k);
+int64_t tf32_conv_ksplit_floats(const ConvGeometry& g);
 lsc_status launch_gemm_tf32(const float* a_hi, const float* a_lo, const float* b_hi,
                             const float* b_lo, int64_t m, int64_t n, int64_t k,
                             const float* bias, int act, float* out, int64_t ldo, bool split,
-                            cudaStream_t stream);
+                            cudaStream_t stream, float* ksplit_ws = nullptr, int64_t ksplit_ws_floats = 0);
 lsc_status launch_conv_tf32(const float* x_hi, const float* x_lo, const float* w_hi,
                             const float* w_lo, const ConvGeometry& g, const float* bias, int act,
-                            float* out_nchw, bool split, cudaStream_t stream);
+                            float* out_nchw, bool split, cudaStream_t stream, float* ksplit_ws = nullptr,
+                            int64_t ksplit_ws_floats = 0);
 // `batches` GEMMs in one launch: batch b's A is rows [b*m, (b+1)*m) of a_hi/a_lo, its B rows
 // [b*n, (b+1)*n) of b_hi/b_lo, its output out + b * out_batch_stride.
 lsc_status launch_gemm_tf32_batched(const float* a_hi, const float* a_lo, const float* b_hi,
                                     const float* b_lo, int64_t batches, int64_t m, int64_t n, int64_t k,
                                     const float* bias, int act, float* out, int64_t ldo,
-                                    int64_t out_batch_stride, bool split, cudaStream_t stream);
+                                    int64_t out_batch_stride, bool split, cudaStream_t stream,
+                                    float* ksplit_ws = nullptr, int64_t ksplit_ws_floats = 0);
 // FP32 3x3 stride-1 convolution as Winograd F(2x2, 3x3) (winograd_f32.cu): NCHW input with
 // g.c channels, transformed filter u [16][Cout][cp] (hi/lo), NCHW output; `scratch` holds
 // winograd_f32_scratch_floats(g, cp, split) floats.
