@@ -142,6 +142,8 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // launched as a dependent kernel: operands and outputs are settled from here on
+  griddep_launch_dependents();
 
   const int m_tiles = (p.m + C::BM - 1) / C::BM;
   const int n_tiles = (p.n + C::BN - 1) / C::BN;
@@ -358,6 +360,8 @@ __global__ void __launch_bounds__(Tf32Cfg<BN, SPLIT>::THREADS, 1)
 __global__ void tf32_splitk_reduce_kernel(const float* __restrict__ partial, int32_t ksplit, int32_t m, int32_t n,
                                           const float* __restrict__ bias, int32_t act, float* __restrict__ out,
                                           int64_t ldo, int32_t out_nchw, int32_t ohw) {
+  griddep_wait();  // launched as a dependent kernel: the partial sums are complete from here on
+  griddep_launch_dependents();
   const int64_t total = static_cast<int64_t>(m) * n;
   const int64_t mn = total;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -382,7 +386,7 @@ __global__ void tf32_splitk_reduce_kernel(const float* __restrict__ partial, int
 }
 
 template <int BN, int ACB, bool SPLIT>
-lsc_status launch_cfg(const CUtensorMap (&tm)[4], const Tf32Params& p, int sm_count,
+lsc_status launch_cfg(const CUtensorMap (&tm)[4], const Tf32Params& p, int sm_count, bool overlap,
                       cudaStream_t stream) {
   using C = Tf32Cfg<BN, SPLIT>;
   static std::once_flag once;
@@ -395,16 +399,14 @@ lsc_status launch_cfg(const CUtensorMap (&tm)[4], const Tf32Params& p, int sm_co
   const int64_t tiles =
       static_cast<int64_t>((p.m + C::BM - 1) / C::BM) * ((p.n + C::BN - 1) / C::BN) * p.batches * p.ksplit;
   const int grid = tiles < sm_count ? static_cast<int>(tiles) : sm_count;
-  contraction_tf32_kernel<BN, ACB, SPLIT>
-      <<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3], p);
-  LSC_CUDA_TRY(cudaGetLastError());
+  LSC_CUDA_TRY(launch_dependent(overlap, contraction_tf32_kernel<BN, ACB, SPLIT>, dim3(grid), dim3(C::THREADS),
+                                static_cast<size_t>(C::SMEM_BYTES), stream, tm[0], tm[1], tm[2], tm[3], p));
   if (p.ksplit > 1) {
     const int64_t total = static_cast<int64_t>(p.m) * p.n;
     const int64_t blocks = (total + 255) / 256;
     const int rgrid = static_cast<int>(blocks < 8 * sm_count ? blocks : 8 * sm_count);
-    tf32_splitk_reduce_kernel<<<rgrid, 256, 0, stream>>>(p.partial, p.ksplit, p.m, p.n, p.bias, p.act, p.out, p.ldo,
-                                                         p.out_nchw, p.ohw);
-    LSC_CUDA_TRY(cudaGetLastError());
+    LSC_CUDA_TRY(launch_dependent(overlap, tf32_splitk_reduce_kernel, dim3(rgrid), dim3(256), 0, stream, p.partial,
+                                  p.ksplit, p.m, p.n, p.bias, p.act, p.out, p.ldo, p.out_nchw, p.ohw));
   }
   return LSC_SUCCESS;
 }
@@ -412,11 +414,13 @@ lsc_status launch_cfg(const CUtensorMap (&tm)[4], const Tf32Params& p, int sm_co
 template <int ACB>
 lsc_status launch_acb(int bn, bool split, const CUtensorMap (&tm)[4], const Tf32Params& p,
                       int sm_count, cudaStream_t stream) {
+  const DeviceState* ds = current_device_state();
+  const bool overlap = ds ? ds->overlap_launches : false;
   if (bn == 64)
-    return split ? launch_cfg<64, ACB, true>(tm, p, sm_count, stream)
-                 : launch_cfg<64, ACB, false>(tm, p, sm_count, stream);
-  return split ? launch_cfg<128, ACB, true>(tm, p, sm_count, stream)
-               : launch_cfg<128, ACB, false>(tm, p, sm_count, stream);
+    return split ? launch_cfg<64, ACB, true>(tm, p, sm_count, overlap, stream)
+                 : launch_cfg<64, ACB, false>(tm, p, sm_count, overlap, stream);
+  return split ? launch_cfg<128, ACB, true>(tm, p, sm_count, overlap, stream)
+               : launch_cfg<128, ACB, false>(tm, p, sm_count, overlap, stream);
 }
 
 lsc_status check_ptr16(const void* p, const char* what) {

@@ -20,6 +20,8 @@ __device__ __forceinline__ void split(float x, float& hi, float& lo) {
 // Row-major [rows, cols] -> hi/lo with the same layout (cols padded to ld with zeros).
 __global__ void split_rows_kernel(const float* __restrict__ x, int64_t rows, int64_t cols,
                                   int64_t ld, float* __restrict__ hi, float* __restrict__ lo) {
+  griddep_wait();  // launched as a dependent kernel: inputs and outputs are settled from here on
+  griddep_launch_dependents();
   const int64_t total = rows * ld;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -36,6 +38,8 @@ __global__ void split_transpose_kernel(const float* __restrict__ x, int64_t k, i
                                        int64_t ldk, float* __restrict__ hi,
                                        float* __restrict__ lo) {
   __shared__ float tile[32][33];
+  griddep_wait();  // launched as a dependent kernel: inputs and outputs are settled from here on
+  griddep_launch_dependents();
   const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 32, n0 = static_cast<int64_t>(blockIdx.x) * 32;
   for (int j = threadIdx.y; j < 32; j += blockDim.y) {
     const int64_t kk = k0 + j, nn = n0 + threadIdx.x;
@@ -59,6 +63,8 @@ __global__ void split_nchw_to_nhwc_kernel(const float* __restrict__ x, int64_t n
                                           float* __restrict__ lo) {
   // one block per (image, 32-pixel strip); threads walk channels
   __shared__ float tile[32][33];
+  griddep_wait();  // launched as a dependent kernel: inputs and outputs are settled from here on
+  griddep_launch_dependents();
   const int64_t img = blockIdx.y;
   const int64_t p0 = static_cast<int64_t>(blockIdx.x) * 32;
   for (int64_t c0 = 0; c0 < cp; c0 += 32) {
@@ -95,7 +101,8 @@ lsc_status prep_split_rows(const float* x, int64_t rows, int64_t cols, int64_t l
   if (rows * ld == 0) return LSC_SUCCESS;
   DeviceState* ds = current_device_state();
   if (!ds) return LSC_ERROR_DEVICE_ERROR;
-  split_rows_kernel<<<grid_1d(rows * ld, ds->sm_count), 256, 0, st>>>(x, rows, cols, ld, hi, lo);
+  LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, split_rows_kernel, dim3(grid_1d(rows * ld, ds->sm_count)),
+                                dim3(256), 0, st, x, rows, cols, ld, hi, lo));
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }
@@ -104,8 +111,11 @@ lsc_status prep_split_transpose(const float* x, int64_t k, int64_t n, int64_t ld
                                 float* lo, cudaStream_t st) {
   if (k == 0 || n == 0) return LSC_SUCCESS;
   if ((ldk + 31) / 32 > 65535) return set_error(LSC_ERROR_INVALID_ARGUMENT, "transpose: K too large");
+  DeviceState* ds = current_device_state();
+  if (!ds) return LSC_ERROR_DEVICE_ERROR;
   const dim3 grid(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>((ldk + 31) / 32));
-  split_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(x, k, n, ldk, hi, lo);
+  LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, split_transpose_kernel, grid, dim3(32, 8), 0, st, x, k, n, ldk,
+                                hi, lo));
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }
@@ -114,8 +124,11 @@ lsc_status prep_split_nchw_to_nhwc(const float* x, int64_t n, int64_t c, int64_t
                                    float* hi, float* lo, cudaStream_t st) {
   if (n == 0 || hw == 0) return LSC_SUCCESS;
   if (n > 65535) return set_error(LSC_ERROR_INVALID_ARGUMENT, "nchw->nhwc: batch too large");
+  DeviceState* ds = current_device_state();
+  if (!ds) return LSC_ERROR_DEVICE_ERROR;
   const dim3 grid(static_cast<unsigned>((hw + 31) / 32), static_cast<unsigned>(n));
-  split_nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, st>>>(x, n, c, hw, cp, hi, lo);
+  LSC_CUDA_TRY(launch_dependent(ds->overlap_launches, split_nchw_to_nhwc_kernel, grid, dim3(32, 8), 0, st, x, n, c,
+                                hw, cp, hi, lo));
   LSC_CUDA_TRY(cudaGetLastError());
   return LSC_SUCCESS;
 }
