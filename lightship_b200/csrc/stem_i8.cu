@@ -23,7 +23,7 @@
 // row before its first pooled row).  Warp roles:
 //   builders (the 7 warps below 15 with warp % 4 in {2, 3}): one TMA tensor load per conv
 //               row brings its two new f32 input rows of the three channels (rows outside the
-//               image arrive as zeros), three conv rows ahead; the rows are quantized into a
+//               image arrive as zeros), four conv rows ahead; the rows are quantized into a
 //               ring of int8 rows held as four copies shifted by 1, 3, 5 and 7 bytes, so that
 //               the eight taps (kw = 0..7) of every (channel, kh) pair of an output pixel are
 //               one aligned 8-byte load; the conv row's im2col rows (pixel x at row x + 4) go
@@ -65,11 +65,11 @@ constexpr int kStK = 192;               // 21 (c, kh) groups x 8 taps = 168, pad
 constexpr int kStKSteps = kStK / 32;
 constexpr int kStStages = 3;
 constexpr int kStABytes = (kStK / 16) * 128 * 16;   // 12 chunks of [128 rows][16 B] (filter, im2col)
-constexpr int kStF32Slots = 10;    // TMA loads of two f32 input rows x 3 channels
+constexpr int kStF32Slots = 12;    // TMA loads of two f32 input rows x 3 channels
 constexpr int kStF32Load = 2 * kStC * kStW * 4;     // bytes per load: [c][2 rows][224]
 constexpr int kStRingRows = 16;     // quantized input rows, by a running row count
 constexpr int kStCopyPitch = 288;   // one shifted copy of a quantized row (bank-spread)
-constexpr int kStLead = 3;          // conv rows whose input is fetched ahead
+constexpr int kStLead = 4;          // conv rows whose input is fetched ahead
 constexpr int kStBuilders = 224;  // 7 warps: two threads per im2col row of the 112 pixels
 constexpr int kStMmaWarp = 15;
 constexpr int kStEpiWarps = 8;
@@ -200,8 +200,8 @@ __global__ void __launch_bounds__(kStThreads, 1)
     const int t = bwarp * 32 + lane;
     // input loads in sequence order: slot = count mod kStF32Slots.  Thread 0 issues the loads
     // of conv row i + kStLead + 1 after the barrier of iteration i, when every builder has
-    // quantized row i's input; rows i+1 .. i+4 then hold at most 4 + 1 + 1 + 4 loads (first
-    // rows are at least three rows apart), within the ten slots.
+    // quantized row i's input; rows i+1 .. i+5 then hold at most 4 + 1 + 1 + 4 + 1 loads (first
+    // rows are at least three rows apart), within the twelve slots.
     int issued_item = 0, issued_loads = 0;  // thread 0
     auto issue_upto = [&](int upto) {
       for (; issued_item <= upto && issued_item < items; ++issued_item) {
