@@ -13,9 +13,10 @@
 // the requantization (bias, scale, ReLU, rounding, clamp) is a monotone non-decreasing map of
 // the accumulator for a positive channel scale, so the max of the requantized codes over a
 // window is the requantized max of the accumulators, and only the pooled quarter of the
-// outputs is requantized.  The results are the separate launches' bit for bit.  (The launcher
-// checks the conditions that argument needs: positive channel scales, and biases small enough
-// that the accumulator plus the bias cannot wrap around: |acc| < 147 * 128 * 128 < 2^22.)
+// outputs is requantized.  The results are the separate launches' bit for bit.  (The caller --
+// the INT8 session's prepare_stem -- checks the conditions that argument needs: positive channel
+// scales, and biases small enough that the accumulator plus the bias cannot wrap around:
+// |acc| < 147 * 128 * 128 < 2^22.)
 //
 // One CTA per SM walks a contiguous range of pooled rows (the whole batch's n * 56 rows split
 // evenly over the grid).  A pooled row py reads conv rows 2py-1, 2py, 2py+1; consecutive pooled
